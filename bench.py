@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Learner-step throughput: samples/s of the fused fwd + bwd + loss + Adam step.
+
+Workload (default): c3, actor + critic 27-512-512-512-{9,1}, global batch 1,048,576
+rows split evenly over the ranks (strong scaling), one flat-gradient all-reduce per
+step between the backward and the replicated Adam. Inputs are seeded synthetic
+learner batches with the real inputs' shapes and distributions (tic-tac-toe boards,
+Dirichlet(0.3) targets, N(0,1) old logits, 5-step returns).
+
+Timed quantities (one JSON line on rank 0):
+  value       samples/s with the batch already in HBM: K steps between CUDA events on
+              the learner's stream, max over ranks
+  e2e         the same through the public API with pinned HOST buffers: each step
+              copies its batch host->device and reads the loss statistics back
+  roofline    the dominant kernel (the hidden-layer GEMM) timed with CUDA events on the
+              same stream with the step's shapes; algorithmic FLOPs / duration vs the
+              measured peak
+  cpu_baseline the CPU restatement (float32 numpy) on a bounded sample, rank 0, N = 1
+
+--impl reference times the reference's computation on the host CPU (the reference
+is Mojo GPU code with no CPU path and no runnable toolchain here, so its algorithm is
+run as the float32 numpy restatement), with all host threads.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3] [--impl ours|reference]
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from spo_mojo_b200.workloads import WORKLOADS, init_params, make_batch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="budget of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------- CPU arm
+def cpu_learner_step(wl, params, batch, nets_state=None):
+    from oracle import spo_oracle as O
+    hp = dict(lr_actor=wl.lr, lr_critic=wl.lr, b1=wl.beta1, b2=wl.beta2, eps=wl.adam_eps,
+              max_norm=wl.max_grad_norm, kl_eps=wl.kl_eps, dual=wl.dual, step=1)
+    nets = {}
+    for which in ("actor", "critic"):
+        if which in params:
+            p = params[which]
+            nets[which] = {"params": p, "m": [(np.zeros_like(w), np.zeros_like(b)) for w, b in p],
+                           "v": [(np.zeros_like(w), np.zeros_like(b)) for w, b in p]}
+    b = dict(batch)
+    if not wl.dual:
+        b["logits_old"] = None
+    return O.learner_step(b, actor=nets.get("actor"), critic=nets.get("critic"),
+                          log_alpha=wl.log_alpha if wl.dual else None, hp=hp, dtype=np.float32)
+
+
+def cpu_measure(wl, seconds, steps=None, warmup=0):
+    """samples/s of the float32 CPU restatement on a bounded sample of the workload."""
+    sample_rows = min(wl.batch, 8192)
+    params = init_params(wl, seed=0)
+    batch = make_batch(wl, sample_rows, seed=7)
+    for _ in range(warmup):
+        cpu_learner_step(wl, params, batch)
+    times = []
+    t_end = time.perf_counter() + seconds
+    n = 0
+    while (steps is None and (n == 0 or time.perf_counter() < t_end)) or (steps is not None and n < steps):
+        t0 = time.perf_counter()
+        cpu_learner_step(wl, params, batch)
+        times.append(time.perf_counter() - t0)
+        n += 1
+    per_step = statistics.median(times)
+    return sample_rows / per_step, sample_rows, len(times), per_step
+
+
+def run_reference(args):
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    cores = os.cpu_count()
+    try:
+        import threadpoolctl
+        threadpoolctl.threadpool_limits(cores)
+    except Exception:
+        pass
+    sps, rows, n, per_step = cpu_measure(wl, seconds=1e9, steps=args.steps, warmup=args.warmup)
+    line = {
+        "impl": "reference", "metric": "learner samples/sec (fwd+bwd+loss+Adam)", "value": sps,
+        "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_step * 1e3 * wl.batch / rows, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.describe(), "global_batch": wl.batch,
+                   "sample_rows_per_step": rows},
+        "cpu_baseline": {"value": sps, "unit": "samples/s", "cores": cores, "kind": "port",
+                         "sample": f"{rows} rows of the workload per step, {n} steps; the reference "
+                                   "is Mojo GPU-only, its algorithm runs as the float32 numpy restatement"},
+        "e2e": {"value": sps, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- GPU arm
+def count_launches(wl, clip):
+    n = 0
+    for net in (wl.actor, wl.critic):
+        if net is None:
+            continue
+        L = net.num_layers
+        n += (L - 1) + 1 + (L - 1) + (L - 2)    # forward GEMMs, head, dW GEMMs, dX GEMMs
+    return n + 1 + 1 + (1 if clip else 0)      # reduce, adam, sum of squares
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from spo_mojo_b200 import ffi
+    from spo_mojo_b200.learner import Comm, Learner
+
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    wl = WORKLOADS[args.workload]
+    B = wl.batch
+    assert B % world == 0, "global batch must split evenly"
+    rows = B // world
+    params = init_params(wl, seed=0)
+    batch_np = make_batch(wl, rows, seed=100 + rank)
+    host = {k: torch.from_numpy(v).pin_memory() for k, v in batch_np.items()}
+    batch = {k: v.to(dev) for k, v in host.items()}
+    L = Learner.for_workload(wl, max_rows=rows, device=local)
+    L.load(actor=params.get("actor"), critic=params.get("critic"), log_alpha=wl.log_alpha)
+    comm = None
+    if world > 1:
+        obj = [Comm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = Comm(obj[0], world, rank)
+    stream = torch.cuda.Stream(dev)
+    scale = 1.0 / B
+
+    def step(b):
+        L.backward(b, grad_scale=scale, stream=stream)
+        if comm is not None:
+            comm.allreduce_(L.grads, stream=stream)
+        L.apply(stream=stream)
+
+    torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step(batch)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+
+    gpu_index = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            gpu_index = int(vis.split(",")[local])
+        except ValueError:
+            gpu_index = vis.split(",")[local]
+    clocks = ClockSampler(gpu_index)
+    clocks.start()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(batch)
+    t1.record(stream)
+    t1.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    clk = clocks.stop()
+    ms_max = ms
+    if world > 1:
+        tm = torch.tensor([ms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms_max = float(tm.item())
+    value = B / (ms_max / 1e3)
+    stats = L.stats()
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        stats_host = torch.empty(ffi.NUM_STATS, dtype=torch.float32).pin_memory()
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = stats_host.numel() * 4
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                for k, v in host.items():
+                    batch[k].copy_(v, non_blocking=True)
+                step(batch)
+                stats_host.copy_(L.stats_tensor(), non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        wall = (time.perf_counter() - w0) * 1e3 / args.steps
+        ems = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            tm = torch.tensor([ems], device=dev)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            ems = float(tm.item())
+        e2e = {"value": B / (ems / 1e3), "unit": "samples/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": ems, "wall_ms_per_step": wall,
+               "loss_read": float(stats_host[0])}
+
+    # ---- roofline of the dominant kernel: the hidden x hidden GEMM (forward shape)
+    roof = None
+    net = wl.actor or wl.critic
+    H = net.dims[1]
+    if rank == 0:
+        pk, kind = peaks()
+        x = torch.rand(rows, H, device=dev)
+        w = torch.rand(H, H, device=dev)
+        bb = torch.zeros(H, device=dev)
+        y = torch.empty(rows, H, device=dev)
+        reps = 20
+        for _ in range(3):
+            ffi.call("spo_linear_fwd", stream.cuda_stream, y.data_ptr(), x.data_ptr(), w.data_ptr(),
+                     bb.data_ptr(), rows, H, H, 1)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record(stream)
+        for _ in range(reps):
+            ffi.call("spo_linear_fwd", stream.cuda_stream, y.data_ptr(), x.data_ptr(), w.data_ptr(),
+                     bb.data_ptr(), rows, H, H, 1)
+        k1.record(stream)
+        k1.synchronize()
+        kms = k0.elapsed_time(k1) / reps
+        flops = 2.0 * rows * H * H
+        achieved = flops / (kms / 1e3) / 1e12
+        peak = pk.get("bf16_tflops_sustained") or pk.get("bf16_tflops")
+        roof = {"bound": "tensor", "kernel": "hidden GEMM %dx%dx%d (forward shape)" % (rows, H, H),
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_kind": f"{kind} bf16 dense, sustained", "ms_per_launch": kms,
+                "traffic": None,
+                "fp32_simt_nominal_tflops": 148 * 128 * 2 * 1.965e9 / 1e12}
+        del x, w, y
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sps, srows, n, per = cpu_measure(wl, seconds=args.cpu_seconds)
+        cpu = {"value": sps, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{srows} rows of {wl.name} per step, median of {n} steps "
+                         "(float32 numpy restatement, all threads)"}
+
+    if comm is not None:
+        comm.close()
+    if rank == 0:
+        clip = wl.max_grad_norm > 0 and math.isfinite(wl.max_grad_norm)
+        line = {
+            "metric": "learner samples/sec (fwd+bwd+loss+Adam)",
+            "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl.describe(), "global_batch": B, "rows_per_rank": rows,
+                       "parallelism": f"dp{world}",
+                       "l2": "working set per step > L2 (inputs %.0f MB, activations %.1f GB); no flush"
+                             % (sum(v.nbytes for v in batch_np.values()) / 1e6,
+                                rows * sum(sum(n.dims[1:-1]) for n in (wl.actor, wl.critic) if n) * 4 / 1e9)},
+            "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+            "gpu_launches": count_launches(wl, clip) * args.steps + (0 if world == 1 else 0),
+            "stats": stats,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

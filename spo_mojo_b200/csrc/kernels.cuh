@@ -1,0 +1,135 @@
+// Internal kernel interfaces of libspo_cuda (not part of the C ABI).
+#pragma once
+
+#include "spo_common.cuh"
+
+namespace spo {
+
+// ---------------------------------------------------------------- loss statistics
+// Slots of the statistics vector (scaled sums: means when scale = 1/batch).
+enum StatSlot : int {
+  kStatActorLoss = 0,   // CE + alpha * KL(pi_old || pi)
+  kStatCE = 1,          // -sum q log pi              (networks/actor_loss.mojo:40-65)
+  kStatEntropy = 2,     // H(q)                        (networks/actor_loss.mojo:105-116)
+  kStatKLq = 3,         // KL(q || pi) = CE - H(q)     (networks/actor_loss.mojo:119-124)
+  kStatKLold = 4,       // KL(pi_old || pi)
+  kStatCriticLoss = 5,  // 0.5 (V - t)^2               (demos/train_critic.mojo:317-327)
+  kStats = 8,
+};
+
+// ---------------------------------------------------------------- fused head
+enum HeadMode : int { kHeadActor = 0, kHeadCritic = 1 };
+
+struct HeadParams {
+  const float* act;        // [M x H] post-ReLU input of the last Linear layer
+  const float* W;          // [H x A]
+  const float* b;          // [A]
+  int64_t M;
+  int H, A;
+  int mode;                // kHeadActor / kHeadCritic
+  int rows_per_tile;       // set by head_launch
+  const float* mask;       // actor: [M x A] 1 legal / 0 illegal (null: all legal)
+  const float* q;          // actor: [M x A] target policy
+  const float* z_old;      // actor: [M x A] pi_old logits, or null (no KL term)
+  const float* log_alpha;  // actor: device scalar, or null (use alpha_host)
+  float alpha_host;
+  const float* target;     // critic: [M x A]
+  float scale;             // gradient scale (1 / global batch)
+  float* out_logits;       // optional [M x A]: masked logits (actor) or V (critic)
+  float* out_pi;           // optional [M x A]: pi (actor)
+  float* dz_out;           // optional [M x A]: dL/dz
+  float* dX;               // optional [M x H]: (dz W^T) * [act > 0]
+  float* dW_part;          // [grid][H x A]
+  float* db_part;          // [grid][A]
+  float* dbx_part;         // optional [grid][H]: column sums of dX
+  float* stats_part;       // optional [grid][kStats]
+};
+
+int head_rows_per_tile(int H);
+size_t head_smem_bytes(int H, int A);
+int head_grid(int64_t M, int H);
+int head_launch(HeadParams p, int grid, cudaStream_t s);
+
+// ---------------------------------------------------------------- partial-sum reduction
+constexpr int kMaxSegs = 80;
+
+struct ReduceSeg {
+  const float* src;        // parts x part_stride floats
+  float* dst;              // count floats
+  int64_t count;
+  int64_t part_stride;
+  int32_t parts;
+};
+
+struct ReduceParams {
+  ReduceSeg seg[kMaxSegs];
+  int nseg;
+};
+
+int reduce_launch(const ReduceParams& p, cudaStream_t s);
+
+// ---------------------------------------------------------------- optimiser
+constexpr int kMaxGroups = 4;
+constexpr int kSumsqParts = 128;  // CTAs of the sum-of-squares pass
+
+struct AdamGroup {
+  int64_t begin, end;      // [begin, end) in the flat buffers, multiples of 4
+  float lr;
+  float max_norm;          // clip when finite and > 0
+};
+
+struct AdamParams {
+  float* p;
+  float* g;
+  float* m;
+  float* v;
+  AdamGroup grp[kMaxGroups];
+  int ngrp;
+  float b1, b2, eps;
+  float grad_scale;        // multiplies every gradient (1 in the learner)
+  const float* sumsq_part; // [ngrp][kSumsqParts] or null (no clipping)
+  int* step;               // device step counter (t = *step + 1) or null
+  unsigned* ticket;        // completion counter for the step update (with step)
+  int host_step;           // used when step == null
+  int64_t alpha_index;     // flat index of log_alpha, or -1
+  const float* kl_stat;    // device: mean KL(pi_old || pi) of the batch (global)
+  float kl_eps;
+  float* report;           // optional device [kReportSize]
+};
+
+enum ReportSlot : int {
+  kRepNorm0 = 0,           // per-group global norms (kMaxGroups)
+  kRepClip0 = 4,           // per-group clip scales (kMaxGroups)
+  kRepDlogAlpha = 8,
+  kRepStep = 9,
+  kReportSize = 16,
+};
+
+int sumsq_groups_launch(const float* g, const AdamGroup* grp, int ngrp, float* part,
+                        cudaStream_t s);
+int adam_launch(const AdamParams& p, int64_t n, cudaStream_t s);
+int sumsq_launch(const float* x, int64_t n, float* part, float* out, cudaStream_t s);
+int ema_launch(float* target, const float* online, int64_t n, float tau, cudaStream_t s);
+
+// ---------------------------------------------------------------- row-wise kernels
+int mask_logits_launch(float* logits, const float* mask, int64_t n, cudaStream_t s);
+int softmax_rows_launch(float* out, const float* in, int64_t rows, int cols, int mode,
+                        cudaStream_t s);  // mode 0 softmax, 1 log_softmax, 2 logsumexp
+int ce_rows_launch(float* out, const float* q, const float* log_pi, int64_t rows, int cols,
+                   cudaStream_t s);
+int entropy_rows_launch(float* out, const float* q, int64_t rows, int cols, cudaStream_t s);
+int kl_rows_launch(float* out, const float* ce, const float* h, int64_t rows, cudaStream_t s);
+int logits_grad_launch(float* dz, const float* pi, const float* q, const float* mask,
+                       int64_t n, float scale, cudaStream_t s);
+int value_grad_launch(float* dv, const float* v, const float* t, int64_t n, float scale,
+                      cudaStream_t s);
+int relu_launch(float* a, int64_t n, cudaStream_t s);
+int relu_bwd_launch(float* g, const float* act, int64_t n, cudaStream_t s);
+// part[c][n] = sum of rows [c*per, (c+1)*per) of x [rows x n], per = ceil(rows / chunks).
+int colsum_part_launch(const float* x, int64_t rows, int64_t n, int64_t chunks, float* part,
+                       cudaStream_t s);
+int gae_launch(float* adv, float* targets, const float* r, const float* discount,
+               const float* v_tm1, const float* v_t, const float* trunc, int64_t batch,
+               int t_len, float lambda, cudaStream_t s);
+
+}  // namespace spo

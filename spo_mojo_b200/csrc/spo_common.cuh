@@ -1,0 +1,75 @@
+// Shared definitions for the libspo_cuda kernels: error reporting, launch checks,
+// the masking constant, and small device helpers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <float.h>
+#include <string>
+
+namespace spo {
+
+// ops/common.mojo:19-23 — the most negative FINITE float32 masks illegal logits.
+constexpr float kNegInf = -FLT_MAX;
+
+constexpr int kMaxLayers = 8;
+
+// Status codes returned by every C-ABI entry point (mirrored in include/spo_cuda.h).
+enum Status : int {
+  kOk = 0,
+  kErrArg = -1,
+  kErrShape = -2,
+  kErrAlign = -3,
+  kErrWorkspace = -4,
+  kErrCuda = -5,
+  kErrNccl = -6,
+  kErrUnsupported = -7,
+  kErrTimeout = -8,
+};
+
+// Records the message for spo_last_error_string() (thread-local) and returns code.
+int set_error(int code, const std::string& msg);
+void clear_error();
+
+#define SPO_CHECK_ARG(cond, code, msg)                                    \
+  do {                                                                    \
+    if (!(cond)) return ::spo::set_error((code), std::string(__func__) + ": " + (msg)); \
+  } while (0)
+
+#define SPO_CUDA_TRY(expr)                                                \
+  do {                                                                    \
+    cudaError_t _e = (expr);                                              \
+    if (_e != cudaSuccess)                                                \
+      return ::spo::set_error(::spo::kErrCuda, std::string(__func__) + ": " #expr ": " + \
+                              cudaGetErrorString(_e));                    \
+  } while (0)
+
+// After a launch: report configuration errors (not asynchronous faults).
+#define SPO_LAUNCH_CHECK()                                                \
+  do {                                                                    \
+    cudaError_t _e = cudaGetLastError();                                  \
+    if (_e != cudaSuccess)                                                \
+      return ::spo::set_error(::spo::kErrCuda, std::string(__func__) + ": launch: " + \
+                              cudaGetErrorString(_e));                    \
+  } while (0)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace spo

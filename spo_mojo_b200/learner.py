@@ -1,0 +1,195 @@
+"""The fused learner step: one M-step update of the actor and/or critic.
+
+Wraps spo_learner_* of libspo_cuda (the composition of demos/train_spo.mojo:417-554
+update(): critic block and actor block, each with its own global-norm clip and Adam,
+plus the log_alpha dual). All state lives in flat device buffers with one layout
+[actor | critic | log_alpha | statistics]; the caller owns them through this object.
+
+Data parallel: every rank runs ``backward`` on its shard with grad_scale =
+1 / global_batch, then the flat gradient buffer (gradients + loss statistics) is
+summed across ranks with ONE all-reduce, then every rank runs the same ``apply``.
+"""
+
+import ctypes
+import math
+
+import torch
+
+from . import ffi
+from .workloads import NetSpec
+
+
+class Learner:
+    def __init__(self, actor_dims=None, critic_dims=None, max_rows=1, lr_actor=3e-4,
+                 lr_critic=3e-4, beta1=0.9, beta2=0.999, adam_eps=1e-8,
+                 max_grad_norm=math.inf, kl_eps=0.01, use_kl=True, dual=True, device=0):
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        d = ffi.LearnerDesc()
+        d.actor = ffi.MlpDesc.of(actor_dims)
+        d.critic = ffi.MlpDesc.of(critic_dims)
+        d.max_rows = int(max_rows)
+        d.lr_actor, d.lr_critic = lr_actor, lr_critic
+        d.beta1, d.beta2, d.adam_eps = beta1, beta2, adam_eps
+        d.max_grad_norm = max_grad_norm
+        d.kl_eps = kl_eps
+        d.use_kl = 1 if (use_kl and actor_dims is not None) else 0
+        d.dual = 1 if (dual and d.use_kl) else 0
+        self.desc = d
+        self.actor_dims = tuple(actor_dims) if actor_dims is not None else None
+        self.critic_dims = tuple(critic_dims) if critic_dims is not None else None
+        self.layout = ffi.LearnerLayout()
+        ffi.call("spo_learner_layout_of", ctypes.byref(d), ctypes.byref(self.layout))
+        nbytes = ffi.lib().spo_learner_workspace_size(ctypes.byref(d))
+        if nbytes == 0:
+            raise ffi.SpoError(-1, ffi.last_error())
+        total = self.layout.total
+        dev = self.device
+        self.workspace = torch.empty(int(nbytes), dtype=torch.uint8, device=dev)
+        self.params = torch.zeros(total, dtype=torch.float32, device=dev)
+        self.grads = torch.zeros(total, dtype=torch.float32, device=dev)
+        self.adam_m = torch.zeros(total, dtype=torch.float32, device=dev)
+        self.adam_v = torch.zeros(total, dtype=torch.float32, device=dev)
+        self.step_counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.report = torch.zeros(ffi.REPORT_SIZE, dtype=torch.float32, device=dev)
+        handle = ctypes.c_void_p()
+        torch.cuda.synchronize(dev)
+        ffi.call("spo_learner_create", ctypes.byref(d), self.workspace.data_ptr(),
+                 self.workspace.numel(), ctypes.byref(handle))
+        self._h = handle
+        self._state = ffi.TrainState(self.params.data_ptr(), self.grads.data_ptr(),
+                                     self.adam_m.data_ptr(), self.adam_v.data_ptr(),
+                                     self.step_counter.data_ptr(), self.report.data_ptr())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            ffi.lib().spo_learner_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ------------------------------------------------------------ buffers
+    def net_slice(self, which, buf=None):
+        buf = self.params if buf is None else buf
+        lay = self.layout
+        if which == "actor":
+            return buf[lay.actor_offset:lay.actor_offset + lay.actor_size]
+        return buf[lay.critic_offset:lay.critic_offset + lay.critic_size]
+
+    def tensors(self, which, buf=None):
+        """[(W, b)] views of one network in a flat buffer (params by default)."""
+        dims = self.actor_dims if which == "actor" else self.critic_dims
+        spec = NetSpec(dims)
+        flat = self.net_slice(which, buf)
+        offs, _ = spec.offsets()
+        out = []
+        for i, (wo, bo) in enumerate(offs):
+            k, n = dims[i], dims[i + 1]
+            out.append((flat[wo:wo + k * n].view(k, n), flat[bo:bo + n]))
+        return out
+
+    def load(self, actor=None, critic=None, log_alpha=0.0):
+        """Set parameters from lists of (W, b) arrays; reset Adam state and step."""
+        self.params.zero_()
+        for which, params in (("actor", actor), ("critic", critic)):
+            if params is None:
+                continue
+            for (w, b), (tw, tb) in zip(params, self.tensors(which)):
+                tw.copy_(torch.as_tensor(w, dtype=torch.float32))
+                tb.copy_(torch.as_tensor(b, dtype=torch.float32))
+        self.params[self.layout.alpha_index] = float(log_alpha)
+        self.adam_m.zero_()
+        self.adam_v.zero_()
+        self.step_counter.zero_()
+
+    @property
+    def log_alpha(self):
+        return self.params[self.layout.alpha_index]
+
+    def stats_tensor(self):
+        off = self.layout.stats_offset
+        return self.grads[off:off + ffi.NUM_STATS]
+
+    def stats(self):
+        s = self.stats_tensor().tolist()
+        return {k: s[v] for k, v in ffi.STAT.items()}
+
+    def report_dict(self):
+        r = self.report.tolist()
+        return {k: r[v] for k, v in ffi.REPORT.items()}
+
+    # ------------------------------------------------------------ the step
+    def _batch(self, batch, rows=None):
+        rows = int(batch["obs"].shape[0]) if rows is None else int(rows)
+        g = batch.get
+        return ffi.Batch(g("obs").data_ptr(),
+                         g("mask").data_ptr() if g("mask") is not None else None,
+                         g("q").data_ptr() if g("q") is not None else None,
+                         g("logits_old").data_ptr() if g("logits_old") is not None else None,
+                         g("target").data_ptr() if g("target") is not None else None,
+                         rows)
+
+    def backward(self, batch, grad_scale=None, stream=None):
+        b = self._batch(batch)
+        scale = (1.0 / b.rows if b.rows else 0.0) if grad_scale is None else grad_scale
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        ffi.call("spo_learner_backward", self._h, s, ctypes.byref(b), scale, ctypes.byref(self._state))
+
+    def apply(self, stream=None):
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        ffi.call("spo_learner_apply", self._h, s, ctypes.byref(self._state))
+
+    def step(self, batch, stream=None):
+        b = self._batch(batch)
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        ffi.call("spo_learner_step", self._h, s, ctypes.byref(b), ctypes.byref(self._state))
+
+    def forward(self, which, obs, mask=None, stream=None):
+        """Inference forward of one network: (logits or V, pi or None)."""
+        dims = self.actor_dims if which == "actor" else self.critic_dims
+        rows = obs.shape[0]
+        out = torch.empty(rows, dims[-1], dtype=torch.float32, device=self.device)
+        pi = torch.empty_like(out) if which == "actor" else None
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        ffi.call("spo_learner_forward", self._h, s, 0 if which == "actor" else 1,
+                 self.params.data_ptr(), obs.data_ptr(),
+                 mask.data_ptr() if mask is not None else None, rows, out.data_ptr(),
+                 pi.data_ptr() if pi is not None else None)
+        return out, pi
+
+    @classmethod
+    def for_workload(cls, wl, max_rows=None, device=0, **kw):
+        return cls(actor_dims=wl.actor.dims if wl.actor else None,
+                   critic_dims=wl.critic.dims if wl.critic else None,
+                   max_rows=max_rows or wl.batch, lr_actor=wl.lr, lr_critic=wl.lr,
+                   beta1=wl.beta1, beta2=wl.beta2, adam_eps=wl.adam_eps,
+                   max_grad_norm=wl.max_grad_norm, kl_eps=wl.kl_eps, use_kl=wl.dual,
+                   dual=wl.dual, device=device, **kw)
+
+
+class Comm:
+    """NCCL communicator of libspo_cuda (one per rank); ids shared by the caller."""
+
+    def __init__(self, unique_id, nranks, rank):
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(unique_id), ffi.COMM_ID_BYTES)
+        ffi.call("spo_comm_init", ctypes.byref(h), buf, nranks, rank)
+        self._h = h
+
+    @staticmethod
+    def unique_id():
+        buf = ctypes.create_string_buffer(ffi.COMM_ID_BYTES)
+        ffi.call("spo_comm_get_unique_id", buf)
+        return bytes(buf.raw)
+
+    def allreduce_(self, tensor, stream=None):
+        s = (stream or torch.cuda.current_stream(tensor.device)).cuda_stream
+        ffi.call("spo_allreduce_sum", self._h, s, tensor.data_ptr(), tensor.numel())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            ffi.lib().spo_comm_destroy(self._h)
+            self._h = None

@@ -1,0 +1,264 @@
+"""The fused learner step (libspo_cuda through spo_learner_*) against the float64
+CPU oracle, on seeded synthetic inputs of the five learner workloads.
+
+Tolerances (the parity bar of this path): losses rel 1e-5; gradients rel 1e-4 of
+max |want| per tensor (the reference's gradient metric,
+tests/test_actor_backward.mojo:59-71); post-Adam parameters rel 1e-4 / abs 1e-6.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import spo_oracle as O
+from spo_mojo_b200.workloads import WORKLOADS, make_batch, init_params, Workload, NetSpec
+
+pytestmark = pytest.mark.gpu
+
+LOSS_RTOL = 1e-5
+GRAD_RTOL = 1e-4
+PARAM_RTOL, PARAM_ATOL = 1e-4, 1e-6
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def to_dev(batch):
+    return {k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in batch.items()}
+
+
+def oracle_run(wl, params, batch, steps=1, max_norm=None):
+    hp = dict(lr_actor=wl.lr, lr_critic=wl.lr, b1=wl.beta1, b2=wl.beta2, eps=wl.adam_eps,
+              max_norm=wl.max_grad_norm if max_norm is None else max_norm,
+              kl_eps=wl.kl_eps, dual=wl.dual)
+    nets = {}
+    for which in ("actor", "critic"):
+        if which in params:
+            p = [(w.astype(np.float64), b.astype(np.float64)) for w, b in params[which]]
+            nets[which] = {"params": p, "m": [(np.zeros_like(w), np.zeros_like(b)) for w, b in p],
+                           "v": [(np.zeros_like(w), np.zeros_like(b)) for w, b in p]}
+    la, am, av = wl.log_alpha, 0.0, 0.0
+    first = None
+    for step in range(1, steps + 1):
+        hp.update(step=step, alpha_m=am, alpha_v=av)
+        b = dict(batch)
+        if not wl.dual:
+            b["logits_old"] = None
+        out = O.learner_step(b, actor=nets.get("actor"), critic=nets.get("critic"),
+                             log_alpha=la if wl.dual else None, hp=hp)
+        if first is None:
+            first = out
+        for which in nets:
+            nets[which]["params"] = out[which]["new_params"]
+            nets[which]["m"] = out[which]["new_m"]
+            nets[which]["v"] = out[which]["new_v"]
+        if "log_alpha" in out:
+            la, am, av = out["log_alpha"]["value"], out["log_alpha"]["m"], out["log_alpha"]["v"]
+    return first, nets, la
+
+
+def run_learner(wl, params, batch_dev, steps=1, max_norm=None, rows=None):
+    from spo_mojo_b200.learner import Learner
+    kw = {} if max_norm is None else {"max_grad_norm": max_norm}
+    L = Learner.for_workload(wl, max_rows=rows or batch_dev["obs"].shape[0], **kw)
+    L.load(actor=params.get("actor"), critic=params.get("critic"), log_alpha=wl.log_alpha)
+    grads0 = stats0 = rep0 = None
+    for i in range(steps):
+        L.step(batch_dev)
+        if i == 0:
+            grads0 = L.grads.clone()
+            stats0 = L.stats()
+            rep0 = L.report_dict()
+    torch.cuda.synchronize()
+    return L, grads0, stats0, rep0
+
+
+def rel_of_max(got, want):
+    want = np.asarray(want, np.float64)
+    return float(np.max(np.abs(np.asarray(got, np.float64) - want))) / max(float(np.max(np.abs(want))), 1e-30)
+
+
+def check_against_oracle(wl, L, grads0, stats0, rep0, ora, nets, la):
+    # losses
+    if wl.actor is not None:
+        al = ora["actor"]["loss"]
+        assert abs(stats0["actor_loss"] - al["loss"]) <= LOSS_RTOL * abs(al["loss"])
+        assert abs(stats0["ce"] - al["ce_mean"]) <= LOSS_RTOL * abs(al["ce_mean"])
+        assert abs(stats0["entropy"] - al["entropy_mean"]) <= LOSS_RTOL * abs(al["entropy_mean"]) + 1e-7
+        assert abs(stats0["kl_q"] - al["kl_q_mean"]) <= LOSS_RTOL * abs(al["ce_mean"])
+        assert abs(stats0["kl_old"] - al["kl_old_mean"]) <= LOSS_RTOL * abs(al["loss"])
+    if wl.critic is not None:
+        cl = ora["critic"]["loss"]
+        assert abs(stats0["critic_loss"] - cl) <= LOSS_RTOL * abs(cl)
+    # gradients, per tensor
+    for which in ("actor", "critic"):
+        if which not in ora:
+            continue
+        for i, ((gw, gb), (ow, ob)) in enumerate(zip(L.tensors(which, grads0), ora[which]["grads"])):
+            assert rel_of_max(gw.cpu().numpy(), ow) <= GRAD_RTOL, f"{which} dW{i + 1}"
+            assert rel_of_max(gb.cpu().numpy(), ob) <= GRAD_RTOL, f"{which} db{i + 1}"
+        # parameters after Adam
+        for i, ((pw, pb), (ow, ob)) in enumerate(zip(L.tensors(which), nets[which]["params"])):
+            np.testing.assert_allclose(pw.cpu().numpy(), ow, rtol=PARAM_RTOL, atol=PARAM_ATOL,
+                                       err_msg=f"{which} W{i + 1} after Adam")
+            np.testing.assert_allclose(pb.cpu().numpy(), ob, rtol=PARAM_RTOL, atol=PARAM_ATOL,
+                                       err_msg=f"{which} b{i + 1} after Adam")
+    if wl.actor is not None and wl.dual:
+        want = ora["log_alpha"]["grad"]
+        assert abs(rep0["dlog_alpha"] - want) <= 1e-4 * abs(want) + 1e-7
+        assert abs(float(L.log_alpha) - la) <= PARAM_RTOL * abs(la) + PARAM_ATOL
+
+
+@pytest.mark.parametrize("name,rows", [("c0", 256), ("c1", 4096), ("c2", 4096), ("c3", 2048), ("c4", 1024)])
+def test_workload_step_matches_oracle(name, rows):
+    wl = WORKLOADS[name]
+    params = init_params(wl, seed=0)
+    batch = make_batch(wl, rows, seed=1)
+    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch))
+    ora, nets, la = oracle_run(wl, params, batch)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+
+
+def test_c2_full_batch_matches_oracle():
+    """c2 at its full 65,536 rows (the oracle still finishes in seconds)."""
+    wl = WORKLOADS["c2"]
+    params = init_params(wl, seed=0)
+    batch = make_batch(wl, wl.batch, seed=2)
+    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch))
+    ora, nets, la = oracle_run(wl, params, batch)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+
+
+def test_three_steps_bias_correction():
+    wl = WORKLOADS["c0"]
+    params = init_params(wl, seed=3)
+    batch = make_batch(wl, 256, seed=4)
+    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch), steps=3)
+    ora, nets, la = oracle_run(wl, params, batch, steps=3)
+    assert int(L.step_counter.item()) == 3
+    for (pw, pb), (ow, ob) in zip(L.tensors("actor"), nets["actor"]["params"]):
+        np.testing.assert_allclose(pw.cpu().numpy(), ow, rtol=PARAM_RTOL, atol=PARAM_ATOL)
+        np.testing.assert_allclose(pb.cpu().numpy(), ob, rtol=PARAM_RTOL, atol=PARAM_ATOL)
+    assert abs(float(L.log_alpha) - la) <= PARAM_RTOL * abs(la) + PARAM_ATOL
+
+
+def test_global_norm_clip_bites():
+    """max_grad_norm small enough that the reference's clip (networks/optim.mojo:133-142)
+    scales both networks' updates."""
+    wl = Workload("clip", actor=NetSpec((27, 64, 64, 9)), critic=NetSpec((27, 64, 64, 1)),
+                  batch=512, max_grad_norm=1e-3)
+    params = init_params(wl, seed=5)
+    batch = make_batch(wl, 512, seed=6)
+    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch))
+    ora, nets, la = oracle_run(wl, params, batch)
+    assert r0["clip_actor"] < 1.0 and r0["clip_critic"] < 1.0
+    assert abs(r0["norm_actor"] - ora["actor"]["norm"]) <= 1e-4 * ora["actor"]["norm"]
+    assert abs(r0["norm_critic"] - ora["critic"]["norm"]) <= 1e-4 * ora["critic"]["norm"]
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+
+
+@pytest.mark.parametrize("rows", [1, 3, 129, 1000])
+def test_ragged_row_counts(rows):
+    wl = WORKLOADS["c2"]
+    params = init_params(wl, seed=7)
+    batch = make_batch(wl, rows, seed=8)
+    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch), rows=4096)
+    ora, nets, la = oracle_run(wl, params, batch)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+
+
+def test_degenerate_rows():
+    """A fully masked row (a finished board: uniform pi, zero dz, no NaN —
+    networks/actor.mojo:57-62) and q with zeros on legal cells (the q == 0 skip of
+    networks/actor_loss.mojo:48-56)."""
+    wl = WORKLOADS["c0"]
+    params = init_params(wl, seed=9)
+    batch = make_batch(wl, 64, seed=10)
+    batch["mask"][0] = 0.0
+    batch["q"][0] = 0.0
+    batch["logits_old"][0] = O.NEG_INF
+    legal = np.flatnonzero(batch["mask"][1])
+    batch["q"][1] = 0.0
+    batch["q"][1, legal[0]] = 1.0
+    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch))
+    assert all(math.isfinite(v) for v in s0.values())
+    assert torch.isfinite(g0).all()
+    ora, nets, la = oracle_run(wl, params, batch)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+    logits, pi = L.forward("actor", to_dev(batch)["obs"], to_dev(batch)["mask"])
+    assert torch.allclose(pi[0], torch.full((9,), 1.0 / 9, device="cuda"))
+
+
+def test_zero_rows_leave_zero_gradients():
+    wl = WORKLOADS["c0"]
+    from spo_mojo_b200.learner import Learner
+    L = Learner.for_workload(wl, max_rows=16)
+    L.load(actor=init_params(wl)["actor"])
+    L.grads.fill_(7.0)
+    b = to_dev(make_batch(wl, 1, seed=0))
+    b = {k: v[:0] for k, v in b.items()}
+    L.backward(b, grad_scale=1.0)
+    torch.cuda.synchronize()
+    lay = L.layout
+    assert torch.count_nonzero(L.grads[:lay.stats_offset + 8]) == 0
+
+
+def test_rows_beyond_capacity_raise():
+    from spo_mojo_b200 import ffi
+    from spo_mojo_b200.learner import Learner
+    wl = WORKLOADS["c0"]
+    L = Learner.for_workload(wl, max_rows=8)
+    with pytest.raises(ffi.SpoError) as e:
+        L.backward(to_dev(make_batch(wl, 9, seed=0)))
+    assert "max_rows" in str(e.value)
+
+
+def test_deterministic():
+    wl = WORKLOADS["c2"]
+    params = init_params(wl, seed=0)
+    batch = to_dev(make_batch(wl, 8192, seed=11))
+    _, g1, _, _ = run_learner(wl, params, batch)
+    _, g2, _, _ = run_learner(wl, params, batch)
+    assert torch.equal(g1, g2)
+
+
+def test_c3_full_batch_additivity_and_forward():
+    """c3 at its full 1,048,576 rows. The float64 oracle cannot run this size in
+    seconds, so: (1) the gradient over the batch equals the sum of the gradients over
+    its two halves with the same 1/B scale (the backward is linear in the per-row
+    terms); (2) the forward of 2,000 sampled rows matches the oracle."""
+    from spo_mojo_b200.learner import Learner
+    wl = WORKLOADS["c3"]
+    params = init_params(wl, seed=0)
+    batch = to_dev(make_batch(wl, wl.batch, seed=12))
+    B = wl.batch
+    L = Learner.for_workload(wl, max_rows=B)
+    L.load(actor=params["actor"], critic=params["critic"])
+    L.backward(batch, grad_scale=1.0 / B)
+    full = L.grads.clone()
+    h = B // 2
+    L.backward({k: v[:h] for k, v in batch.items()}, grad_scale=1.0 / B)
+    part = L.grads.clone()
+    L.backward({k: v[h:] for k, v in batch.items()}, grad_scale=1.0 / B)
+    part += L.grads
+    torch.cuda.synchronize()
+    assert torch.isfinite(full).all()
+    for which in ("actor", "critic"):
+        for (fw, fb), (pw, pb) in zip(L.tensors(which, full), L.tensors(which, part)):
+            assert rel_of_max(fw.cpu().numpy(), pw.cpu().numpy()) <= GRAD_RTOL
+            assert rel_of_max(fb.cpu().numpy(), pb.cpu().numpy()) <= GRAD_RTOL
+    idx = np.random.default_rng(0).choice(B, 2000, replace=False)
+    obs = batch["obs"][torch.from_numpy(idx).cuda()].contiguous()
+    mask = batch["mask"][torch.from_numpy(idx).cuda()].contiguous()
+    logits, pi = L.forward("actor", obs, mask)
+    _, z = O.mlp_forward(params["actor"], obs.cpu().numpy())
+    zm = O.masked_logits(z, mask.cpu().numpy())
+    np.testing.assert_allclose(pi.cpu().numpy(), O.softmax_rows(zm), atol=2e-5)
+    v, _ = L.forward("critic", obs)
+    _, vo = O.mlp_forward(params["critic"], obs.cpu().numpy())
+    np.testing.assert_allclose(v.cpu().numpy(), vo, rtol=1e-4, atol=3e-5 * math.sqrt(512))
