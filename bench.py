@@ -54,6 +54,8 @@ def parse():
                     help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the global batch (profiling of small cases only; not a bench line)")
     return ap.parse_args()
 
 
@@ -207,6 +209,9 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     wl = WORKLOADS[args.workload]
+    if args.rows:
+        import dataclasses
+        wl = dataclasses.replace(wl, batch=args.rows, name=wl.name + f"@{args.rows}rows")
     B = wl.batch
     assert B % world == 0, "global batch must split evenly"
     rows = B // world

@@ -210,6 +210,46 @@ SPO_API int spo_truncated_gae(spo_stream_t stream, float* adv, float* targets, c
                       const float* discount, const float* v_tm1, const float* v_t,
                       const float* truncation, int64_t batch, int32_t t_len, float lambda);
 
+/* ------------------------------------------------------------------ tensor-core GEMM
+ * The hidden-layer products of linear_forward / linear_backward
+ * (networks/linear.mojo:37-167) on sm_100a tensor cores (tcgen05, TF32 inputs, fp32
+ * accumulation) at fp32 accuracy through the 3xTF32 split: every operand is a pair
+ * (hi, lo) with hi = x with its 13 low mantissa bits cleared and lo = x - hi, and
+ * C = lo_A hi_B + hi_A lo_B + hi_A hi_B.
+ *   SPO_TC_FWD     C = relu(A B^T + bias) -> (c_hi, c_lo) split, A [m x k], B [n x k]
+ *   SPO_TC_DX      C = (A B^T) * (mask > 0) -> (c_hi, c_lo), column sums -> colsum
+ *   SPO_TC_DX_F32  as SPO_TC_DX, C written as plain fp32 to c_hi
+ *   SPO_TC_DW      C = A^T B from A [k x m], B [k x n], rows of k split in chunks of
+ *                  k_chunk, one fp32 partial per chunk -> c_part [splits][m x n]
+ * Shapes: n % 128 == 0; FWD/DX: k % 32 == 0, n <= 1024 for DX; DW: m % 128 == 0.
+ * colsum receives [grid][n] partials (grid from spo_tc_gemm_shape). All pointers
+ * 16-byte aligned. err (optional) receives a nonzero code if a bounded wait of the
+ * kernel gave up (the kernel then returns without hanging). */
+#define SPO_TC_FWD 0
+#define SPO_TC_DX 1
+#define SPO_TC_DX_F32 2
+#define SPO_TC_DW 3
+typedef struct spo_tc_gemm_desc {
+  int32_t kind;
+  const float* a_hi;
+  const float* a_lo;
+  const float* b_hi;
+  const float* b_lo;
+  int64_t m, n, k, k_chunk;
+  const float* bias;
+  const float* mask;
+  float* c_hi;
+  float* c_lo;
+  float* c_part;
+  float* colsum;
+  int32_t* err;
+} spo_tc_gemm_desc;
+SPO_API int spo_tc_gemm_shape(const spo_tc_gemm_desc* desc, int32_t* grid, int32_t* splits);
+SPO_API int spo_tc_gemm(spo_stream_t stream, const spo_tc_gemm_desc* desc);
+/* hi/lo split of n floats; keep_positive: positive x never get hi == 0 (ReLU outputs). */
+SPO_API int spo_split_tf32(spo_stream_t stream, float* hi, float* lo, const float* x, int64_t n,
+                           int32_t keep_positive);
+
 /* ------------------------------------------------------------------ learner step
  * One M-step update of the actor and/or critic, demos/train_spo.mojo:417-554 and
  * demos/train_critic.mojo:280-363 (minus target construction): forward, loss,

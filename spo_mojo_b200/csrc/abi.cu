@@ -466,7 +466,7 @@ int learner_backward(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float 
     const int i = Lr->net[0].present ? 0 : 1;
     add_seg(red, stats_src[i], stats, kStats, kStats, stats_parts[i]);
   }
-  add_seg(red, nullptr, st->grads + lay.alpha_index, 4, 0, 0);  // dual gradient set by Adam
+  add_seg(red, nullptr, st->grads + lay.alpha_index, kAlignFloats, 0, 0);  // dual gradient: set by Adam
   if (red.nseg > kMaxSegs) return set_error(kErrUnsupported, "too many reduction segments");
   return reduce_launch(red, s);
 }

@@ -200,6 +200,12 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const AdamParams P, int6
 }
 
 // ---------------------------------------------------------------- EMA
+// optax.incremental_update rounds each product before the add (no fused multiply-add),
+// which the reference's goldens record; the explicit _rn intrinsics keep that order.
+__device__ __forceinline__ float ema_one(float t, float o, float tau, float keep) {
+  return __fadd_rn(__fmul_rn(tau, o), __fmul_rn(keep, t));
+}
+
 __global__ void __launch_bounds__(kThreads) ema_kernel(float* target, const float* online,
                                                         int64_t n, float tau) {
   const int64_t n4 = n / 4;
@@ -213,15 +219,15 @@ __global__ void __launch_bounds__(kThreads) ema_kernel(float* target, const floa
     for (int64_t i = gt; i < n4; i += gs) {
       float4 t = t4[i];
       const float4 o = __ldg(o4 + i);
-      t.x = tau * o.x + keep * t.x;
-      t.y = tau * o.y + keep * t.y;
-      t.z = tau * o.z + keep * t.z;
-      t.w = tau * o.w + keep * t.w;
+      t.x = ema_one(t.x, o.x, tau, keep);
+      t.y = ema_one(t.y, o.y, tau, keep);
+      t.z = ema_one(t.z, o.z, tau, keep);
+      t.w = ema_one(t.w, o.w, tau, keep);
       t4[i] = t;
     }
-    for (int64_t i = 4 * n4 + gt; i < n; i += gs) target[i] = tau * online[i] + keep * target[i];
+    for (int64_t i = 4 * n4 + gt; i < n; i += gs) target[i] = ema_one(target[i], online[i], tau, keep);
   } else {
-    for (int64_t i = gt; i < n; i += gs) target[i] = tau * online[i] + keep * target[i];
+    for (int64_t i = gt; i < n; i += gs) target[i] = ema_one(target[i], online[i], tau, keep);
   }
 }
 

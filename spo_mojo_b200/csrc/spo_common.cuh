@@ -56,6 +56,7 @@ void clear_error();
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t align_up_i64(int64_t n, int64_t a) { return (n + a - 1) / a * a; }
 
 // Number of SMs of the current device (cached per device).
 int sm_count();

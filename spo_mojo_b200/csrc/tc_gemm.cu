@@ -1,0 +1,636 @@
+// tcgen05 3xTF32 GEMM (see tc_gemm.cuh) — persistent, warp-specialised, sm_100a.
+//
+// CTA = 6 warps:
+//   warp 0     TMA producer (one thread): hi/lo tiles of A and B into a STAGES-deep ring
+//   warp 1     TMEM allocator + MMA issuer (one thread): 3 tcgen05.mma per 8-wide k-step
+//              (lo.hi, hi.lo, hi.hi) into a double-buffered fp32 TMEM accumulator
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
+//              32*(w%4)..+31 = tile rows), fused bias/ReLU/mask/column sums, hi/lo split,
+//              stores to global memory
+// Tiles are 128 x 128 outputs; k-blocks are 32 fp32 (one 128-byte swizzle row). Operand
+// tiles are written by TMA with 128-byte swizzling; K-major operands are read by the
+// UMMA descriptors with SBO = 1024 B (8-row atoms) and a 32-byte start advance per
+// k-step, MN-major operands (the dW products) are loaded as 32-element-wide boxes with
+// LBO = 4096 B between boxes and SBO = 1024 B between 8-row k-groups.
+//
+// Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA sets an abort
+// flag and the caller's error word, the producer waits (bounded) for its copies in
+// flight, the MMA thread drains its issued MMAs (bounded), TMEM is freed and the kernel
+// returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "kernels.cuh"
+#include "tc_gemm.cuh"
+
+namespace spo {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BK = 32;
+constexpr int STAGES = 3;
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
+constexpr uint32_t B_TILE = BN * BK * 4;                 // 16 KB
+constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 64 KB
+constexpr uint32_t TMEM_COLS = 2 * BN;                   // two accumulators
+constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
+constexpr uint64_t kDrainNs = 500000000ull;              // 0.5 s
+constexpr int kMaxColsumN = 1024;
+
+enum WaitCode : int { kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, kErrWaitTFull = 4 };
+
+struct __align__(64) Ctl {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct KParams {
+  int kind;
+  int a_mn, b_mn;
+  int64_t M, N, K, k_chunk;
+  int m_tiles, n_tiles, splits;
+  int64_t units;
+  const float* bias;
+  const float* mask;
+  float* c_hi;
+  float* c_lo;
+  float* c_part;
+  float* colsum;
+  int* err;
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait. Returns false when this CTA aborted (another role gave up) or after
+// kWaitNs, in which case it raises the abort flag and records `code` in *err.
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                          int code) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = now_ns();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (now_ns() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+// Bounded wait used on the exit path only (ignores the abort flag).
+__device__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = now_ns();
+  while (!mbar_try(bar, parity) && now_ns() - t0 < kDrainNs) {
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// UMMA shared-memory descriptor, SWIZZLE_128B, sm100 version bits.
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void store4(float* p, float a, float b, float c, float d) {
+  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+
+// ---------------------------------------------------------------- the kernel
+__global__ void __launch_bounds__(kThreads, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
+               const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
+               const KParams P) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  Ctl* ctl = reinterpret_cast<Ctl*>(smem + STAGES * STAGE_BYTES);
+  float* colacc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ctl) + sizeof(Ctl));
+  volatile int* abort_flag = &ctl->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t smem0 = smem_u32(smem);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&ctl->full[s]), 1);
+      mbar_init(smem_u32(&ctl->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&ctl->tfull[a]), 1);
+      mbar_init(smem_u32(&ctl->tempty[a]), kEpiThreads);
+    }
+    mbar_init(smem_u32(&ctl->drain), 1);
+    ctl->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&ctl->tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+
+  const int64_t per_split = (int64_t)P.m_tiles * P.n_tiles;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------ TMA producer
+    uint32_t it = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
+      const int64_t split = u / per_split, rem = u % per_split;
+      const int32_t m0 = (int32_t)((rem / P.n_tiles) * BM);
+      const int32_t n0 = (int32_t)((rem % P.n_tiles) * BN);
+      const int64_t kbeg = split * P.k_chunk;
+      const int64_t kend = min(P.K, kbeg + P.k_chunk);
+      const int nkb = (int)((kend - kbeg + BK - 1) / BK);
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+        if (!mbar_wait(smem_u32(&ctl->empty[s]), ph ^ 1, abort_flag, P.err, kErrWaitEmpty)) {
+          ok = false;
+          break;
+        }
+        const uint32_t bar = smem_u32(&ctl->full[s]);
+        mbar_expect_tx(bar, STAGE_BYTES);
+        const int32_t k0 = (int32_t)(kbeg + (int64_t)kb * BK);
+        const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
+        const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
+        if (P.a_mn) {
+#pragma unroll
+          for (int j = 0; j < BM / 32; ++j) {
+            tma_load_2d(a_hi + j * 4096, &tm_ah, bar, m0 + 32 * j, k0);
+            tma_load_2d(a_lo + j * 4096, &tm_al, bar, m0 + 32 * j, k0);
+          }
+        } else {
+          tma_load_2d(a_hi, &tm_ah, bar, k0, m0);
+          tma_load_2d(a_lo, &tm_al, bar, k0, m0);
+        }
+        if (P.b_mn) {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j) {
+            tma_load_2d(b_hi + j * 4096, &tm_bh, bar, n0 + 32 * j, k0);
+            tma_load_2d(b_lo + j * 4096, &tm_bl, bar, n0 + 32 * j, k0);
+          }
+        } else {
+          tma_load_2d(b_hi, &tm_bh, bar, k0, n0);
+          tma_load_2d(b_lo, &tm_bl, bar, k0, n0);
+        }
+      }
+    }
+    if (!ok) {
+      // let the copies already issued land before the CTA's shared memory goes away
+      const uint32_t first = it >= (uint32_t)STAGES ? it - STAGES : 0;
+      for (uint32_t i = first; i < it; ++i)
+        mbar_drain(smem_u32(&ctl->full[i % STAGES]), (i / STAGES) & 1);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------ MMA issuer
+    const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)P.a_mn << 15) |
+                           ((uint32_t)P.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+    const uint32_t a_step = P.a_mn ? 1024u : 32u, b_step = P.b_mn ? 1024u : 32u;
+    const uint32_t a_lbo = P.a_mn ? 4096u : 16u, b_lbo = P.b_mn ? 4096u : 16u;
+    uint32_t it = 0, tile_i = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x, ++tile_i) {
+      const int64_t split = u / per_split;
+      const int64_t kbeg = split * P.k_chunk;
+      const int64_t kend = min(P.K, kbeg + P.k_chunk);
+      const int nkb = (int)((kend - kbeg + BK - 1) / BK);
+      const uint32_t acc = tile_i & 1;
+      if (!mbar_wait(smem_u32(&ctl->tempty[acc]), ((tile_i >> 1) & 1) ^ 1, abort_flag, P.err,
+                     kErrWaitTEmpty)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem_base + acc * BN;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+        if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
+        const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
+#pragma unroll
+        for (int ks = 0; ks < BK / 8; ++ks) {
+          const uint64_t adh = make_desc(a_hi + ks * a_step, a_lbo, 1024);
+          const uint64_t adl = make_desc(a_lo + ks * a_step, a_lbo, 1024);
+          const uint64_t bdh = make_desc(b_hi + ks * b_step, b_lbo, 1024);
+          const uint64_t bdl = make_desc(b_lo + ks * b_step, b_lbo, 1024);
+          mma_tf32(d, adl, bdh, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
+          mma_tf32(d, adh, bdl, idesc, 1u);
+          mma_tf32(d, adh, bdh, idesc, 1u);
+        }
+        mma_commit(smem_u32(&ctl->empty[s]));
+      }
+      if (!ok) break;
+      mma_commit(smem_u32(&ctl->tfull[acc]));
+    }
+    // all MMAs issued by this thread complete before TMEM is released
+    mma_commit(smem_u32(&ctl->drain));
+    mbar_drain(smem_u32(&ctl->drain), 0);
+  } else if (warp >= 2) {
+    // ------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row_t = q * 32 + lane;
+    const bool dx = P.kind == TC_DX || P.kind == TC_DX_F32;
+    if (dx)
+      for (int c = lane; c < P.N; c += 32) colacc[q * P.N + c] = 0.f;
+    __syncwarp();
+    uint32_t tile_i = 0;
+    for (int64_t u = blockIdx.x; u < P.units; u += gridDim.x, ++tile_i) {
+      const int64_t split = u / per_split, rem = u % per_split;
+      const int64_t m0 = (rem / P.n_tiles) * BM;
+      const int64_t n0 = (rem % P.n_tiles) * BN;
+      const uint32_t acc = tile_i & 1;
+      if (!mbar_wait(smem_u32(&ctl->tfull[acc]), (tile_i >> 1) & 1, abort_flag, P.err,
+                     kErrWaitTFull))
+        break;
+      tc_fence_after();
+      const int64_t row = m0 + row_t;
+      const bool in = row < P.M;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c0, v);
+        const int64_t col0 = n0 + c0;
+        if (P.kind == TC_FWD) {
+          if (in) {
+            float* ph = P.c_hi + row * P.N + col0;
+            float* pl = P.c_lo + row * P.N + col0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 b4 = __ldg(reinterpret_cast<const float4*>(P.bias + col0 + j));
+              float h[4], l[4];
+              const float x[4] = {v[j] + b4.x, v[j + 1] + b4.y, v[j + 2] + b4.z, v[j + 3] + b4.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) tf32_split_pos(x[t] > 0.f ? x[t] : 0.f, h[t], l[t]);
+              store4(ph + j, h[0], h[1], h[2], h[3]);
+              store4(pl + j, l[0], l[1], l[2], l[3]);
+            }
+          }
+        } else if (dx) {
+          if (in) {
+            const float* mrow = P.mask + row * P.N + col0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 m4 = *reinterpret_cast<const float4*>(mrow + j);
+              v[j] = m4.x > 0.f ? v[j] : 0.f;
+              v[j + 1] = m4.y > 0.f ? v[j + 1] : 0.f;
+              v[j + 2] = m4.z > 0.f ? v[j + 2] : 0.f;
+              v[j + 3] = m4.w > 0.f ? v[j + 3] : 0.f;
+            }
+            if (P.kind == TC_DX) {
+              float* ph = P.c_hi + row * P.N + col0;
+              float* pl = P.c_lo + row * P.N + col0;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                float h[4], l[4];
+#pragma unroll
+                for (int t = 0; t < 4; ++t) tf32_split(v[j + t], h[t], l[t]);
+                store4(ph + j, h[0], h[1], h[2], h[3]);
+                store4(pl + j, l[0], l[1], l[2], l[3]);
+              }
+            } else {
+              float* pc = P.c_hi + row * P.N + col0;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) store4(pc + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          if (P.colsum) {
+            // transpose-reduce: afterwards lane L holds the sum over this warp's 32 rows
+            // of column col0 + L
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+              const bool upper = (lane & o) != 0;
+#pragma unroll
+              for (int i = 0; i < o; ++i) {
+                const float send = upper ? v[i] : v[i + o];
+                const float keep = upper ? v[i + o] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+              }
+            }
+            colacc[q * P.N + col0 + lane] += v[0];
+          }
+        } else {  // TC_DW
+          if (in) {
+            float* pc = P.c_part + split * P.M * P.N + row * P.N + col0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) store4(pc + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&ctl->tempty[acc]));
+    }
+    if (dx && P.colsum) {
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
+      const int t = threadIdx.x - 2 * 32;
+      for (int c = t; c < P.N; c += kEpiThreads)
+        P.colsum[(int64_t)blockIdx.x * P.N + c] =
+            ((colacc[c] + colacc[P.N + c]) + colacc[2 * P.N + c]) + colacc[3 * P.N + c];
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------- split kernels
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo, int64_t n, int keep_positive) {
+  const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gs) {
+    float h, l;
+    if (keep_positive)
+      tf32_split_pos(x[i], h, l);
+    else
+      tf32_split(x[i], h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+__global__ void split_weights_kernel(const float* __restrict__ w, int64_t K, int64_t N,
+                                     float* __restrict__ wt_hi, float* __restrict__ wt_lo,
+                                     float* __restrict__ w_hi, float* __restrict__ w_lo) {
+  __shared__ float hs[32][33];
+  __shared__ float ls[32][33];
+  const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int64_t k = k0 + i, n = n0 + threadIdx.x;
+    float h = 0.f, l = 0.f;
+    if (k < K && n < N) {
+      tf32_split(w[k * N + n], h, l);
+      w_hi[k * N + n] = h;
+      w_lo[k * N + n] = l;
+    }
+    hs[i][threadIdx.x] = h;
+    ls[i][threadIdx.x] = l;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int64_t n = n0 + i, k = k0 + threadIdx.x;
+    if (k < K && n < N) {
+      wt_hi[n * K + k] = hs[threadIdx.x][i];
+      wt_lo[n * K + k] = ls[threadIdx.x][i];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D fp32 map of a row-major [outer x inner] array, 128-byte swizzle, zero fill.
+int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
+             uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(kErrCuda, "cuTensorMapEncodeTiled unavailable");
+  if (!aligned16(ptr) || (inner * 4) % 16 != 0)
+    return set_error(kErrAlign, "tensor map: base and row pitch must be 16-byte aligned");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
+                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(kErrCuda, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return kOk;
+}
+
+size_t tc_smem_bytes(int kind, int64_t N) {
+  size_t b = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(Ctl);
+  if (kind == TC_DX || kind == TC_DX_F32) b += (size_t)4 * N * sizeof(float);
+  return b;
+}
+
+int64_t units_of(const TcGemmArgs& a, int* splits) {
+  const int64_t mt = ceil_div(a.M, BM), nt = a.N / BN;
+  int sp = 1;
+  if (a.kind == TC_DW) sp = (int)ceil_div(a.K, a.k_chunk);
+  if (splits) *splits = sp;
+  return mt * nt * sp;
+}
+
+}  // namespace
+
+bool tc_gemm_supported(int kind, int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || N < 1 || K < 1 || N % BN != 0) return false;
+  if (kind == TC_DW) return M % BM == 0 && M <= (1 << 20) && N <= (1 << 20);
+  if (K % BK != 0) return false;
+  if ((kind == TC_DX || kind == TC_DX_F32) && N > kMaxColsumN) return false;
+  return M < (int64_t(1) << 31);
+}
+
+int tc_gemm_splits(const TcGemmArgs& a) {
+  int s = 1;
+  units_of(a, &s);
+  return s;
+}
+
+int tc_gemm_grid(const TcGemmArgs& a) {
+  const int64_t u = units_of(a, nullptr);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(u, sm_count()));
+}
+
+int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
+  SPO_CHECK_ARG(tc_gemm_supported(a.kind, a.M, a.N, a.K), kErrUnsupported,
+                "tc_gemm: unsupported shape (N % 128, K % 32, dW M % 128)");
+  SPO_CHECK_ARG(a.a_hi && a.a_lo && a.b_hi && a.b_lo, kErrArg, "tc_gemm: null operand");
+  if (a.kind == TC_DW)
+    SPO_CHECK_ARG(a.k_chunk >= BK && a.k_chunk % BK == 0 && a.c_part, kErrArg,
+                  "tc_gemm: dW needs c_part and k_chunk a multiple of 32");
+  else
+    SPO_CHECK_ARG(a.c_hi && aligned16(a.c_hi) && (a.kind == TC_DX_F32 || (a.c_lo && aligned16(a.c_lo))),
+                  kErrArg, "tc_gemm: null or misaligned output");
+  if (a.kind == TC_FWD) SPO_CHECK_ARG(a.bias && aligned16(a.bias), kErrArg, "tc_gemm: bias");
+  if (a.kind == TC_DX || a.kind == TC_DX_F32)
+    SPO_CHECK_ARG(a.mask && aligned16(a.mask), kErrArg, "tc_gemm: mask");
+  const bool mn = a.kind == TC_DW;
+  CUtensorMap m_ah, m_al, m_bh, m_bl;
+  int rc;
+  if (mn) {  // A [K x M], B [K x N] row-major; boxes 32 wide (MN) x 32 deep (K)
+    if ((rc = make_map(&m_ah, a.a_hi, a.M, a.K, 32, BK))) return rc;
+    if ((rc = make_map(&m_al, a.a_lo, a.M, a.K, 32, BK))) return rc;
+    if ((rc = make_map(&m_bh, a.b_hi, a.N, a.K, 32, BK))) return rc;
+    if ((rc = make_map(&m_bl, a.b_lo, a.N, a.K, 32, BK))) return rc;
+  } else {   // A [M x K], B [N x K] row-major; boxes 32 deep (K) x 128 rows
+    if ((rc = make_map(&m_ah, a.a_hi, a.K, a.M, BK, BM))) return rc;
+    if ((rc = make_map(&m_al, a.a_lo, a.K, a.M, BK, BM))) return rc;
+    if ((rc = make_map(&m_bh, a.b_hi, a.K, a.N, BK, BN))) return rc;
+    if ((rc = make_map(&m_bl, a.b_lo, a.K, a.N, BK, BN))) return rc;
+  }
+  KParams P{};
+  P.kind = a.kind;
+  P.a_mn = mn;
+  P.b_mn = mn;
+  P.M = a.M;
+  P.N = a.N;
+  P.K = a.K;
+  P.k_chunk = mn ? a.k_chunk : align_up_i64(a.K, BK);
+  P.m_tiles = (int)ceil_div(a.M, BM);
+  P.n_tiles = (int)(a.N / BN);
+  P.units = units_of(a, &P.splits);
+  P.bias = a.bias;
+  P.mask = a.mask;
+  P.c_hi = a.c_hi;
+  P.c_lo = a.c_lo;
+  P.c_part = a.c_part;
+  P.colsum = a.colsum;
+  P.err = a.err;
+  const int grid = tc_gemm_grid(a);
+  const size_t smem = tc_smem_bytes(a.kind, a.N);
+  static bool attr_set = false;
+  if (!attr_set) {
+    SPO_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)tc_smem_bytes(TC_DX, kMaxColsumN)));
+    attr_set = true;
+  }
+  tc_gemm_kernel<<<grid, kThreads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
+
+int split_tf32_launch(const float* x, float* hi, float* lo, int64_t n, bool keep_positive,
+                      cudaStream_t s) {
+  if (n <= 0) return kOk;
+  const int grid = (int)std::min<int64_t>(ceil_div(n, 256), 8LL * sm_count());
+  split_tf32_kernel<<<grid, 256, 0, s>>>(x, hi, lo, n, keep_positive ? 1 : 0);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
+
+int split_weights_launch(const float* w, int64_t K, int64_t N, float* wt_hi, float* wt_lo,
+                         float* w_hi, float* w_lo, cudaStream_t s) {
+  if (K <= 0 || N <= 0) return kOk;
+  split_weights_kernel<<<dim3((unsigned)ceil_div(N, 32), (unsigned)ceil_div(K, 32)), dim3(32, 8), 0,
+                         s>>>(w, K, N, wt_hi, wt_lo, w_hi, w_lo);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
+
+}  // namespace spo

@@ -1,0 +1,73 @@
+// Tensor-core (tcgen05, sm_100a) GEMM of the learner's hidden layers, fp32-accurate
+// through the 3xTF32 split, with the learner epilogues fused.
+//
+// Every fp32 operand x is held as a pair (hi, lo): hi = x with its 13 low mantissa
+// bits cleared (exactly representable in TF32), lo = x - hi (exact in fp32). Then
+//   x . y ~= lo_x hi_y + hi_x lo_y + hi_x hi_y
+// (the dropped lo_x lo_y term is ~2^-22 relative), accumulated in fp32 in tensor
+// memory: the published error-compensated "3xTF32" method (the scheme CUTLASS calls
+// 3xTF32; Ootomo & Yokota 2022). Products of hi/lo halves are exact in the tensor core,
+// so the result carries fp32-level error instead of TF32's 2^-11.
+#pragma once
+
+#include "spo_common.cuh"
+
+namespace spo {
+
+enum TcKind : int {
+  TC_FWD = 0,      // C = relu(A B + bias), written as (hi, lo)
+  TC_DX = 1,       // C = (A B) * [mask > 0], written as (hi, lo), column sums
+  TC_DX_F32 = 2,   // same, written as plain fp32
+  TC_DW = 3,       // split-K partial tiles of A^T-style products (both operands MN-major)
+};
+
+struct TcGemmArgs {
+  int kind;
+  // Operand arrays (each a hi/lo pair). Layout in memory:
+  //   TC_FWD/TC_DX: A row-major [M x K] (pitch K), B row-major [N x K] (pitch K)
+  //   TC_DW:        A row-major [K x M] (pitch M), B row-major [K x N] (pitch N)
+  const float* a_hi;
+  const float* a_lo;
+  const float* b_hi;
+  const float* b_lo;
+  int64_t M, N, K;
+  int64_t k_chunk;         // TC_DW: rows of K per split (multiple of 32)
+  const float* bias;       // TC_FWD: [N]
+  const float* mask;       // TC_DX*: [M x N] (pitch N), keep where > 0
+  float* c_hi;             // [M x N] (pitch N): hi or fp32 result
+  float* c_lo;             // [M x N] (pitch N): lo (TC_FWD, TC_DX)
+  float* c_part;           // TC_DW: [splits][M x N]
+  float* colsum;           // TC_DX*: [grid][N] column sums (optional)
+  int* err;                // device error word (bounded waits), optional
+};
+
+// Launch configuration queries (host).
+int tc_gemm_grid(const TcGemmArgs& a);     // CTAs the launch will use (= colsum parts)
+int tc_gemm_splits(const TcGemmArgs& a);   // TC_DW partial count
+bool tc_gemm_supported(int kind, int64_t M, int64_t N, int64_t K);
+int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s);
+
+// hi/lo split of n floats (elementwise); keep_positive: a positive x never gets hi == 0
+// (so hi > 0 <=> x > 0, the ReLU mask test).
+int split_tf32_launch(const float* x, float* hi, float* lo, int64_t n, bool keep_positive,
+                      cudaStream_t s);
+// W [K x N] -> Wt_hi/Wt_lo [N x K] (transposed) and W_hi/W_lo [K x N].
+int split_weights_launch(const float* w, int64_t K, int64_t N, float* wt_hi, float* wt_lo,
+                         float* w_hi, float* w_lo, cudaStream_t s);
+
+__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
+  hi = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+  lo = v - hi;
+}
+
+// Split of a ReLU output: a positive value never maps to hi == 0 (tiny subnormals keep
+// their full value in hi), so the mask of the layer below can be read from hi alone.
+__device__ __forceinline__ void tf32_split_pos(float v, float& hi, float& lo) {
+  tf32_split(v, hi, lo);
+  if (hi == 0.f && v > 0.f) {
+    hi = v;
+    lo = 0.f;
+  }
+}
+
+}  // namespace spo

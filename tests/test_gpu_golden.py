@@ -142,8 +142,8 @@ def test_actor_backward_fused_learner(ctx, name, batch, hidden):
     dims = (18, hidden, hidden, 9)
     L = Learner(actor_dims=dims, max_rows=batch, use_kl=False, dual=False)
     L.load(actor=_params(t, dims))
-    L.backward({"obs": dev(read_f32(t + "x")), "mask": dev(read_f32(t + "mask")),
-                "q": dev(read_f32(t + "q"))})
+    L.backward({"obs": dev(read_f32(t + "x", (batch, 18))), "mask": dev(read_f32(t + "mask", (batch, 9))),
+                "q": dev(read_f32(t + "q", (batch, 9)))})
     st = L.stats()
     assert abs(st["actor_loss"] - float(read_f32(t + "loss")[0])) <= 2e-5
     for i, (dw, db) in enumerate(L.tensors("actor", L.grads)):
