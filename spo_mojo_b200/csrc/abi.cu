@@ -1043,3 +1043,50 @@ int spo_allreduce_sum(spo_comm_t comm, spo_stream_t stream, float* buf, int64_t 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- tensor-core GEMM
+#include "tc_gemm.cuh"
+
+static int tc_args_of(const spo_tc_gemm_desc* d, TcGemmArgs* a) {
+  SPO_CHECK_ARG(d != nullptr, kErrArg, "null descriptor");
+  SPO_CHECK_ARG(d->kind >= SPO_TC_FWD && d->kind <= SPO_TC_DW, kErrArg, "bad kind");
+  *a = TcGemmArgs{};
+  a->kind = d->kind;
+  a->a_hi = d->a_hi; a->a_lo = d->a_lo; a->b_hi = d->b_hi; a->b_lo = d->b_lo;
+  a->M = d->m; a->N = d->n; a->K = d->k; a->k_chunk = d->k_chunk;
+  a->bias = d->bias; a->mask = d->mask;
+  a->c_hi = d->c_hi; a->c_lo = d->c_lo; a->c_part = d->c_part; a->colsum = d->colsum;
+  a->err = d->err;
+  if (a->kind == TC_DW) {
+    SPO_CHECK_ARG(a->k_chunk >= 32 && a->k_chunk % 32 == 0, kErrArg, "k_chunk must be a multiple of 32");
+  }
+  SPO_CHECK_ARG(tc_gemm_supported(a->kind, a->M, a->N, a->K), kErrUnsupported,
+                "tensor-core GEMM: unsupported shape");
+  return kOk;
+}
+
+extern "C" {
+
+int spo_tc_gemm_shape(const spo_tc_gemm_desc* desc, int32_t* grid, int32_t* splits) {
+  TcGemmArgs a;
+  int rc = tc_args_of(desc, &a);
+  if (rc) return rc;
+  if (grid) *grid = tc_gemm_grid(a);
+  if (splits) *splits = tc_gemm_splits(a);
+  return kOk;
+}
+
+int spo_tc_gemm(spo_stream_t stream, const spo_tc_gemm_desc* desc) {
+  TcGemmArgs a;
+  int rc = tc_args_of(desc, &a);
+  if (rc) return rc;
+  return tc_gemm_launch(a, S(stream));
+}
+
+int spo_split_tf32(spo_stream_t stream, float* hi, float* lo, const float* x, int64_t n,
+                   int32_t keep_positive) {
+  SPO_CHECK_ARG(n >= 0 && (n == 0 || (hi && lo && x)), kErrArg, "bad argument");
+  return split_tf32_launch(x, hi, lo, n, keep_positive != 0, S(stream));
+}
+
+}  // extern "C"

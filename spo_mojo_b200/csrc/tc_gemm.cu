@@ -11,7 +11,9 @@
 // tiles are written by TMA with 128-byte swizzling; K-major operands are read by the
 // UMMA descriptors with SBO = 1024 B (8-row atoms) and a 32-byte start advance per
 // k-step, MN-major operands (the dW products) are loaded as 32-element-wide boxes with
-// LBO = 4096 B between boxes and SBO = 1024 B between 8-row k-groups.
+// LBO = 4096 B between boxes; TF32 MN-major operands need the 128-byte swizzle with
+// 32-byte atoms (TMA SWIZZLE_128B_ATOM_32B, descriptor layout type 1), whose k-groups
+// are 4 rows: SBO = 512 B.
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA sets an abort
 // flag and the caller's error word, the producer waits (bounded) for its copies in
@@ -36,7 +38,9 @@ constexpr int kEpiThreads = 128;
 constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
 constexpr uint32_t B_TILE = BN * BK * 4;                 // 16 KB
 constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 64 KB
-constexpr uint32_t TMEM_COLS = 2 * BN;                   // two accumulators
+constexpr int SEG = 8;                                   // k-blocks per TMEM accumulation
+constexpr uint32_t RS_COL = 2 * BN;                      // fp32 running sum after the two accumulators
+constexpr uint32_t TMEM_COLS = 512;                      // 2 accumulators + running sum, power of 2
 constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
 constexpr uint64_t kDrainNs = 500000000ull;              // 0.5 s
 constexpr int kMaxColsumN = 1024;
@@ -176,14 +180,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// UMMA shared-memory descriptor, SWIZZLE_128B, sm100 version bits.
-__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor (sm100 version bits), 128-byte swizzle layouts.
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)layout << 61;  // 2 = SWIZZLE_128B, 1 = SWIZZLE_128B_BASE32B
   return d;
 }
 
@@ -290,44 +314,52 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
                            ((uint32_t)(BM >> 4) << 24);
     const uint32_t a_step = P.a_mn ? 1024u : 32u, b_step = P.b_mn ? 1024u : 32u;
     const uint32_t a_lbo = P.a_mn ? 4096u : 16u, b_lbo = P.b_mn ? 4096u : 16u;
-    uint32_t it = 0, tile_i = 0;
+    const uint32_t a_sbo = P.a_mn ? 512u : 1024u, b_sbo = P.b_mn ? 512u : 1024u;
+    const uint32_t a_lay = P.a_mn ? 1u : 2u, b_lay = P.b_mn ? 1u : 2u;
+    // Each unit's k-range is cut into segments of at most SEG k-blocks; every segment
+    // gets a fresh accumulator (ping-pong), which the epilogue folds into its fp32
+    // running sum. Few accumulations per TMEM accumulator keep the sum fp32-accurate.
+    uint32_t it = 0, seg_i = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x, ++tile_i) {
+    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
       const int64_t split = u / per_split;
       const int64_t kbeg = split * P.k_chunk;
       const int64_t kend = min(P.K, kbeg + P.k_chunk);
       const int nkb = (int)((kend - kbeg + BK - 1) / BK);
-      const uint32_t acc = tile_i & 1;
-      if (!mbar_wait(smem_u32(&ctl->tempty[acc]), ((tile_i >> 1) & 1) ^ 1, abort_flag, P.err,
-                     kErrWaitTEmpty)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t d = tmem_base + acc * BN;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-        if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull)) {
+      for (int kb0 = 0; kb0 < nkb && ok; kb0 += SEG, ++seg_i) {
+        const uint32_t acc = seg_i & 1;
+        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), ((seg_i >> 1) & 1) ^ 1, abort_flag, P.err,
+                       kErrWaitTEmpty)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
-        const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
+        const uint32_t d = tmem_base + acc * BN;
+        const int kb1 = min(nkb, kb0 + SEG);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+          if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
+          const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
 #pragma unroll
-        for (int ks = 0; ks < BK / 8; ++ks) {
-          const uint64_t adh = make_desc(a_hi + ks * a_step, a_lbo, 1024);
-          const uint64_t adl = make_desc(a_lo + ks * a_step, a_lbo, 1024);
-          const uint64_t bdh = make_desc(b_hi + ks * b_step, b_lbo, 1024);
-          const uint64_t bdl = make_desc(b_lo + ks * b_step, b_lbo, 1024);
-          mma_tf32(d, adl, bdh, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
-          mma_tf32(d, adh, bdl, idesc, 1u);
-          mma_tf32(d, adh, bdh, idesc, 1u);
+          for (int ks = 0; ks < BK / 8; ++ks) {
+            const uint64_t adh = make_desc(a_hi + ks * a_step, a_lbo, a_sbo, a_lay);
+            const uint64_t adl = make_desc(a_lo + ks * a_step, a_lbo, a_sbo, a_lay);
+            const uint64_t bdh = make_desc(b_hi + ks * b_step, b_lbo, b_sbo, b_lay);
+            const uint64_t bdl = make_desc(b_lo + ks * b_step, b_lbo, b_sbo, b_lay);
+            mma_tf32(d, adl, bdh, idesc, (kb > kb0 || ks > 0) ? 1u : 0u);
+            mma_tf32(d, adh, bdl, idesc, 1u);
+            mma_tf32(d, adh, bdh, idesc, 1u);
+          }
+          mma_commit(smem_u32(&ctl->empty[s]));
         }
-        mma_commit(smem_u32(&ctl->empty[s]));
+        if (!ok) break;
+        mma_commit(smem_u32(&ctl->tfull[acc]));
       }
-      if (!ok) break;
-      mma_commit(smem_u32(&ctl->tfull[acc]));
     }
     // all MMAs issued by this thread complete before TMEM is released
     mma_commit(smem_u32(&ctl->drain));
@@ -340,22 +372,42 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     if (dx)
       for (int c = lane; c < P.N; c += 32) colacc[q * P.N + c] = 0.f;
     __syncwarp();
-    uint32_t tile_i = 0;
-    for (int64_t u = blockIdx.x; u < P.units; u += gridDim.x, ++tile_i) {
+    uint32_t seg_i = 0;
+    bool ok = true;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
       const int64_t split = u / per_split, rem = u % per_split;
       const int64_t m0 = (rem / P.n_tiles) * BM;
       const int64_t n0 = (rem % P.n_tiles) * BN;
-      const uint32_t acc = tile_i & 1;
-      if (!mbar_wait(smem_u32(&ctl->tfull[acc]), (tile_i >> 1) & 1, abort_flag, P.err,
-                     kErrWaitTFull))
-        break;
-      tc_fence_after();
+      const int64_t kbeg = split * P.k_chunk;
+      const int64_t kend = min(P.K, kbeg + P.k_chunk);
+      const int nkb = (int)((kend - kbeg + BK - 1) / BK);
+      const int nseg = (nkb + SEG - 1) / SEG;
       const int64_t row = m0 + row_t;
       const bool in = row < P.M;
+      for (int sg = 0; sg < nseg; ++sg, ++seg_i) {
+      const uint32_t acc = seg_i & 1;
+      if (!mbar_wait(smem_u32(&ctl->tfull[acc]), (seg_i >> 1) & 1, abort_flag, P.err,
+                     kErrWaitTFull)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool first_seg = sg == 0, last_seg = sg == nseg - 1;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c0, v);
+        tmem_ld32(tmem_base + lane_addr + acc * BN + c0, v);
+        if (!first_seg) {
+          float r[32];
+          tmem_ld32(tmem_base + lane_addr + RS_COL + c0, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = r[j] + v[j];
+        }
+        if (!last_seg) {
+          tmem_st32(tmem_base + lane_addr + RS_COL + c0, v);
+          continue;
+        }
         const int64_t col0 = n0 + c0;
         if (P.kind == TC_FWD) {
           if (in) {
@@ -426,8 +478,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           }
         }
       }
+      if (!last_seg) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(smem_u32(&ctl->tempty[acc]));
+      }
     }
     if (dx && P.colsum) {
       asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
@@ -503,9 +557,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D fp32 map of a row-major [outer x inner] array, 128-byte swizzle, zero fill.
+// 2-D fp32 map of a row-major [outer x inner] array, 128-byte swizzle (16-byte or
+// 32-byte atoms), zero fill out of bounds.
 int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
-             uint32_t box_outer) {
+             uint32_t box_outer, CUtensorMapSwizzle swz) {
   auto fn = encode_fn();
   if (!fn) return set_error(kErrCuda, "cuTensorMapEncodeTiled unavailable");
   if (!aligned16(ptr) || (inner * 4) % 16 != 0)
@@ -515,7 +570,7 @@ int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, u
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
-                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(kErrCuda, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -574,15 +629,17 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   CUtensorMap m_ah, m_al, m_bh, m_bl;
   int rc;
   if (mn) {  // A [K x M], B [K x N] row-major; boxes 32 wide (MN) x 32 deep (K)
-    if ((rc = make_map(&m_ah, a.a_hi, a.M, a.K, 32, BK))) return rc;
-    if ((rc = make_map(&m_al, a.a_lo, a.M, a.K, 32, BK))) return rc;
-    if ((rc = make_map(&m_bh, a.b_hi, a.N, a.K, 32, BK))) return rc;
-    if ((rc = make_map(&m_bl, a.b_lo, a.N, a.K, 32, BK))) return rc;
+    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    if ((rc = make_map(&m_ah, a.a_hi, a.M, a.K, 32, BK, sw))) return rc;
+    if ((rc = make_map(&m_al, a.a_lo, a.M, a.K, 32, BK, sw))) return rc;
+    if ((rc = make_map(&m_bh, a.b_hi, a.N, a.K, 32, BK, sw))) return rc;
+    if ((rc = make_map(&m_bl, a.b_lo, a.N, a.K, 32, BK, sw))) return rc;
   } else {   // A [M x K], B [N x K] row-major; boxes 32 deep (K) x 128 rows
-    if ((rc = make_map(&m_ah, a.a_hi, a.K, a.M, BK, BM))) return rc;
-    if ((rc = make_map(&m_al, a.a_lo, a.K, a.M, BK, BM))) return rc;
-    if ((rc = make_map(&m_bh, a.b_hi, a.K, a.N, BK, BN))) return rc;
-    if ((rc = make_map(&m_bl, a.b_lo, a.K, a.N, BK, BN))) return rc;
+    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    if ((rc = make_map(&m_ah, a.a_hi, a.K, a.M, BK, BM, sw))) return rc;
+    if ((rc = make_map(&m_al, a.a_lo, a.K, a.M, BK, BM, sw))) return rc;
+    if ((rc = make_map(&m_bh, a.b_hi, a.K, a.N, BK, BN, sw))) return rc;
+    if ((rc = make_map(&m_bl, a.b_lo, a.K, a.N, BK, BN, sw))) return rc;
   }
   KParams P{};
   P.kind = a.kind;

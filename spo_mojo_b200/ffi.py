@@ -53,6 +53,18 @@ class MlpDesc(ctypes.Structure):
         return d
 
 
+class TcGemmDesc(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("a_hi", ctypes.c_void_p), ("a_lo", ctypes.c_void_p),
+                ("b_hi", ctypes.c_void_p), ("b_lo", ctypes.c_void_p), ("m", ctypes.c_int64),
+                ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("k_chunk", ctypes.c_int64),
+                ("bias", ctypes.c_void_p), ("mask", ctypes.c_void_p), ("c_hi", ctypes.c_void_p),
+                ("c_lo", ctypes.c_void_p), ("c_part", ctypes.c_void_p), ("colsum", ctypes.c_void_p),
+                ("err", ctypes.c_void_p)]
+
+
+TC_FWD, TC_DX, TC_DX_F32, TC_DW = 0, 1, 2, 3
+
+
 class LearnerDesc(ctypes.Structure):
     _fields_ = [("actor", MlpDesc), ("critic", MlpDesc), ("max_rows", ctypes.c_int64),
                 ("lr_actor", ctypes.c_float), ("lr_critic", ctypes.c_float),
@@ -123,6 +135,9 @@ SIGNATURES = {
     "spo_adam_flat": (INT, [P, P, P, P, P, I64, F, F, F, F, I32, F]),
     "spo_ema": (INT, [P, P, P, I64, F]),
     "spo_truncated_gae": (INT, [P, P, P, P, P, P, P, P, I64, I32, F]),
+    "spo_tc_gemm_shape": (INT, [ctypes.POINTER(TcGemmDesc), ctypes.POINTER(I32), ctypes.POINTER(I32)]),
+    "spo_tc_gemm": (INT, [P, ctypes.POINTER(TcGemmDesc)]),
+    "spo_split_tf32": (INT, [P, P, P, P, I64, I32]),
     "spo_learner_layout_of": (INT, [ctypes.POINTER(LearnerDesc), ctypes.POINTER(LearnerLayout)]),
     "spo_learner_workspace_size": (SZ, [ctypes.POINTER(LearnerDesc)]),
     "spo_learner_create": (INT, [ctypes.POINTER(LearnerDesc), P, SZ, ctypes.POINTER(P)]),

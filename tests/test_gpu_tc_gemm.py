@@ -1,0 +1,133 @@
+"""The tcgen05 3xTF32 GEMM (spo_tc_gemm) against float64 products, for each fused
+epilogue the learner uses. The bar is fp32-level accuracy: max |error| <= 1e-5 of
+max |reference| (plain TF32 would sit near 1e-3)."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def ffi():
+    from spo_mojo_b200 import ffi as f
+    return f
+
+
+def split(x):
+    f = ffi()
+    hi, lo = torch.empty_like(x), torch.empty_like(x)
+    f.call("spo_split_tf32", None, hi.data_ptr(), lo.data_ptr(), x.data_ptr(), x.numel(), 0)
+    return hi, lo
+
+
+def run(desc):
+    f = ffi()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    desc.err = err.data_ptr()
+    grid, splits = ctypes.c_int32(), ctypes.c_int32()
+    f.call("spo_tc_gemm_shape", ctypes.byref(desc), ctypes.byref(grid), ctypes.byref(splits))
+    f.call("spo_tc_gemm", None, ctypes.byref(desc))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, "a bounded wait in the kernel gave up"
+    return grid.value, splits.value
+
+
+def rel_err(got, want):
+    want = np.asarray(want, np.float64)
+    return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / max(np.max(np.abs(want)), 1e-30))
+
+
+def test_split_is_exact():
+    x = torch.randn(4099, device="cuda") * 10
+    hi, lo = split(x)
+    assert torch.equal(hi + lo, x)
+    assert torch.all((hi.view(torch.int32) & 0x1FFF) == 0)
+
+
+@pytest.mark.parametrize("M,K,N", [(128, 128, 128), (1000, 256, 256), (4096, 512, 512), (300, 1024, 1024)])
+def test_forward_bias_relu(M, K, N):
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(M + K + N)
+    x = torch.randn(M, K, device="cuda", generator=g).relu_()
+    w = torch.randn(K, N, device="cuda", generator=g) / K ** 0.5
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+    xh, xl = split(x)
+    wth, wtl = split(w.t().contiguous())
+    yh, yl = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+    d = f.TcGemmDesc(kind=f.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wth.data_ptr(),
+                     b_lo=wtl.data_ptr(), m=M, n=N, k=K, bias=b.data_ptr(), c_hi=yh.data_ptr(),
+                     c_lo=yl.data_ptr())
+    run(d)
+    want = np.maximum(x.double().cpu().numpy() @ w.double().cpu().numpy() + b.double().cpu().numpy(), 0)
+    got = (yh.double() + yl.double()).cpu().numpy()
+    assert rel_err(got, want) <= 1e-5
+    assert np.array_equal(yh.cpu().numpy() > 0, got > 0)   # hi carries the ReLU mask
+
+
+@pytest.mark.parametrize("M,Kout,Nin", [(1000, 512, 512), (256, 128, 128), (2048, 1024, 512)])
+@pytest.mark.parametrize("kind", ["dx", "dx_f32"])
+def test_dx_mask_colsum(M, Kout, Nin, kind):
+    """dZ_prev = (dY W^T) * [act > 0] with W [Nin x Kout]; column sums = bias grad."""
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(M + Kout + Nin)
+    dy = torch.randn(M, Kout, device="cuda", generator=g) * 1e-3
+    w = torch.randn(Nin, Kout, device="cuda", generator=g) / Kout ** 0.5
+    act = torch.randn(M, Nin, device="cuda", generator=g).relu_()
+    ah, _ = split(act)
+    dyh, dyl = split(dy)
+    wh, wl = split(w)
+    out_h = torch.empty(M, Nin, device="cuda")
+    out_l = torch.empty(M, Nin, device="cuda")
+    desc = f.TcGemmDesc(kind=f.TC_DX if kind == "dx" else f.TC_DX_F32, a_hi=dyh.data_ptr(),
+                        a_lo=dyl.data_ptr(), b_hi=wh.data_ptr(), b_lo=wl.data_ptr(), m=M, n=Nin,
+                        k=Kout, mask=ah.data_ptr(), c_hi=out_h.data_ptr(),
+                        c_lo=out_l.data_ptr() if kind == "dx" else None)
+    grid = ctypes.c_int32()
+    f.call("spo_tc_gemm_shape", ctypes.byref(desc), ctypes.byref(grid), None)
+    cs = torch.full((grid.value, Nin), float("nan"), device="cuda")
+    desc.colsum = cs.data_ptr()
+    run(desc)
+    want = (dy.double() @ w.double().t()).cpu().numpy() * (act.cpu().numpy() > 0)
+    got = (out_h.double() + (out_l.double() if kind == "dx" else 0)).cpu().numpy()
+    assert rel_err(got, want) <= 1e-5
+    assert np.all(got[act.cpu().numpy() <= 0] == 0)
+    assert rel_err(cs.double().sum(0).cpu().numpy(), want.sum(0)) <= 1e-5
+
+
+@pytest.mark.parametrize("rows,Kin,N,chunk", [(4096, 512, 512, 1024), (1000, 128, 128, 256),
+                                               (65536, 256, 256, 4096), (777, 1024, 1024, 224)])
+def test_dw_split_partials(rows, Kin, N, chunk):
+    """dW = act^T dZ from row-major act [rows x Kin] and dZ [rows x N] (both MN-major
+    operands), rows split in chunks, one partial per chunk."""
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(rows + Kin)
+    act = torch.randn(rows, Kin, device="cuda", generator=g).relu_()
+    dz = torch.randn(rows, N, device="cuda", generator=g) * 1e-4
+    ah, al = split(act)
+    zh, zl = split(dz)
+    splits = -(-rows // chunk)
+    part = torch.full((splits, Kin, N), float("nan"), device="cuda")
+    d = f.TcGemmDesc(kind=f.TC_DW, a_hi=ah.data_ptr(), a_lo=al.data_ptr(), b_hi=zh.data_ptr(),
+                     b_lo=zl.data_ptr(), m=Kin, n=N, k=rows, k_chunk=chunk, c_part=part.data_ptr())
+    grid, sp = run(d)
+    assert sp == splits
+    want = act.double().t().cpu().numpy() @ dz.double().cpu().numpy()
+    got = part.double().sum(0).cpu().numpy()
+    assert rel_err(got, want) <= 1e-5
+
+
+def test_unsupported_shapes_are_rejected():
+    f = ffi()
+    d = f.TcGemmDesc(kind=f.TC_FWD, m=128, n=96, k=128)  # n not a multiple of 128
+    with pytest.raises(f.SpoError) as e:
+        f.call("spo_tc_gemm_shape", ctypes.byref(d), None, None)
+    assert e.value.code == -7
