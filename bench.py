@@ -54,6 +54,8 @@ def parse():
                     help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--engine", default="tensor", choices=["tensor", "cuda"],
+                    help="tensor: tcgen05 3xTF32 for the hidden layers; cuda: fp32 FMA everywhere")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the global batch (profiling of small cases only; not a bench line)")
     return ap.parse_args()
@@ -186,13 +188,73 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- GPU arm
-def count_launches(wl, clip):
+def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
+    """Time the dominant kernel — the hidden x hidden forward GEMM with the step's shape —
+    through the same C-ABI entry the learner uses, with CUDA events on the step's stream.
+    achieved = algorithmic fp32 FLOPs (2 rows H^2) / average launch time."""
+    import ctypes
+    import torch
+    from spo_mojo_b200 import ffi
+    pk, kind = peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.rand(rows, H, device=dev, generator=g)
+    w = torch.rand(H, H, device=dev, generator=g)
+    bb = torch.zeros(H, device=dev)
+    y = torch.empty(rows, H, device=dev)
+    if engine == "tensor":
+        xh, xl, wh, wl, yl = (torch.empty_like(t) for t in (x, x, w, w, y))
+        for src, hi, lo in ((x, xh, xl), (w, wh, wl)):
+            ffi.call("spo_split_tf32", stream.cuda_stream, hi.data_ptr(), lo.data_ptr(), src.data_ptr(),
+                     src.numel(), 1)
+        d = ffi.TcGemmDesc(kind=ffi.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wh.data_ptr(),
+                           b_lo=wl.data_ptr(), m=rows, n=H, k=H, bias=bb.data_ptr(), c_hi=y.data_ptr(),
+                           c_lo=yl.data_ptr())
+        launch = lambda: ffi.call("spo_tc_gemm", stream.cuda_stream, ctypes.byref(d))  # noqa: E731
+        name = "tc_gemm_kernel (tcgen05 3xTF32), hidden forward %dx%dx%d" % (rows, H, H)
+    else:
+        launch = lambda: ffi.call("spo_linear_fwd", stream.cuda_stream, y.data_ptr(), x.data_ptr(),  # noqa: E731
+                                  w.data_ptr(), bb.data_ptr(), rows, H, H, 1)
+        name = "gemm_simt_kernel (fp32 FMA), hidden forward %dx%dx%d" % (rows, H, H)
+    for _ in range(3):
+        launch()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for _ in range(reps):
+        launch()
+    k1.record(stream)
+    k1.synchronize()
+    kms = k0.elapsed_time(k1) / reps
+    flops = 2.0 * rows * H * H
+    achieved = flops / (kms / 1e3) / 1e12
+    peak = pk.get("bf16_tflops_sustained") or pk.get("bf16_tflops")
+    roof = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak,
+            "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_kind": f"{kind} bf16 dense, sustained", "ms_per_launch": kms,
+            "traffic": TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("bytes") if rows == 1048576 else None,
+            "traffic_source": TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("source")}
+    if engine == "tensor":
+        # 3xTF32 issues three TF32 MMAs per fp32 product; TF32 runs at half the bf16 rate
+        roof["tf32_mma_tflops"] = 3 * achieved
+        roof["tf32_frac_of_half_bf16_peak"] = 3 * achieved / (peak / 2)
+    return roof
+
+
+# DRAM bytes (read + write) per launch of the roofline kernel at 1,048,576 rows, from the
+# ncu captures summarised under profiles/ (scaled from the captured row count).
+TRAFFIC_PER_LAUNCH = {}
+
+
+def count_launches(wl, clip, engine="tensor"):
+    """libspo_cuda kernel launches of one learner step."""
     n = 0
     for net in (wl.actor, wl.critic):
         if net is None:
             continue
         L = net.num_layers
         n += (L - 1) + 1 + (L - 1) + (L - 2)    # forward GEMMs, head, dW GEMMs, dX GEMMs
+        hidden = net.dims[1:-1]
+        if engine == "tensor" and L >= 3 and all(h % 128 == 0 and h <= 1024 for h in hidden):
+            n += L - 2                           # per-step TF32 split of the hidden weights
     return n + 1 + 1 + (1 if clip else 0)      # reduce, adam, sum of squares
 
 
@@ -219,7 +281,7 @@ def run_ours(args):
     batch_np = make_batch(wl, rows, seed=100 + rank)
     host = {k: torch.from_numpy(v).pin_memory() for k, v in batch_np.items()}
     batch = {k: v.to(dev) for k, v in host.items()}
-    L = Learner.for_workload(wl, max_rows=rows, device=local)
+    L = Learner.for_workload(wl, max_rows=rows, device=local, engine=args.engine)
     L.load(actor=params.get("actor"), critic=params.get("critic"), log_alpha=wl.log_alpha)
     comm = None
     if world > 1:
@@ -304,32 +366,7 @@ def run_ours(args):
     net = wl.actor or wl.critic
     H = net.dims[1]
     if rank == 0:
-        pk, kind = peaks()
-        x = torch.rand(rows, H, device=dev)
-        w = torch.rand(H, H, device=dev)
-        bb = torch.zeros(H, device=dev)
-        y = torch.empty(rows, H, device=dev)
-        reps = 20
-        for _ in range(3):
-            ffi.call("spo_linear_fwd", stream.cuda_stream, y.data_ptr(), x.data_ptr(), w.data_ptr(),
-                     bb.data_ptr(), rows, H, H, 1)
-        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        k0.record(stream)
-        for _ in range(reps):
-            ffi.call("spo_linear_fwd", stream.cuda_stream, y.data_ptr(), x.data_ptr(), w.data_ptr(),
-                     bb.data_ptr(), rows, H, H, 1)
-        k1.record(stream)
-        k1.synchronize()
-        kms = k0.elapsed_time(k1) / reps
-        flops = 2.0 * rows * H * H
-        achieved = flops / (kms / 1e3) / 1e12
-        peak = pk.get("bf16_tflops_sustained") or pk.get("bf16_tflops")
-        roof = {"bound": "tensor", "kernel": "hidden GEMM %dx%dx%d (forward shape)" % (rows, H, H),
-                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_kind": f"{kind} bf16 dense, sustained", "ms_per_launch": kms,
-                "traffic": None,
-                "fp32_simt_nominal_tflops": 148 * 128 * 2 * 1.965e9 / 1e12}
-        del x, w, y
+        roof = roofline_hidden_gemm(args, rows, H, dev, stream, engine=args.engine)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -353,7 +390,8 @@ def run_ours(args):
                              % (sum(v.nbytes for v in batch_np.values()) / 1e6,
                                 rows * sum(sum(n.dims[1:-1]) for n in (wl.actor, wl.critic) if n) * 4 / 1e9)},
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
-            "gpu_launches": count_launches(wl, clip) * args.steps + (0 if world == 1 else 0),
+            "gpu_launches": count_launches(wl, clip, args.engine) * args.steps,
+            "engine": args.engine,
             "stats": stats,
         }
         print(json.dumps(line))

@@ -213,9 +213,9 @@ SPO_API int spo_truncated_gae(spo_stream_t stream, float* adv, float* targets, c
 /* ------------------------------------------------------------------ tensor-core GEMM
  * The hidden-layer products of linear_forward / linear_backward
  * (networks/linear.mojo:37-167) on sm_100a tensor cores (tcgen05, TF32 inputs, fp32
- * accumulation) at fp32 accuracy through the 3xTF32 split: every operand is a pair
- * (hi, lo) with hi = x with its 13 low mantissa bits cleared and lo = x - hi, and
- * C = lo_A hi_B + hi_A lo_B + hi_A hi_B.
+ * accumulation) at near-fp32 accuracy through the 3xTF32 split: every operand is a pair
+ * of TF32 values (hi, lo) with hi = round-to-nearest TF32 of x and lo = the same rounding
+ * of x - hi (spo_split_tf32), and C = lo_A hi_B + hi_A lo_B + hi_A hi_B.
  *   SPO_TC_FWD     C = relu(A B^T + bias) -> (c_hi, c_lo) split, A [m x k], B [n x k]
  *   SPO_TC_DX      C = (A B^T) * (mask > 0) -> (c_hi, c_lo), column sums -> colsum
  *   SPO_TC_DX_F32  as SPO_TC_DX, C written as plain fp32 to c_hi
@@ -269,6 +269,9 @@ typedef struct spo_learner_desc {
   float kl_eps;         /* dual target epsilon */
   int32_t use_kl;       /* alpha * KL(pi_old || pi) term (needs batch.logits_old) */
   int32_t dual;         /* update log_alpha with the dual gradient */
+  int32_t engine;       /* 0: tensor cores (3xTF32 tcgen05) for the hidden x hidden layers
+                           when every hidden width is a multiple of 128 and <= 1024;
+                           1: CUDA cores (fp32 FMA) for every layer */
 } spo_learner_desc;
 
 typedef struct spo_learner_layout {
@@ -312,6 +315,16 @@ SPO_API int spo_learner_backward(spo_learner_t learner, spo_stream_t stream, con
                          float grad_scale, const spo_train_state* state);
 /* Optional clip, Adam over the flat buffers, dual update; increments *step. */
 SPO_API int spo_learner_apply(spo_learner_t learner, spo_stream_t stream, const spo_train_state* state);
+/* The activation cache of the last forward (CriticCache a1, a2, ...,
+ * networks/mlp.mojo:84-102): device pointers to the post-ReLU activations of hidden layer
+ * `layer` (0-based, [rows x d_{layer+1}]) of network `which` (0 actor, 1 critic). With the
+ * tensor-core engine the activation is stored as a TF32 hi/lo pair (value = hi + lo) and
+ * *lo is set; otherwise *lo is NULL. Valid until the next call on the learner. */
+SPO_API int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer,
+                              const float** hi, const float** lo);
+/* Reads (synchronously) and clears the learner's device error word: 0 when every
+ * bounded wait of its tensor-core kernels completed since the last call. */
+SPO_API int spo_learner_status(spo_learner_t learner, int32_t* device_error);
 /* backward (grad_scale = 1 / rows) + apply. */
 SPO_API int spo_learner_step(spo_learner_t learner, spo_stream_t stream, const spo_batch* batch,
                      const spo_train_state* state);

@@ -77,13 +77,18 @@ def mlp_forward(params, x, dtype=np.float64):
     return acts, h
 
 
-def mlp_backward(params, x, acts, dout, dtype=np.float64):
+def mlp_backward(params, x, acts, dout, dtype=np.float64, masks=None):
     """Gradients of all layers from dL/d(output) (networks/mlp.mojo:236-275).
 
     backward_from_dvalue: walk the layers top-down; each linear_backward hands dx to
     the layer below, which passes through relu_backward_kernel
     (networks/mlp.mojo:155-166): the gradient is zeroed where the STORED post-ReLU
     activation is <= 0. Returns a list of (dW, db) in layer order.
+
+    ``masks`` (optional, one boolean array per hidden layer) replaces the ReLU decisions
+    acts > 0: a checker uses it to differentiate through the same branch of the
+    piecewise-linear network as an fp32 computation whose activations sit within
+    rounding distance of zero.
     """
     grads = [None] * len(params)
     d = dout.astype(dtype, copy=False)
@@ -92,7 +97,8 @@ def mlp_backward(params, x, acts, dout, dtype=np.float64):
         dw, db, dx = linear_backward(inp, params[i][0], d, dtype)
         grads[i] = (dw, db)
         if i > 0:
-            d = np.where(acts[i - 1] > 0, dx, 0.0)
+            keep = acts[i - 1] > 0 if masks is None else masks[i - 1]
+            d = np.where(keep, dx, 0.0)
     return grads
 
 

@@ -24,6 +24,7 @@
 #include "../../include/spo_cuda.h"
 #include "gemm_simt.cuh"
 #include "kernels.cuh"
+#include "tc_gemm.cuh"
 
 namespace spo {
 
@@ -225,9 +226,18 @@ struct NetPlan {
   spo_mlp_desc d{};
   int64_t w_off[SPO_MAX_LAYERS], b_off[SPO_MAX_LAYERS], size = 0, offset = 0;
   int64_t max_hidden = 0;
+  // Tensor-core mode: hidden x hidden products on tcgen05 (3xTF32). Activations and the
+  // gradients between hidden layers are then stored as TF32 hi/lo pairs (acts/acts_lo,
+  // dz/dz_lo); dz0 is the plain fp32 gradient of layer 0's output (its dW stays on the
+  // CUDA cores: the 27-wide input has no 16-byte-aligned rows for TMA).
+  bool tc = false;
   // workspace carve-outs
-  float* acts[SPO_MAX_LAYERS] = {};  // a_l, l = 0..L-2: [rows x d_{l+1}]
-  float* dz[2] = {};                 // ping-pong [rows x max_hidden]
+  float* acts[SPO_MAX_LAYERS] = {};     // a_l, l = 0..L-2: [rows x d_{l+1}] (hi in TC mode)
+  float* acts_lo[SPO_MAX_LAYERS] = {};  // TC mode: lo halves
+  float* dz[2] = {};                    // ping-pong [rows x max_hidden] (hi in TC mode)
+  float* dz_lo[2] = {};                 // TC mode
+  float* dz0 = nullptr;                 // TC mode: [rows x d_1] fp32
+  float* wsplit[SPO_MAX_LAYERS][4] = {};  // TC mode, hidden l: W^T hi, W^T lo, W hi, W lo
   float* head_dw = nullptr;          // [Gh][d_{L-1} x d_L]
   float* head_db = nullptr;          // [Gh][d_L]
   float* head_dbx = nullptr;         // [Gh][d_{L-1}]
@@ -244,6 +254,7 @@ struct spo_learner {
   spo::NetPlan net[2];  // 0 actor, 1 critic
   float* sumsq_part = nullptr;
   unsigned* ticket = nullptr;
+  int* err = nullptr;  // device error word of the tensor-core kernels' bounded waits
   size_t ws_bytes = 0;
 };
 
@@ -252,22 +263,72 @@ namespace {
 
 int64_t head_parts_bound() { return 2LL * sm_count(); }
 
+// Tensor-core mode when every hidden width is a multiple of 128 (the tcgen05 tile) and at
+// most 1024 (the fused head and the dX column sums), with at least one hidden x hidden
+// layer to put on the tensor cores.
+bool net_uses_tc(const spo_mlp_desc& d, int engine) {
+  if (engine == 1 || d.num_layers < 3) return false;
+  for (int l = 1; l < d.num_layers; ++l)
+    if (d.dims[l] % 128 != 0 || d.dims[l] > 1024) return false;
+  return true;
+}
+
+// Upper bound of the row splits of a tensor-core dW launch for `rows` rows.
+int64_t tc_dw_splits_max(int64_t rows) {
+  return std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 32) / 64, 4LL * sm_count()));
+}
+
+// Row splits S of a tensor-core dW product with `tiles` output tiles: at least 64
+// k-blocks (2048 rows) per unit, and the smallest S whose tiles*S units fill the SMs in
+// whole waves (>= 95% of the last wave busy), else the best such fill.
+int64_t tc_dw_splits(int64_t tiles, int64_t rows) {
+  const int64_t sms = sm_count();
+  const int64_t smax = tc_dw_splits_max(rows);
+  int64_t best = 1;
+  double best_eff = -1.0;
+  for (int64_t S = 1; S <= smax; ++S) {
+    const int64_t units = tiles * S;
+    const double eff = (double)units / (double)(ceil_div(units, sms) * sms);
+    if (units >= sms && eff >= 0.95) return S;
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = S;
+    }
+  }
+  return best;
+}
+
 void carve_net(NetPlan& n, Carve& c, int64_t rows) {
   const spo_mlp_desc& d = n.d;
   const int L = d.num_layers;
-  for (int l = 0; l + 1 < L; ++l) n.acts[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
-  for (int i = 0; i < 2; ++i) n.dz[i] = c.take<float>((size_t)rows * n.max_hidden);
+  for (int l = 0; l + 1 < L; ++l) {
+    n.acts[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
+    if (n.tc) n.acts_lo[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
+  }
+  for (int i = 0; i < 2; ++i) {
+    n.dz[i] = c.take<float>((size_t)rows * n.max_hidden);
+    if (n.tc) n.dz_lo[i] = c.take<float>((size_t)rows * n.max_hidden);
+  }
+  if (n.tc) {
+    n.dz0 = c.take<float>((size_t)rows * d.dims[1]);
+    for (int l = 1; l + 1 < L; ++l)
+      for (int k = 0; k < 4; ++k) n.wsplit[l][k] = c.take<float>((size_t)d.dims[l] * d.dims[l + 1]);
+  }
   const int64_t gh = head_parts_bound();
   const int64_t hl = d.dims[L - 1], al = d.dims[L];
   n.head_dw = c.take<float>((size_t)(gh * hl * al));
   n.head_db = c.take<float>((size_t)(gh * al));
   n.head_dbx = c.take<float>((size_t)(gh * hl));
   n.head_stats = c.take<float>((size_t)(gh * kStats));
-  for (int l = 0; l + 1 < L; ++l)
-    n.dw_part[l] = c.take<float>((size_t)(dw_parts_bound(d.dims[l], d.dims[l + 1]) *
-                                          d.dims[l] * d.dims[l + 1]));
-  for (int l = 0; l + 2 < L; ++l)  // db of layer l comes from layer l+1's dX GEMM
-    n.db_part[l] = c.take<float>((size_t)(fwd_parts_bound(d.dims[l + 1]) * d.dims[l + 1]));
+  for (int l = 0; l + 1 < L; ++l) {
+    const int64_t parts = (n.tc && l >= 1) ? tc_dw_splits_max(rows)
+                                           : dw_parts_bound(d.dims[l], d.dims[l + 1]);
+    n.dw_part[l] = c.take<float>((size_t)(parts * d.dims[l] * d.dims[l + 1]));
+  }
+  for (int l = 0; l + 2 < L; ++l) {  // db of layer l comes from layer l+1's dX GEMM
+    const int64_t parts = std::max<int64_t>(fwd_parts_bound(d.dims[l + 1]), n.tc ? sm_count() : 0);
+    n.db_part[l] = c.take<float>((size_t)(parts * d.dims[l + 1]));
+  }
 }
 
 int check_net_desc(const spo_mlp_desc& d, int out_dim, const char* which) {
@@ -318,6 +379,7 @@ int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* b
     n.offset = off;
     off += n.size;
     for (int l = 1; l < d.num_layers; ++l) n.max_hidden = std::max<int64_t>(n.max_hidden, d.dims[l]);
+    n.tc = net_uses_tc(d, desc->engine);
   }
   spo_learner_layout& lay = L->layout;
   lay.actor_offset = L->net[0].offset;
@@ -341,22 +403,130 @@ int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* b
     if (L->net[i].present) carve_net(L->net[i], c, desc->max_rows);
   L->sumsq_part = c.take<float>(kMaxGroups * kSumsqParts);
   L->ticket = c.take<unsigned>(4);
+  L->err = c.take<int>(4);
   *bytes = c.off + 256;
   return kOk;
 }
 
 
-// Forward of layers 0..L-2 (ReLU) into the activation cache.
+// Layer 0 forward with the activation written as a TF32 hi/lo pair.
+int gemm_fwd_split(cudaStream_t s, float* y_hi, float* y_lo, const float* x, const float* w,
+                   const float* b, int64_t rows, int64_t k, int64_t n) {
+  if (rows == 0) return kOk;
+  FwdCfg c = fwd_cfg(rows, n);
+  GemmParams p{};
+  p.A = x; p.B = w; p.C = y_hi; p.C2 = y_lo; p.bias = b;
+  p.M = rows; p.N = n; p.K = k;
+  p.lda = k; p.ldb = n; p.ldc = n;
+  p.k_chunk = align_up(std::max<int64_t>(k, 1), 16);
+  return gemm_simt_launch(c.tile, OP_ROW, OP_ROW, EPI_BIAS_RELU_SPLIT, p, c.grid, s);
+}
+
+// Forward of layers 0..L-2 (ReLU) into the activation cache. In tensor-core mode the
+// hidden weights are first split into TF32 hi/lo pairs (W^T for the forward, W for dX).
 int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, const float* obs,
-                       int64_t rows) {
+                       int64_t rows, int* err) {
   const spo_mlp_desc& d = n.d;
-  const float* h = obs;
-  for (int l = 0; l + 1 < d.num_layers; ++l) {
-    int rc = gemm_fwd(s, n.acts[l], h, params + n.w_off[l], params + n.b_off[l], rows, d.dims[l],
-                      d.dims[l + 1], true);
-    if (rc) return rc;
-    h = n.acts[l];
+  if (!n.tc) {
+    const float* h = obs;
+    for (int l = 0; l + 1 < d.num_layers; ++l) {
+      int rc = gemm_fwd(s, n.acts[l], h, params + n.w_off[l], params + n.b_off[l], rows, d.dims[l],
+                        d.dims[l + 1], true);
+      if (rc) return rc;
+      h = n.acts[l];
+    }
+    return kOk;
   }
+  for (int l = 1; l + 1 < d.num_layers; ++l) {
+    int rc = split_weights_launch(params + n.w_off[l], d.dims[l], d.dims[l + 1], n.wsplit[l][0],
+                                  n.wsplit[l][1], n.wsplit[l][2], n.wsplit[l][3], s);
+    if (rc) return rc;
+  }
+  int rc = gemm_fwd_split(s, n.acts[0], n.acts_lo[0], obs, params + n.w_off[0], params + n.b_off[0],
+                          rows, d.dims[0], d.dims[1]);
+  if (rc) return rc;
+  if (rows == 0) return kOk;
+  for (int l = 1; l + 1 < d.num_layers; ++l) {
+    TcGemmArgs a{};
+    a.kind = TC_FWD;
+    a.a_hi = n.acts[l - 1];
+    a.a_lo = n.acts_lo[l - 1];
+    a.b_hi = n.wsplit[l][0];
+    a.b_lo = n.wsplit[l][1];
+    a.M = rows;
+    a.N = d.dims[l + 1];
+    a.K = d.dims[l];
+    a.bias = params + n.b_off[l];
+    a.c_hi = n.acts[l];
+    a.c_lo = n.acts_lo[l];
+    a.err = err;
+    rc = tc_gemm_launch(a, s);
+    if (rc) return rc;
+  }
+  return kOk;
+}
+
+// Backward of the hidden layers L-2..1 on the tensor cores (dW split over rows; dX with
+// the ReLU mask and the bias-gradient column sums fused), then layer 0's dW on the CUDA
+// cores from the fp32 dz0.
+int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, const float* obs,
+                    int64_t rows, float* grads, ReduceParams& red, int* err) {
+  const spo_mlp_desc& d = n.d;
+  const int L = d.num_layers;
+  int cur = 0;
+  int rc;
+  for (int l = L - 2; l >= 1; --l) {
+    const int64_t kin = d.dims[l], nout = d.dims[l + 1];
+    int parts = 0;
+    if (rows > 0) {
+      TcGemmArgs w{};
+      w.kind = TC_DW;
+      w.a_hi = n.acts[l - 1];
+      w.a_lo = n.acts_lo[l - 1];
+      w.b_hi = n.dz[cur];
+      w.b_lo = n.dz_lo[cur];
+      w.M = kin;
+      w.N = nout;
+      w.K = rows;
+      const int64_t S = tc_dw_splits((kin / 128) * (nout / 128), rows);
+      w.k_chunk = align_up(ceil_div(ceil_div(rows, 32), S), 1) * 32;
+      w.c_part = n.dw_part[l];
+      w.err = err;
+      parts = tc_gemm_splits(w);
+      rc = tc_gemm_launch(w, s);
+      if (rc) return rc;
+    }
+    add_seg(red, n.dw_part[l], grads + n.w_off[l], kin * nout, kin * nout, parts);
+
+    int cparts = 0;
+    if (rows > 0) {
+      TcGemmArgs x{};
+      const bool last = l == 1;
+      x.kind = last ? TC_DX_F32 : TC_DX;
+      x.a_hi = n.dz[cur];
+      x.a_lo = n.dz_lo[cur];
+      x.b_hi = n.wsplit[l][2];
+      x.b_lo = n.wsplit[l][3];
+      x.M = rows;
+      x.N = kin;
+      x.K = nout;
+      x.mask = n.acts[l - 1];
+      x.c_hi = last ? n.dz0 : n.dz[cur ^ 1];
+      x.c_lo = last ? nullptr : n.dz_lo[cur ^ 1];
+      x.colsum = n.db_part[l - 1];
+      x.err = err;
+      cparts = tc_gemm_grid(x);
+      rc = tc_gemm_launch(x, s);
+      if (rc) return rc;
+    }
+    add_seg(red, n.db_part[l - 1], grads + n.b_off[l - 1], kin, kin, cparts);
+    cur ^= 1;
+  }
+  int parts = 0;
+  rc = gemm_dw(s, n.dw_part[0], obs, n.dz0, rows, d.dims[0], d.dims[1], &parts);
+  if (rc) return rc;
+  add_seg(red, n.dw_part[0], grads + n.w_off[0], (int64_t)d.dims[0] * d.dims[1],
+          (int64_t)d.dims[0] * d.dims[1], parts);
   return kOk;
 }
 
@@ -369,12 +539,14 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
   const spo_mlp_desc& d = n.d;
   const int L = d.num_layers;
   const int64_t rows = b.rows;
-  int rc = net_forward_hidden(n, s, params, b.obs, rows);
+  int rc = net_forward_hidden(n, s, params, b.obs, rows, Lr->err);
   if (rc) return rc;
 
   const int hl = d.dims[L - 1], al = d.dims[L];
   HeadParams hp{};
   hp.act = n.acts[L - 2];
+  hp.act_lo = n.tc ? n.acts_lo[L - 2] : nullptr;
+  hp.dX_lo = n.tc ? n.dz_lo[0] : nullptr;
   hp.W = params + n.w_off[L - 1];
   hp.b = params + n.b_off[L - 1];
   hp.M = rows;
@@ -408,6 +580,12 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
   *stats_src = n.head_stats;
   *stats_parts = ghp;
 
+  if (n.tc) {
+    rc = net_backward_tc(n, s, params, b.obs, rows, grads, red, Lr->err);
+    if (rc) return rc;
+    add_gap_segs(red, d, n.w_off, n.b_off, n.size, grads);
+    return kOk;
+  }
   int cur = 0;
   for (int l = L - 2; l >= 0; --l) {
     const float* in = l == 0 ? b.obs : n.acts[l - 1];
@@ -907,6 +1085,7 @@ int spo_learner_create(const spo_learner_desc* desc, void* workspace, size_t wor
     if (rc == kOk) {
       L->ws_bytes = need;
       cudaError_t e = cudaMemset(L->ticket, 0, 4 * sizeof(unsigned));
+      if (e == cudaSuccess) e = cudaMemset(L->err, 0, 4 * sizeof(int));
       if (e != cudaSuccess) rc = set_error(kErrCuda, std::string("memset: ") + cudaGetErrorString(e));
     }
     if (rc != kOk) {
@@ -934,6 +1113,27 @@ int spo_learner_apply(spo_learner_t learner, spo_stream_t stream, const spo_trai
   return learner_apply(learner, S(stream), state);
 }
 
+int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer, const float** hi,
+                      const float** lo) {
+  SPO_CHECK_ARG(learner && hi && lo, kErrArg, "null argument");
+  SPO_CHECK_ARG((which == 0 || which == 1) && learner->net[which].present, kErrArg,
+                "no such network");
+  const NetPlan& n = learner->net[which];
+  SPO_CHECK_ARG(layer >= 0 && layer + 1 < n.d.num_layers, kErrArg, "no such hidden layer");
+  *hi = n.acts[layer];
+  *lo = n.tc ? n.acts_lo[layer] : nullptr;
+  return kOk;
+}
+
+int spo_learner_status(spo_learner_t learner, int32_t* device_error) {
+  SPO_CHECK_ARG(learner && device_error, kErrArg, "null argument");
+  int v = 0;
+  SPO_CUDA_TRY(cudaMemcpy(&v, learner->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v != 0) SPO_CUDA_TRY(cudaMemset(learner->err, 0, sizeof(int)));
+  *device_error = v;
+  return kOk;
+}
+
 int spo_learner_step(spo_learner_t learner, spo_stream_t stream, const spo_batch* batch,
                      const spo_train_state* state) {
   SPO_CHECK_ARG(learner && batch, kErrArg, "null argument");
@@ -953,9 +1153,13 @@ int spo_learner_forward(spo_learner_t learner, spo_stream_t stream, int32_t whic
   const NetPlan& n = learner->net[which];
   const float* p = params + n.offset;
   cudaStream_t s = S(stream);
-  int rc = net_forward_hidden(n, s, p, obs, rows);
+  int rc = net_forward_hidden(n, s, p, obs, rows, learner->err);
   if (rc) return rc;
   const int L = n.d.num_layers;
+  if (n.tc) {  // the last layer reads plain fp32: fold lo into hi (the cache is scratch here)
+    rc = combine_tf32_launch(n.acts[L - 2], n.acts_lo[L - 2], rows * n.d.dims[L - 1], s);
+    if (rc) return rc;
+  }
   rc = gemm_fwd(s, out, n.acts[L - 2], p + n.w_off[L - 1], p + n.b_off[L - 1], rows, n.d.dims[L - 1],
                 n.d.dims[L], false);
   if (rc) return rc;
@@ -1045,7 +1249,6 @@ int spo_allreduce_sum(spo_comm_t comm, spo_stream_t stream, float* buf, int64_t 
 }  // extern "C"
 
 // ---------------------------------------------------------------- tensor-core GEMM
-#include "tc_gemm.cuh"
 
 static int tc_args_of(const spo_tc_gemm_desc* d, TcGemmArgs* a) {
   SPO_CHECK_ARG(d != nullptr, kErrArg, "null descriptor");

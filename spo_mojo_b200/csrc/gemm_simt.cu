@@ -26,6 +26,7 @@ int launch_tile(int aop, int bop, int epi, const GemmParams& p, dim3 grid, cudaS
   if (aop == OP_ROW && bop == OP_ROW) {
     if (epi == EPI_BIAS) return launch_v<BM, BN, BK, TM, TN, OP_ROW, OP_ROW, EPI_BIAS>(p, grid, s, va, vb);
     if (epi == EPI_BIAS_RELU) return launch_v<BM, BN, BK, TM, TN, OP_ROW, OP_ROW, EPI_BIAS_RELU>(p, grid, s, va, vb);
+    if (epi == EPI_BIAS_RELU_SPLIT) return launch_v<BM, BN, BK, TM, TN, OP_ROW, OP_ROW, EPI_BIAS_RELU_SPLIT>(p, grid, s, va, vb);
   } else if (aop == OP_ROW && bop == OP_COL) {
     if (epi == EPI_STORE) return launch_v<BM, BN, BK, TM, TN, OP_ROW, OP_COL, EPI_STORE>(p, grid, s, va, vb);
     if (epi == EPI_RELU_MASK) return launch_v<BM, BN, BK, TM, TN, OP_ROW, OP_COL, EPI_RELU_MASK>(p, grid, s, va, vb);

@@ -22,12 +22,15 @@
 namespace spo {
 
 enum : int { OP_ROW = 0, OP_COL = 1 };
-enum : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU_MASK = 3 };
+// EPI_BIAS_RELU_SPLIT: bias + ReLU written as a TF32 hi/lo pair (C = hi, C2 = lo), the
+// operand format of the tensor-core layers that consume it.
+enum : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU_MASK = 3, EPI_BIAS_RELU_SPLIT = 4 };
 
 struct GemmParams {
   const float* A;
   const float* B;
   float* C;
+  float* C2;               // EPI_BIAS_RELU_SPLIT: lo half, same layout as C
   const float* bias;       // EPI_BIAS*: [N]
   const float* mask;       // EPI_RELU_MASK: keep C where mask[m * ldm + n] > 0
   float* colsum;           // optional: [gridDim.y][N] column sums of the stored C
@@ -234,11 +237,13 @@ gemm_simt_kernel(const GemmParams p) {
         const int64_t col0 = n0 + cj * TX * 4 + tx * 4;
         float v[4] = {acc[i][cj * 4], acc[i][cj * 4 + 1], acc[i][cj * 4 + 2], acc[i][cj * 4 + 3]};
         const bool full = p.vec_c && col0 + 3 < p.N;
-        if (EPI == EPI_BIAS || EPI == EPI_BIAS_RELU) {
+        float lo[4] = {0.f, 0.f, 0.f, 0.f};
+        if (EPI == EPI_BIAS || EPI == EPI_BIAS_RELU || EPI == EPI_BIAS_RELU_SPLIT) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if (col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
-            if (EPI == EPI_BIAS_RELU) v[j] = fmaxf(v[j], 0.f);
+            if (EPI != EPI_BIAS) v[j] = v[j] > 0.f ? v[j] : 0.f;
+            if (EPI == EPI_BIAS_RELU_SPLIT) tf32_split_pos(v[j], v[j], lo[j]);
           }
         } else if (EPI == EPI_RELU_MASK) {
           if (full) {
@@ -255,10 +260,15 @@ gemm_simt_kernel(const GemmParams p) {
         }
         if (full) {
           *reinterpret_cast<float4*>(C + row * p.ldc + col0) = make_float4(v[0], v[1], v[2], v[3]);
+          if (EPI == EPI_BIAS_RELU_SPLIT)
+            *reinterpret_cast<float4*>(p.C2 + row * p.ldc + col0) = make_float4(lo[0], lo[1], lo[2], lo[3]);
         } else {
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            if (col0 + j < p.N) C[row * p.ldc + col0 + j] = v[j];
+            if (col0 + j < p.N) {
+              C[row * p.ldc + col0 + j] = v[j];
+              if (EPI == EPI_BIAS_RELU_SPLIT) p.C2[row * p.ldc + col0 + j] = lo[j];
+            }
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j)

@@ -90,7 +90,17 @@ head_kernel(const HeadParams p) {
       const float4* src = reinterpret_cast<const float4*>(p.act + r0 * H);
       float4* dst = reinterpret_cast<float4*>(as);
       const int n4 = rows * hv;
-      for (int i = tid; i < n4; i += kHeadThreads) dst[i] = __ldg(src + i);
+      if (p.act_lo) {
+        const float4* slo = reinterpret_cast<const float4*>(p.act_lo + r0 * H);
+        for (int i = tid; i < n4; i += kHeadThreads) {
+          float4 a = __ldg(src + i);
+          const float4 b = __ldg(slo + i);
+          a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+          dst[i] = a;
+        }
+      } else {
+        for (int i = tid; i < n4; i += kHeadThreads) dst[i] = __ldg(src + i);
+      }
     }
     __syncthreads();
 
@@ -203,7 +213,14 @@ head_kernel(const HeadParams p) {
           g = fmaf(d, wreg[j][a], g);
         }
         g = av > 0.f ? g : 0.f;
-        if (p.dX) p.dX[(r0 + r) * H + h] = g;
+        if (p.dX_lo) {
+          float hi, lo;
+          tf32_split(g, hi, lo);
+          p.dX[(r0 + r) * H + h] = hi;
+          p.dX_lo[(r0 + r) * H + h] = lo;
+        } else if (p.dX) {
+          p.dX[(r0 + r) * H + h] = g;
+        }
         dbx[j] += g;
       }
     }
@@ -256,7 +273,9 @@ int head_grid(int64_t M, int H) {
 int head_launch(HeadParams p, int grid, cudaStream_t s) {
   SPO_CHECK_ARG(p.H > 0 && p.H <= kHeadThreads * kHeadMaxHJ && p.H % 4 == 0, kErrShape,
                 "head: hidden width must be a multiple of 4 and at most 1024");
-  SPO_CHECK_ARG(aligned16(p.act), kErrAlign, "head: activations must be 16-byte aligned");
+  SPO_CHECK_ARG(aligned16(p.act) && (!p.act_lo || aligned16(p.act_lo)), kErrAlign,
+                "head: activations must be 16-byte aligned");
+  SPO_CHECK_ARG(!p.dX_lo || p.dX, kErrArg, "head: dX_lo needs dX");
   SPO_CHECK_ARG(p.A == 1 || p.A == 9, kErrUnsupported, "head: output width must be 1 or 9");
   SPO_CHECK_ARG(p.mode == kHeadCritic ? p.target != nullptr : p.q != nullptr, kErrArg,
                 "head: missing loss inputs");

@@ -22,6 +22,7 @@ enum HeadMode : int { kHeadActor = 0, kHeadCritic = 1 };
 
 struct HeadParams {
   const float* act;        // [M x H] post-ReLU input of the last Linear layer
+  const float* act_lo;     // optional: lo half when act is stored as a TF32 hi/lo pair
   const float* W;          // [H x A]
   const float* b;          // [A]
   int64_t M;
@@ -39,6 +40,7 @@ struct HeadParams {
   float* out_pi;           // optional [M x A]: pi (actor)
   float* dz_out;           // optional [M x A]: dL/dz
   float* dX;               // optional [M x H]: (dz W^T) * [act > 0]
+  float* dX_lo;            // optional: write dX as a TF32 hi/lo pair (dX = hi)
   float* dW_part;          // [grid][H x A]
   float* db_part;          // [grid][A]
   float* dbx_part;         // optional [grid][H]: column sums of dX

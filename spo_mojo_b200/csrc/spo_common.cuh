@@ -73,4 +73,31 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// TF32 hi/lo split of an fp32 value (the operand format of the 3xTF32 tensor-core GEMM).
+// Round-to-nearest (ties away) conversion to TF32: the fp32 bit pattern of the nearest
+// value with 10 mantissa bits.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Both halves are rounded to nearest and are exact TF32 values, so the tensor core sees
+// them unchanged: hi = rna(v), lo = rna(v - hi) (v - hi is exact in fp32). The part
+// dropped, v - hi - lo, is below 2^-22 |v| and unbiased.
+__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
+  hi = tf32_rna(v);
+  lo = tf32_rna(v - hi);
+}
+
+// Split of a ReLU output: a positive value never maps to hi == 0 (tiny subnormals keep
+// their full value in hi), so the mask of the layer below can be read from hi alone.
+__device__ __forceinline__ void tf32_split_pos(float v, float& hi, float& lo) {
+  tf32_split(v, hi, lo);
+  if (hi == 0.f && v > 0.f) {
+    hi = v;
+    lo = 0.f;
+  }
+}
+
 }  // namespace spo

@@ -38,7 +38,14 @@ constexpr int kEpiThreads = 128;
 constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
 constexpr uint32_t B_TILE = BN * BK * 4;                 // 16 KB
 constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 64 KB
-constexpr int SEG = 8;                                   // k-blocks per TMEM accumulation
+// The tensor core's accumulation into TMEM is not exact fp32: its error grows with the
+// number of MMAs summed into one accumulator. Folding every 2 k-blocks (64 reduction
+// elements) keeps learner outputs near 1e-6 relative; 8 k-blocks measured 3-5e-6, enough
+// to flip ReLU decisions of activations within that distance of zero.
+#ifndef SPO_TC_SEG
+#define SPO_TC_SEG 2
+#endif
+constexpr int SEG = SPO_TC_SEG;                          // k-blocks per TMEM accumulation
 constexpr uint32_t RS_COL = 2 * BN;                      // fp32 running sum after the two accumulators
 constexpr uint32_t TMEM_COLS = 512;                      // 2 accumulators + running sum, power of 2
 constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
@@ -517,6 +524,11 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
   }
 }
 
+__global__ void combine_tf32_kernel(float* __restrict__ hi, const float* __restrict__ lo, int64_t n) {
+  const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gs) hi[i] += lo[i];
+}
+
 __global__ void split_weights_kernel(const float* __restrict__ w, int64_t K, int64_t N,
                                      float* __restrict__ wt_hi, float* __restrict__ wt_lo,
                                      float* __restrict__ w_hi, float* __restrict__ w_lo) {
@@ -677,6 +689,14 @@ int split_tf32_launch(const float* x, float* hi, float* lo, int64_t n, bool keep
   if (n <= 0) return kOk;
   const int grid = (int)std::min<int64_t>(ceil_div(n, 256), 8LL * sm_count());
   split_tf32_kernel<<<grid, 256, 0, s>>>(x, hi, lo, n, keep_positive ? 1 : 0);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
+
+int combine_tf32_launch(float* hi, const float* lo, int64_t n, cudaStream_t s) {
+  if (n <= 0) return kOk;
+  const int grid = (int)std::min<int64_t>(ceil_div(n, 256), 8LL * sm_count());
+  combine_tf32_kernel<<<grid, 256, 0, s>>>(hi, lo, n);
   SPO_LAUNCH_CHECK();
   return kOk;
 }

@@ -1,13 +1,16 @@
 // Tensor-core (tcgen05, sm_100a) GEMM of the learner's hidden layers, fp32-accurate
 // through the 3xTF32 split, with the learner epilogues fused.
 //
-// Every fp32 operand x is held as a pair (hi, lo): hi = x with its 13 low mantissa
-// bits cleared (exactly representable in TF32), lo = x - hi (exact in fp32). Then
+// Every fp32 operand x is held as a pair of exact TF32 values (hi, lo):
+// hi = rna_tf32(x), lo = rna_tf32(x - hi), so x - hi - lo is below 2^-22 |x| and
+// unbiased. Then
 //   x . y ~= lo_x hi_y + hi_x lo_y + hi_x hi_y
-// (the dropped lo_x lo_y term is ~2^-22 relative), accumulated in fp32 in tensor
+// (the dropped lo_x lo_y term is ~2^-24 relative), accumulated in fp32 in tensor
 // memory: the published error-compensated "3xTF32" method (the scheme CUTLASS calls
 // 3xTF32; Ootomo & Yokota 2022). Products of hi/lo halves are exact in the tensor core,
-// so the result carries fp32-level error instead of TF32's 2^-11.
+// so the result carries near-fp32 error instead of TF32's 2^-11. The accumulator is
+// folded into an fp32 running sum every SPO_TC_SEG k-blocks to bound the error of the
+// tensor memory accumulation.
 #pragma once
 
 #include "spo_common.cuh"
@@ -51,23 +54,10 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s);
 // (so hi > 0 <=> x > 0, the ReLU mask test).
 int split_tf32_launch(const float* x, float* hi, float* lo, int64_t n, bool keep_positive,
                       cudaStream_t s);
+// hi[i] += lo[i] (back to plain fp32, in place).
+int combine_tf32_launch(float* hi, const float* lo, int64_t n, cudaStream_t s);
 // W [K x N] -> Wt_hi/Wt_lo [N x K] (transposed) and W_hi/W_lo [K x N].
 int split_weights_launch(const float* w, int64_t K, int64_t N, float* wt_hi, float* wt_lo,
                          float* w_hi, float* w_lo, cudaStream_t s);
-
-__device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
-  hi = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
-  lo = v - hi;
-}
-
-// Split of a ReLU output: a positive value never maps to hi == 0 (tiny subnormals keep
-// their full value in hi), so the mask of the layer below can be read from hi alone.
-__device__ __forceinline__ void tf32_split_pos(float v, float& hi, float& lo) {
-  tf32_split(v, hi, lo);
-  if (hi == 0.f && v > 0.f) {
-    hi = v;
-    lo = 0.f;
-  }
-}
 
 }  // namespace spo

@@ -70,7 +70,7 @@ class LearnerDesc(ctypes.Structure):
                 ("lr_actor", ctypes.c_float), ("lr_critic", ctypes.c_float),
                 ("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("adam_eps", ctypes.c_float),
                 ("max_grad_norm", ctypes.c_float), ("kl_eps", ctypes.c_float),
-                ("use_kl", ctypes.c_int32), ("dual", ctypes.c_int32)]
+                ("use_kl", ctypes.c_int32), ("dual", ctypes.c_int32), ("engine", ctypes.c_int32)]
 
 
 class LearnerLayout(ctypes.Structure):
@@ -145,6 +145,8 @@ SIGNATURES = {
     "spo_learner_backward": (INT, [P, P, ctypes.POINTER(Batch), F, ctypes.POINTER(TrainState)]),
     "spo_learner_apply": (INT, [P, P, ctypes.POINTER(TrainState)]),
     "spo_learner_step": (INT, [P, P, ctypes.POINTER(Batch), ctypes.POINTER(TrainState)]),
+    "spo_learner_status": (INT, [P, ctypes.POINTER(I32)]),
+    "spo_learner_cache": (INT, [P, I32, I32, ctypes.POINTER(P), ctypes.POINTER(P)]),
     "spo_learner_forward": (INT, [P, P, I32, P, P, P, I64, P, P]),
     "spo_comm_get_unique_id": (INT, [P]),
     "spo_comm_init": (INT, [ctypes.POINTER(P), P, I32, I32]),

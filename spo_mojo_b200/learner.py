@@ -19,10 +19,24 @@ from . import ffi
 from .workloads import NetSpec
 
 
+class _DeviceArray:
+    """__cuda_array_interface__ wrapper of n float32 values of library-owned device memory."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 2, "strides": None}
+
+
+def _device_view(ptr, n, device):
+    """A float32 tensor aliasing n floats of device memory owned by the library."""
+    return torch.as_tensor(_DeviceArray(ptr, n), device=device)
+
+
 class Learner:
     def __init__(self, actor_dims=None, critic_dims=None, max_rows=1, lr_actor=3e-4,
                  lr_critic=3e-4, beta1=0.9, beta2=0.999, adam_eps=1e-8,
-                 max_grad_norm=math.inf, kl_eps=0.01, use_kl=True, dual=True, device=0):
+                 max_grad_norm=math.inf, kl_eps=0.01, use_kl=True, dual=True, device=0,
+                 engine="tensor"):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         d = ffi.LearnerDesc()
         d.actor = ffi.MlpDesc.of(actor_dims)
@@ -34,6 +48,9 @@ class Learner:
         d.kl_eps = kl_eps
         d.use_kl = 1 if (use_kl and actor_dims is not None) else 0
         d.dual = 1 if (dual and d.use_kl) else 0
+        if engine not in ("tensor", "cuda"):
+            raise ValueError("engine must be 'tensor' (tcgen05 3xTF32 where shapes allow) or 'cuda'")
+        d.engine = 0 if engine == "tensor" else 1
         self.desc = d
         self.actor_dims = tuple(actor_dims) if actor_dims is not None else None
         self.critic_dims = tuple(critic_dims) if critic_dims is not None else None
@@ -116,6 +133,28 @@ class Learner:
     def stats(self):
         s = self.stats_tensor().tolist()
         return {k: s[v] for k, v in ffi.STAT.items()}
+
+    def activations(self, which, rows):
+        """Post-ReLU activations of the last forward, one [rows x d] tensor per hidden
+        layer (a copy; hi + lo with the tensor-core engine)."""
+        dims = self.actor_dims if which == "actor" else self.critic_dims
+        out = []
+        for layer in range(len(dims) - 2):
+            hi, lo = ctypes.c_void_p(), ctypes.c_void_p()
+            ffi.call("spo_learner_cache", self._h, 0 if which == "actor" else 1, layer,
+                     ctypes.byref(hi), ctypes.byref(lo))
+            n = rows * dims[layer + 1]
+            t = _device_view(hi.value, n, self.device).clone()
+            if lo.value:
+                t += _device_view(lo.value, n, self.device)
+            out.append(t.view(rows, dims[layer + 1]))
+        return out
+
+    def device_status(self):
+        """0 when every bounded wait of the tensor-core kernels completed (synchronises)."""
+        v = ctypes.c_int32()
+        ffi.call("spo_learner_status", self._h, ctypes.byref(v))
+        return v.value
 
     def report_dict(self):
         r = self.report.tolist()

@@ -18,6 +18,7 @@ from spo_mojo_b200.workloads import WORKLOADS, make_batch, init_params, Workload
 pytestmark = pytest.mark.gpu
 
 LOSS_RTOL = 1e-5
+FWD_RTOL = 1e-5
 GRAD_RTOL = 1e-4
 PARAM_RTOL, PARAM_ATOL = 1e-4, 1e-6
 
@@ -62,10 +63,10 @@ def oracle_run(wl, params, batch, steps=1, max_norm=None):
     return first, nets, la
 
 
-def run_learner(wl, params, batch_dev, steps=1, max_norm=None, rows=None):
+def run_learner(wl, params, batch_dev, steps=1, max_norm=None, rows=None, engine="tensor"):
     from spo_mojo_b200.learner import Learner
     kw = {} if max_norm is None else {"max_grad_norm": max_norm}
-    L = Learner.for_workload(wl, max_rows=rows or batch_dev["obs"].shape[0], **kw)
+    L = Learner.for_workload(wl, max_rows=rows or batch_dev["obs"].shape[0], engine=engine, **kw)
     L.load(actor=params.get("actor"), critic=params.get("critic"), log_alpha=wl.log_alpha)
     grads0 = stats0 = rep0 = None
     for i in range(steps):
@@ -75,6 +76,7 @@ def run_learner(wl, params, batch_dev, steps=1, max_norm=None, rows=None):
             stats0 = L.stats()
             rep0 = L.report_dict()
     torch.cuda.synchronize()
+    assert L.device_status() == 0, "a bounded wait of a tensor-core kernel gave up"
     return L, grads0, stats0, rep0
 
 
@@ -83,7 +85,12 @@ def rel_of_max(got, want):
     return float(np.max(np.abs(np.asarray(got, np.float64) - want))) / max(float(np.max(np.abs(want))), 1e-30)
 
 
-def check_against_oracle(wl, L, grads0, stats0, rep0, ora, nets, la):
+def check_against_oracle(wl, L, grads0, stats0, rep0, ora, nets, la, params, batch):
+    """Losses vs the oracle; hidden activations within FWD_RTOL of max; ReLU decisions
+    that differ from float64 (activations within fp32 rounding of zero) at most
+    max(2, 1e-5 of the activations); gradients vs the oracle's backward taken through
+    this library's ReLU decisions (the same branch of the piecewise-linear network);
+    post-Adam parameters as check_adam describes."""
     # losses
     if wl.actor is not None:
         al = ora["actor"]["loss"]
@@ -95,33 +102,73 @@ def check_against_oracle(wl, L, grads0, stats0, rep0, ora, nets, la):
     if wl.critic is not None:
         cl = ora["critic"]["loss"]
         assert abs(stats0["critic_loss"] - cl) <= LOSS_RTOL * abs(cl)
-    # gradients, per tensor
+    # forward activations, ReLU decisions, then gradients per tensor
+    x = batch["obs"]
+    rows = x.shape[0]
     for which in ("actor", "critic"):
         if which not in ora:
             continue
-        for i, ((gw, gb), (ow, ob)) in enumerate(zip(L.tensors(which, grads0), ora[which]["grads"])):
+        acts_o, out_o = O.mlp_forward(params[which], x)
+        ours = [a.cpu().numpy() for a in L.activations(which, rows)]
+        flips = 0
+        for i, (a_g, a_o) in enumerate(zip(ours, acts_o)):
+            assert rel_of_max(a_g, a_o) <= FWD_RTOL, f"{which} activation {i + 1}"
+            flips += int(((a_g > 0) != (a_o > 0)).sum())
+        assert flips <= max(2, 1e-5 * sum(a.size for a in acts_o)), f"{which}: {flips} ReLU flips"
+        if which == "actor":
+            dout = ora["actor"]["loss"]["dz"]
+        else:
+            dout = O.value_loss(out_o, batch["target"], 1.0 / rows)["dv"]
+        og = O.mlp_backward(params[which], x, acts_o, dout, masks=[a > 0 for a in ours])
+        for i, ((gw, gb), (ow, ob)) in enumerate(zip(L.tensors(which, grads0), og)):
             assert rel_of_max(gw.cpu().numpy(), ow) <= GRAD_RTOL, f"{which} dW{i + 1}"
             assert rel_of_max(gb.cpu().numpy(), ob) <= GRAD_RTOL, f"{which} db{i + 1}"
-        # parameters after Adam
-        for i, ((pw, pb), (ow, ob)) in enumerate(zip(L.tensors(which), nets[which]["params"])):
-            np.testing.assert_allclose(pw.cpu().numpy(), ow, rtol=PARAM_RTOL, atol=PARAM_ATOL,
-                                       err_msg=f"{which} W{i + 1} after Adam")
-            np.testing.assert_allclose(pb.cpu().numpy(), ob, rtol=PARAM_RTOL, atol=PARAM_ATOL,
-                                       err_msg=f"{which} b{i + 1} after Adam")
+        clip_o = O.global_clip_scale(O.global_norm([t for pair in og for t in pair]), wl.max_grad_norm)
+        want = [(O.adam_step(w, gw_, np.zeros_like(gw_), np.zeros_like(gw_), 1, wl.lr, wl.beta1,
+                             wl.beta2, wl.adam_eps, clip_o)[0],
+                 O.adam_step(b, gb_, np.zeros_like(gb_), np.zeros_like(gb_), 1, wl.lr, wl.beta1,
+                             wl.beta2, wl.adam_eps, clip_o)[0])
+                for (w, b), (gw_, gb_) in zip(params[which], og)]
+        check_adam(wl, L, which, grads0, og, want, params[which], rep0[f"clip_{which}"])
     if wl.actor is not None and wl.dual:
         want = ora["log_alpha"]["grad"]
         assert abs(rep0["dlog_alpha"] - want) <= 1e-4 * abs(want) + 1e-7
         assert abs(float(L.log_alpha) - la) <= PARAM_RTOL * abs(la) + PARAM_ATOL
 
 
+def check_adam(wl, L, which, grads_gpu, grads_ora, params_ora, p0, clip):
+    """Post-Adam parameters, rel 1e-4 / abs 1e-6, checked two ways.
+
+    Adam's first step moves a parameter by lr * g / (|g| + eps): for a gradient within
+    the gradient tolerance of zero its sign, hence the update, is not determined by the
+    fp32 inputs at all. So (1) the update is checked exactly as the optimiser defines it,
+    by applying the oracle's Adam (float64) to this library's own gradients, on every
+    element; (2) against the full oracle on every element whose gradient is clear of the
+    gradient tolerance (|g| > 10 * GRAD_RTOL * max|g| of its tensor).
+    """
+    for i, ((pw, pb), (gw, gb), (ogw, ogb), (ow, ob), (w0, b0)) in enumerate(
+            zip(L.tensors(which), L.tensors(which, grads_gpu), grads_ora, params_ora, p0)):
+        for got, g_gpu, g_or, want, start, nm in ((pw, gw, ogw, ow, w0, "W"), (pb, gb, ogb, ob, b0, "b")):
+            got = got.cpu().numpy()
+            g_gpu = g_gpu.cpu().numpy().astype(np.float64)
+            mine, _, _ = O.adam_step(start, g_gpu, np.zeros_like(g_gpu), np.zeros_like(g_gpu), 1,
+                                     wl.lr, wl.beta1, wl.beta2, wl.adam_eps, clip)
+            np.testing.assert_allclose(got, mine, rtol=PARAM_RTOL, atol=PARAM_ATOL,
+                                       err_msg=f"{which} {nm}{i + 1}: Adam on our gradients")
+            clear = np.abs(g_or) > 10 * GRAD_RTOL * max(np.max(np.abs(g_or)), 1e-30)
+            np.testing.assert_allclose(got[clear], want[clear], rtol=PARAM_RTOL, atol=PARAM_ATOL,
+                                       err_msg=f"{which} {nm}{i + 1}: oracle Adam")
+
+
+@pytest.mark.parametrize("engine", ["tensor", "cuda"])
 @pytest.mark.parametrize("name,rows", [("c0", 256), ("c1", 4096), ("c2", 4096), ("c3", 2048), ("c4", 1024)])
-def test_workload_step_matches_oracle(name, rows):
+def test_workload_step_matches_oracle(name, rows, engine):
     wl = WORKLOADS[name]
     params = init_params(wl, seed=0)
     batch = make_batch(wl, rows, seed=1)
-    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch))
+    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch), engine=engine)
     ora, nets, la = oracle_run(wl, params, batch)
-    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la, params, batch)
 
 
 def test_c2_full_batch_matches_oracle():
@@ -131,20 +178,59 @@ def test_c2_full_batch_matches_oracle():
     batch = make_batch(wl, wl.batch, seed=2)
     L, g0, s0, r0 = run_learner(wl, params, to_dev(batch))
     ora, nets, la = oracle_run(wl, params, batch)
-    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la, params, batch)
 
 
-def test_three_steps_bias_correction():
+@pytest.mark.parametrize("engine", ["tensor", "cuda"])
+def test_three_steps_bias_correction(engine):
+    """Three consecutive steps (Adam bias corrections 1/(1-b^t), t = 1, 2, 3, from the
+    device step counter): each step's loss matches the float64 oracle run over the same
+    three steps, and the parameters match the oracle's Adam applied step by step to this
+    library's own gradients (moments carried across steps)."""
+    from spo_mojo_b200.learner import Learner
     wl = WORKLOADS["c0"]
     params = init_params(wl, seed=3)
     batch = make_batch(wl, 256, seed=4)
-    L, g0, s0, r0 = run_learner(wl, params, to_dev(batch), steps=3)
-    ora, nets, la = oracle_run(wl, params, batch, steps=3)
+    dev = to_dev(batch)
+    L = Learner.for_workload(wl, max_rows=256, engine=engine)
+    L.load(actor=params["actor"], log_alpha=wl.log_alpha)
+    p = [(w.astype(np.float64), b.astype(np.float64)) for w, b in params["actor"]]
+    m = [(np.zeros_like(w), np.zeros_like(b)) for w, b in p]
+    v = [(np.zeros_like(w), np.zeros_like(b)) for w, b in p]
+    la, am, av = wl.log_alpha, 0.0, 0.0
+    hp = dict(lr_actor=wl.lr, lr_critic=wl.lr, b1=wl.beta1, b2=wl.beta2, eps=wl.adam_eps,
+              max_norm=wl.max_grad_norm, kl_eps=wl.kl_eps, dual=True)
+    full = {"params": [(w.astype(np.float64), b.astype(np.float64)) for w, b in params["actor"]],
+            "m": [(np.zeros_like(a), np.zeros_like(b)) for a, b in p],
+            "v": [(np.zeros_like(a), np.zeros_like(b)) for a, b in p]}
+    fla, fam, fav = la, 0.0, 0.0
+    for t in (1, 2, 3):
+        L.backward(dev)
+        L.apply()
+        torch.cuda.synchronize()
+        st = L.stats()
+        hp.update(step=t, alpha_m=fam, alpha_v=fav)
+        out = O.learner_step(batch, actor=full, log_alpha=fla, hp=hp)
+        assert abs(st["actor_loss"] - out["actor"]["loss"]["loss"]) <= LOSS_RTOL * abs(out["actor"]["loss"]["loss"])
+        full = {"params": out["actor"]["new_params"], "m": out["actor"]["new_m"], "v": out["actor"]["new_v"]}
+        fla, fam, fav = out["log_alpha"]["value"], out["log_alpha"]["m"], out["log_alpha"]["v"]
+        # the oracle's Adam on our gradients, moments carried
+        g = [(gw.cpu().numpy().astype(np.float64), gb.cpu().numpy().astype(np.float64))
+             for gw, gb in L.tensors("actor", L.grads)]
+        for i in range(len(p)):
+            pw, mw, vw = O.adam_step(p[i][0], g[i][0], m[i][0], v[i][0], t, wl.lr, wl.beta1, wl.beta2, wl.adam_eps)
+            pb, mb, vb = O.adam_step(p[i][1], g[i][1], m[i][1], v[i][1], t, wl.lr, wl.beta1, wl.beta2, wl.adam_eps)
+            p[i], m[i], v[i] = (pw, pb), (mw, mb), (vw, vb)
+        gla = float(L.grads[L.layout.alpha_index])
+        lap, am, av = O.adam_step(np.array([la]), np.array([gla]), np.array([am]), np.array([av]), t,
+                                  wl.lr, wl.beta1, wl.beta2, wl.adam_eps)
+        la, am, av = float(lap[0]), float(am[0]), float(av[0])
+        for (pw, pb), (ow, ob) in zip(L.tensors("actor"), p):
+            np.testing.assert_allclose(pw.cpu().numpy(), ow, rtol=PARAM_RTOL, atol=PARAM_ATOL)
+            np.testing.assert_allclose(pb.cpu().numpy(), ob, rtol=PARAM_RTOL, atol=PARAM_ATOL)
+        assert abs(float(L.log_alpha) - la) <= PARAM_RTOL * abs(la) + PARAM_ATOL
     assert int(L.step_counter.item()) == 3
-    for (pw, pb), (ow, ob) in zip(L.tensors("actor"), nets["actor"]["params"]):
-        np.testing.assert_allclose(pw.cpu().numpy(), ow, rtol=PARAM_RTOL, atol=PARAM_ATOL)
-        np.testing.assert_allclose(pb.cpu().numpy(), ob, rtol=PARAM_RTOL, atol=PARAM_ATOL)
-    assert abs(float(L.log_alpha) - la) <= PARAM_RTOL * abs(la) + PARAM_ATOL
+    assert L.device_status() == 0
 
 
 def test_global_norm_clip_bites():
@@ -159,7 +245,7 @@ def test_global_norm_clip_bites():
     assert r0["clip_actor"] < 1.0 and r0["clip_critic"] < 1.0
     assert abs(r0["norm_actor"] - ora["actor"]["norm"]) <= 1e-4 * ora["actor"]["norm"]
     assert abs(r0["norm_critic"] - ora["critic"]["norm"]) <= 1e-4 * ora["critic"]["norm"]
-    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la, params, batch)
 
 
 @pytest.mark.parametrize("rows", [1, 3, 129, 1000])
@@ -169,7 +255,7 @@ def test_ragged_row_counts(rows):
     batch = make_batch(wl, rows, seed=8)
     L, g0, s0, r0 = run_learner(wl, params, to_dev(batch), rows=4096)
     ora, nets, la = oracle_run(wl, params, batch)
-    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la, params, batch)
 
 
 def test_degenerate_rows():
@@ -189,7 +275,7 @@ def test_degenerate_rows():
     assert all(math.isfinite(v) for v in s0.values())
     assert torch.isfinite(g0).all()
     ora, nets, la = oracle_run(wl, params, batch)
-    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la)
+    check_against_oracle(wl, L, g0, s0, r0, ora, nets, la, params, batch)
     logits, pi = L.forward("actor", to_dev(batch)["obs"], to_dev(batch)["mask"])
     assert torch.allclose(pi[0], torch.full((9,), 1.0 / 9, device="cuda"))
 
@@ -218,13 +304,64 @@ def test_rows_beyond_capacity_raise():
     assert "max_rows" in str(e.value)
 
 
-def test_deterministic():
+@pytest.mark.parametrize("engine", ["tensor", "cuda"])
+def test_deterministic(engine):
     wl = WORKLOADS["c2"]
     params = init_params(wl, seed=0)
     batch = to_dev(make_batch(wl, 8192, seed=11))
-    _, g1, _, _ = run_learner(wl, params, batch)
-    _, g2, _, _ = run_learner(wl, params, batch)
+    _, g1, _, _ = run_learner(wl, params, batch, engine=engine)
+    _, g2, _, _ = run_learner(wl, params, batch, engine=engine)
     assert torch.equal(g1, g2)
+
+
+@pytest.mark.parametrize("engine", ["tensor", "cuda"])
+def test_c3_full_batch_vs_float64(engine):
+    """c3 at its full 1,048,576 rows against a float64 restatement run on the GPU.
+
+    Forward: every hidden activation within 1e-5 of max, losses within 1e-5 relative.
+    ReLU decisions of activations within fp32 noise of zero can differ from float64
+    (at most 1e-5 of the activations may); the backward is therefore compared with the
+    float64 backward taken through this library's own ReLU decisions, at rel 1e-4 of max.
+    """
+    import fp64_reference as R
+    from spo_mojo_b200.learner import Learner
+    wl = WORKLOADS["c3"]
+    B = wl.batch
+    params = init_params(wl, seed=0)
+    batch = to_dev(make_batch(wl, B, seed=13))
+    L = Learner.for_workload(wl, max_rows=B, engine=engine)
+    L.load(actor=params["actor"], critic=params["critic"])
+    L.backward(batch)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    st = L.stats()
+    x = batch["obs"].double()
+    for which in ("actor", "critic"):
+        p64 = [(torch.from_numpy(w).cuda().double(), torch.from_numpy(b).cuda().double())
+               for w, b in params[which]]
+        acts, out = R.mlp_forward(p64, x)
+        ours = L.activations(which, B)
+        flips = 0
+        for a64, a32 in zip(acts, ours):
+            err = (a32.double() - a64).abs().max() / a64.abs().max()
+            assert float(err) <= 1e-5
+            flips += int(((a32 > 0) != (a64 > 0)).sum())
+        assert flips <= 1e-5 * sum(a.numel() for a in acts)
+        if which == "actor":
+            lo = R.actor_loss(out, batch["mask"].double(), batch["q"].double(),
+                              batch["logits_old"].double(), wl.log_alpha, 1.0 / B)
+            assert abs(st["actor_loss"] - lo["loss"]) <= LOSS_RTOL * abs(lo["loss"])
+            assert abs(st["kl_old"] - lo["kl_old"]) <= LOSS_RTOL * abs(lo["loss"])
+            dout = lo["dz"]
+        else:
+            lo = R.value_loss(out, batch["target"].double(), 1.0 / B)
+            assert abs(st["critic_loss"] - lo["loss"]) <= LOSS_RTOL * abs(lo["loss"])
+            dout = lo["dv"]
+        grads = R.mlp_backward(p64, x, acts, dout, masks=[a > 0 for a in ours])
+        for i, ((gw, gb), (rw, rb)) in enumerate(zip(L.tensors(which, L.grads), grads)):
+            assert rel_of_max(gw.cpu().numpy(), rw.cpu().numpy()) <= GRAD_RTOL, f"{which} dW{i + 1}"
+            assert rel_of_max(gb.cpu().numpy(), rb.cpu().numpy()) <= GRAD_RTOL, f"{which} db{i + 1}"
+        del acts, ours, grads
 
 
 def test_c3_full_batch_additivity_and_forward():
