@@ -105,6 +105,20 @@ SPO_API int spo_linear_bwd(spo_stream_t stream, float* dw, float* db, float* dx,
                    const float* w, const float* dy, const float* relu_src, int64_t m,
                    int64_t k, int64_t n, void* workspace, size_t workspace_bytes);
 
+/* No counterpart in the reference. spo_linear_bwd for callers that cannot allocate
+ * device memory — e.g. a host framework that pre-reserves nearly all of the GPU's memory
+ * for its own pool, so cudaMalloc has nothing left to give — and so cannot provide a
+ * workspace. It allocates nothing: its scratch is one static 8 MiB device array that
+ * every GPU loading this library keeps until the process exits. Limits: k*n + 256*n must
+ * not exceed 2,097,152 floats (larger shapes return SPO_ERR_WORKSPACE; use
+ * spo_linear_bwd). The first call on a device looks the array's address up (once, with
+ * that device current); make that first call before any stream capture. All calls share
+ * the array, so calls whose work overlaps on the GPU (other streams, other threads)
+ * race: serialise them. Nothing in the array needs clearing between calls. */
+SPO_API int spo_linear_bwd_noalloc(spo_stream_t stream, float* dw, float* db, float* dx,
+                                   const float* x, const float* w, const float* dy,
+                                   const float* relu_src, int64_t m, int64_t k, int64_t n);
+
 /* relu networks/mlp.mojo:34-46 and relu_backward_kernel :155-166 (in place). */
 SPO_API int spo_relu(spo_stream_t stream, float* a, int64_t n);
 SPO_API int spo_relu_bwd(spo_stream_t stream, float* grad, const float* act, int64_t n);

@@ -1293,3 +1293,85 @@ int spo_split_tf32(spo_stream_t stream, float* hi, float* lo, const float* x, in
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free variant
+// spo_linear_bwd without a caller workspace, for callers that cannot allocate device
+// memory: a host framework that pre-reserves nearly all of the GPU's memory for its own
+// pool (JAX does by default) leaves cudaMalloc nothing to give, and some embedders forbid
+// allocation outside their arena. Its scratch (split-K partials of dW and the column-sum
+// chunks of db) lives in one file-scope device array, resident on every GPU that loads
+// this library until the process exits.
+namespace {
+
+constexpr int64_t kStaticScratchFloats = 2 * 1024 * 1024;  // 8 MiB per device
+static __device__ __align__(256) float g_static_scratch[kStaticScratchFloats];
+
+std::mutex g_static_mu;
+float* g_static_ptr[64] = {};
+
+// Device address of g_static_scratch on the current device. The host-side name of the
+// array is only a stand-in and must never reach a kernel; the address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+int static_scratch(float** out) {
+  int dev = 0;
+  SPO_CUDA_TRY(cudaGetDevice(&dev));
+  SPO_CHECK_ARG(dev >= 0 && dev < 64, kErrUnsupported, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    SPO_CUDA_TRY(cudaGetSymbolAddress(&p, g_static_scratch));
+    g_static_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_static_ptr[dev];
+  return kOk;
+}
+
+}  // namespace
+
+extern "C" int spo_linear_bwd_noalloc(spo_stream_t stream, float* dw, float* db, float* dx,
+                                      const float* x, const float* w, const float* dy,
+                                      const float* relu_src, int64_t m, int64_t k, int64_t n) {
+  SPO_CHECK_ARG(m >= 0 && k >= 1 && n >= 1, kErrShape, "bad shape");
+  SPO_CHECK_ARG(dw && db && (m == 0 || (x && dy)) && (!dx || w), kErrArg, "null pointer");
+  const int64_t cs_floats = kColsumChunks * n;
+  SPO_CHECK_ARG(k * n + cs_floats <= kStaticScratchFloats, kErrWorkspace,
+                "spo_linear_bwd_noalloc: k*n + 256*n = " + std::to_string(k * n + cs_floats) +
+                    " floats exceeds its static scratch of " + std::to_string(kStaticScratchFloats) +
+                    " floats; use spo_linear_bwd with a workspace");
+  float* scratch = nullptr;
+  int rc = static_scratch(&scratch);
+  if (rc) return rc;
+  float* cs = scratch;                 // [kColsumChunks][n]
+  float* part = scratch + cs_floats;   // [parts][k x n]
+  const int64_t max_parts = (kStaticScratchFloats - cs_floats) / (k * n);
+  cudaStream_t s = S(stream);
+
+  // dW: split-K over rows as spo_linear_bwd does, with the split count capped so that the
+  // partials fit the static array. Every split writes its whole partial tile, so nothing
+  // has to be cleared between calls.
+  DwCfg c = dw_cfg(k, n, m);
+  int parts = c.parts;
+  if (parts > max_parts) {
+    c.k_chunk = std::max<int64_t>(16, align_up(ceil_div(m, max_parts), 16));
+    parts = (int)ceil_div(m, c.k_chunk);
+    c.grid.z = (unsigned)parts;
+  }
+  if (parts > 0) {
+    GemmParams p{};
+    p.A = x; p.B = dy; p.C = part;
+    p.M = k; p.N = n; p.K = m;
+    p.lda = k; p.ldb = n; p.ldc = n;
+    p.k_chunk = c.k_chunk;
+    p.c_split_stride = k * n;
+    rc = gemm_simt_launch(c.tile, OP_COL, OP_ROW, EPI_STORE, p, c.grid, s);
+    if (rc) return rc;
+  }
+  ReduceParams red{};
+  add_seg(red, part, dw, k * n, k * n, parts);
+  rc = reduce_launch(red, s);
+  if (rc) return rc;
+  rc = colsum(s, db, dy, m, n, cs);
+  if (rc) return rc;
+  if (dx) return gemm_dx(s, dx, dy, w, relu_src, m, k, n, nullptr, nullptr);
+  return kOk;
+}

@@ -108,6 +108,7 @@ SIGNATURES = {
     "spo_linear_fwd": (INT, [P, P, P, P, P, I64, I64, I64, I32]),
     "spo_linear_bwd_workspace_size": (SZ, [I64, I64, I64]),
     "spo_linear_bwd": (INT, [P, P, P, P, P, P, P, P, I64, I64, I64, P, SZ]),
+    "spo_linear_bwd_noalloc": (INT, [P, P, P, P, P, P, P, P, I64, I64, I64]),
     "spo_relu": (INT, [P, P, I64]),
     "spo_relu_bwd": (INT, [P, P, P, I64]),
     "spo_mlp_param_layout": (INT, [ctypes.POINTER(MlpDesc), ctypes.POINTER(I64), ctypes.POINTER(I64),
