@@ -35,8 +35,10 @@ def _device_view(ptr, n, device):
 class Learner:
     def __init__(self, actor_dims=None, critic_dims=None, max_rows=1, lr_actor=3e-4,
                  lr_critic=3e-4, beta1=0.9, beta2=0.999, adam_eps=1e-8,
-                 max_grad_norm=math.inf, kl_eps=0.01, use_kl=True, dual=True, device=0,
+                 max_grad_norm=math.inf, kl_eps=0.01, use_kl=True, dual=True, device=None,
                  engine="tensor"):
+        if device is None:                   # the caller's current device (one per rank)
+            device = torch.cuda.current_device()
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         d = ffi.LearnerDesc()
         d.actor = ffi.MlpDesc.of(actor_dims)
@@ -200,7 +202,7 @@ class Learner:
         return out, pi
 
     @classmethod
-    def for_workload(cls, wl, max_rows=None, device=0, **kw):
+    def for_workload(cls, wl, max_rows=None, device=None, **kw):
         return cls(actor_dims=wl.actor.dims if wl.actor else None,
                    critic_dims=wl.critic.dims if wl.critic else None,
                    max_rows=max_rows or wl.batch, lr_actor=wl.lr, lr_critic=wl.lr,
