@@ -21,7 +21,7 @@
 
 #include <nccl.h>
 
-#include "../../include/spo_cuda.h"
+#include "spo_cuda.h"
 #include "gemm_simt.cuh"
 #include "kernels.cuh"
 #include "tc_gemm.cuh"

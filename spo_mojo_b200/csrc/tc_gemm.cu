@@ -1,12 +1,14 @@
 // tcgen05 3xTF32 GEMM (see tc_gemm.cuh) — persistent, warp-specialised, sm_100a.
 //
-// CTA = 6 warps:
+// CTA = 10 warps:
 //   warp 0     TMA producer (one thread): hi/lo tiles of A and B into a STAGES-deep ring
 //   warp 1     TMEM allocator + MMA issuer (one thread): 3 tcgen05.mma per 8-wide k-step
-//              (lo.hi, hi.lo, hi.hi) into a double-buffered fp32 TMEM accumulator
-//   warps 2-5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM lanes
-//              32*(w%4)..+31 = tile rows), fused bias/ReLU/mask/column sums, hi/lo split,
-//              stores to global memory
+//              (lo.hi, hi.lo, hi.hi) into one of NACC fp32 TMEM accumulators
+//   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (= tile rows) and one half
+//              of the tile's columns; it folds each accumulator into an fp32 running sum
+//              held in registers, releases the accumulator as soon as its tcgen05.ld has
+//              completed, and on the unit's last segment applies the fused bias/ReLU/mask/
+//              column sums, hi/lo split and stores to global memory
 // Tiles are 128 x 128 outputs; k-blocks are 32 fp32 (one 128-byte swizzle row). Operand
 // tiles are written by TMA with 128-byte swizzling; K-major operands are read by the
 // UMMA descriptors with SBO = 1024 B (8-row atoms) and a 32-byte start advance per
@@ -33,8 +35,10 @@ constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 32;
 constexpr int STAGES = 3;
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr int EPI_COLS = BN / 2;                         // columns per epilogue warp
 constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
 constexpr uint32_t B_TILE = BN * BK * 4;                 // 16 KB
 constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 64 KB
@@ -46,8 +50,8 @@ constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 64 KB
 #define SPO_TC_SEG 2
 #endif
 constexpr int SEG = SPO_TC_SEG;                          // k-blocks per TMEM accumulation
-constexpr uint32_t RS_COL = 2 * BN;                      // fp32 running sum after the two accumulators
-constexpr uint32_t TMEM_COLS = 512;                      // 2 accumulators + running sum, power of 2
+constexpr int NACC = 4;                                  // TMEM accumulators in flight
+constexpr uint32_t TMEM_COLS = NACC * BN;                // 512: the whole TMEM of the SM
 constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
 constexpr uint64_t kDrainNs = 500000000ull;              // 0.5 s
 constexpr int kMaxColsumN = 1024;
@@ -57,8 +61,8 @@ enum WaitCode : int { kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, k
 struct __align__(64) Ctl {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[NACC];
+  uint64_t tempty[NACC];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -170,40 +174,25 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// tcgen05.ld.16x256b.x8 without its wait: 16 TMEM lanes (rows) x 64 columns. Register
+// r[4g + i] of thread t holds row (t / 4) + 8 (i / 2), column 8 g + 2 (t % 4) + (i % 2),
+// relative to the lane and column of taddr (the layout of an mma accumulator fragment).
+// The registers hold the data only after tmem_wait_tie(r), which waits for this thread's
+// loads and names the registers as its operands so that no use of them is scheduled
+// above the wait.
+__device__ __forceinline__ void tmem_ld16x256_x8(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
-      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-      : "memory");
+__device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
 }
 
 // UMMA shared-memory descriptor (sm100 version bits), 128-byte swizzle layouts.
@@ -218,11 +207,16 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
-__device__ __forceinline__ void store4(float* p, float a, float b, float c, float d) {
-  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+__device__ __forceinline__ void store2(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // ---------------------------------------------------------------- the kernel
+// 10 warps share the SM's four 16K-register files 3/3/2/2: at most 168 registers a thread
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
                const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
@@ -242,9 +236,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       mbar_init(smem_u32(&ctl->full[s]), 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NACC; ++a) {
       mbar_init(smem_u32(&ctl->tfull[a]), 1);
-      mbar_init(smem_u32(&ctl->tempty[a]), kEpiThreads);
+      mbar_init(smem_u32(&ctl->tempty[a]), kEpiWarps);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
@@ -324,8 +318,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     const uint32_t a_sbo = P.a_mn ? 512u : 1024u, b_sbo = P.b_mn ? 512u : 1024u;
     const uint32_t a_lay = P.a_mn ? 1u : 2u, b_lay = P.b_mn ? 1u : 2u;
     // Each unit's k-range is cut into segments of at most SEG k-blocks; every segment
-    // gets a fresh accumulator (ping-pong), which the epilogue folds into its fp32
-    // running sum. Few accumulations per TMEM accumulator keep the sum fp32-accurate.
+    // gets a fresh accumulator (round robin over NACC), which the epilogue folds into its
+    // fp32 running sum. Few accumulations per TMEM accumulator keep the sum fp32-accurate.
     uint32_t it = 0, seg_i = 0;
     bool ok = true;
     for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
@@ -334,8 +328,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       const int64_t kend = min(P.K, kbeg + P.k_chunk);
       const int nkb = (int)((kend - kbeg + BK - 1) / BK);
       for (int kb0 = 0; kb0 < nkb && ok; kb0 += SEG, ++seg_i) {
-        const uint32_t acc = seg_i & 1;
-        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), ((seg_i >> 1) & 1) ^ 1, abort_flag, P.err,
+        const uint32_t acc = seg_i % NACC;
+        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), ((seg_i / NACC) & 1) ^ 1, abort_flag, P.err,
                        kErrWaitTEmpty)) {
           ok = false;
           break;
@@ -373,15 +367,24 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     mbar_drain(smem_u32(&ctl->drain), 0);
   } else if (warp >= 2) {
     // ------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int row_t = q * 32 + lane;
+    // Warp w reads TMEM lanes 32 (w % 4) .. +31 (tile rows) and columns cb .. cb + 63.
+    // Each 16-row half is read in the 16x256b layout: thread t holds, for column group g
+    // (8 columns), rows t/4 and t/4 + 8 at columns 8g + 2(t%4) + {0, 1}. Rows of a store
+    // instruction are then written 32 contiguous bytes each (4 threads x float2): whole
+    // sectors, with no shared-memory staging.
+    const int q = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;        // which EPI_COLS columns of the tile
+    const int cb = half * EPI_COLS;
+    const int tr = lane >> 2, tc = 2 * (lane & 3);
     const bool dx = P.kind == TC_DX || P.kind == TC_DX_F32;
     if (dx)
-      for (int c = lane; c < P.N; c += 32) colacc[q * P.N + c] = 0.f;
+      for (int c = lane; c < P.N; c += 32)
+        if (((c / EPI_COLS) & 1) == half) colacc[q * P.N + c] = 0.f;
     __syncwarp();
     uint32_t seg_i = 0;
     bool ok = true;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    float rs[2 * 32];                        // fp32 running sums: [16-row half][4 g + i]
     for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
       const int64_t split = u / per_split, rem = u % per_split;
       const int64_t m0 = (rem / P.n_tiles) * BM;
@@ -390,104 +393,134 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       const int64_t kend = min(P.K, kbeg + P.k_chunk);
       const int nkb = (int)((kend - kbeg + BK - 1) / BK);
       const int nseg = (nkb + SEG - 1) / SEG;
-      const int64_t row = m0 + row_t;
-      const bool in = row < P.M;
-      for (int sg = 0; sg < nseg; ++sg, ++seg_i) {
-      const uint32_t acc = seg_i & 1;
-      if (!mbar_wait(smem_u32(&ctl->tfull[acc]), (seg_i >> 1) & 1, abort_flag, P.err,
-                     kErrWaitTFull)) {
-        ok = false;
-        break;
+      const int64_t wrow0 = m0 + q * 32;     // first row of this warp
+      if (dx) {
+        // the mask rows this warp reads at the end of the tile: into L2 while the MMAs run
+        const int64_t r = wrow0 + lane;
+        if (r < P.M) prefetch_l2(P.mask + r * P.N + n0 + cb, EPI_COLS * 4);
       }
-      tc_fence_after();
-      const bool first_seg = sg == 0, last_seg = sg == nseg - 1;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem_base + lane_addr + acc * BN + c0, v);
-        if (!first_seg) {
-          float r[32];
-          tmem_ld32(tmem_base + lane_addr + RS_COL + c0, r);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = r[j] + v[j];
+      for (int sg = 0; sg < nseg; ++sg, ++seg_i) {
+        const uint32_t acc = seg_i % NACC;
+        if (!mbar_wait(smem_u32(&ctl->tfull[acc]), (seg_i / NACC) & 1, abort_flag, P.err,
+                       kErrWaitTFull)) {
+          ok = false;
+          break;
         }
-        if (!last_seg) {
-          tmem_st32(tmem_base + lane_addr + RS_COL + c0, v);
-          continue;
-        }
-        const int64_t col0 = n0 + c0;
-        if (P.kind == TC_FWD) {
-          if (in) {
-            float* ph = P.c_hi + row * P.N + col0;
-            float* pl = P.c_lo + row * P.N + col0;
+        tc_fence_after();
+        uint32_t r0[32], r1[32];
+        const uint32_t ta = tmem_base + lane_addr + acc * BN + cb;
+        tmem_ld16x256_x8(ta, r0);
+        tmem_ld16x256_x8(ta + (16u << 16), r1);
+        tmem_wait_tie(r0);
+        tmem_wait_tie(r1);
+        // the accumulator is free for the next segment's MMAs once the loads completed
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ctl->tempty[acc]));
+        if (sg == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 b4 = __ldg(reinterpret_cast<const float4*>(P.bias + col0 + j));
+          for (int j = 0; j < 32; ++j) {
+            rs[j] = __uint_as_float(r0[j]);
+            rs[32 + j] = __uint_as_float(r1[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            rs[j] = rs[j] + __uint_as_float(r0[j]);
+            rs[32 + j] = rs[32 + j] + __uint_as_float(r1[j]);
+          }
+        }
+        if (sg != nseg - 1) continue;
+        float cs[16];                        // column sums (DX): [g][column pair]
+#pragma unroll
+        for (int j = 0; j < 16; ++j) cs[j] = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float* v = rs + 32 * hh;
+          const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
+          const bool ina = ra < P.M, inb = rb < P.M;
+          const int64_t cbase = n0 + cb + tc;
+          if (P.kind == TC_FWD) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const int64_t col = cbase + 8 * g;
+              const float2 b2 = __ldg(reinterpret_cast<const float2*>(P.bias + col));
+              const float x[4] = {v[4 * g] + b2.x, v[4 * g + 1] + b2.y, v[4 * g + 2] + b2.x,
+                                  v[4 * g + 3] + b2.y};
               float h[4], l[4];
-              const float x[4] = {v[j] + b4.x, v[j + 1] + b4.y, v[j + 2] + b4.z, v[j + 3] + b4.w};
 #pragma unroll
               for (int t = 0; t < 4; ++t) tf32_split_pos(x[t] > 0.f ? x[t] : 0.f, h[t], l[t]);
-              store4(ph + j, h[0], h[1], h[2], h[3]);
-              store4(pl + j, l[0], l[1], l[2], l[3]);
+              if (ina) {
+                store2(P.c_hi + ra * P.N + col, h[0], h[1]);
+                store2(P.c_lo + ra * P.N + col, l[0], l[1]);
+              }
+              if (inb) {
+                store2(P.c_hi + rb * P.N + col, h[2], h[3]);
+                store2(P.c_lo + rb * P.N + col, l[2], l[3]);
+              }
             }
-          }
-        } else if (dx) {
-          if (in) {
-            const float* mrow = P.mask + row * P.N + col0;
+          } else if (dx) {
+            float2 mk[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 m4 = *reinterpret_cast<const float4*>(mrow + j);
-              v[j] = m4.x > 0.f ? v[j] : 0.f;
-              v[j + 1] = m4.y > 0.f ? v[j + 1] : 0.f;
-              v[j + 2] = m4.z > 0.f ? v[j + 2] : 0.f;
-              v[j + 3] = m4.w > 0.f ? v[j + 3] : 0.f;
+            for (int g = 0; g < 8; ++g) {
+              const int64_t col = cbase + 8 * g;
+              mk[2 * g] = ina ? __ldg(reinterpret_cast<const float2*>(P.mask + ra * P.N + col))
+                              : make_float2(0.f, 0.f);
+              mk[2 * g + 1] = inb ? __ldg(reinterpret_cast<const float2*>(P.mask + rb * P.N + col))
+                                  : make_float2(0.f, 0.f);
             }
-            if (P.kind == TC_DX) {
-              float* ph = P.c_hi + row * P.N + col0;
-              float* pl = P.c_lo + row * P.N + col0;
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
+            for (int g = 0; g < 8; ++g) {
+              const int64_t col = cbase + 8 * g;
+              v[4 * g] = mk[2 * g].x > 0.f ? v[4 * g] : 0.f;
+              v[4 * g + 1] = mk[2 * g].y > 0.f ? v[4 * g + 1] : 0.f;
+              v[4 * g + 2] = mk[2 * g + 1].x > 0.f ? v[4 * g + 2] : 0.f;
+              v[4 * g + 3] = mk[2 * g + 1].y > 0.f ? v[4 * g + 3] : 0.f;
+              if (P.kind == TC_DX) {
                 float h[4], l[4];
 #pragma unroll
-                for (int t = 0; t < 4; ++t) tf32_split(v[j + t], h[t], l[t]);
-                store4(ph + j, h[0], h[1], h[2], h[3]);
-                store4(pl + j, l[0], l[1], l[2], l[3]);
+                for (int t = 0; t < 4; ++t) tf32_split(v[4 * g + t], h[t], l[t]);
+                if (ina) {
+                  store2(P.c_hi + ra * P.N + col, h[0], h[1]);
+                  store2(P.c_lo + ra * P.N + col, l[0], l[1]);
+                }
+                if (inb) {
+                  store2(P.c_hi + rb * P.N + col, h[2], h[3]);
+                  store2(P.c_lo + rb * P.N + col, l[2], l[3]);
+                }
+              } else {
+                if (ina) store2(P.c_hi + ra * P.N + col, v[4 * g], v[4 * g + 1]);
+                if (inb) store2(P.c_hi + rb * P.N + col, v[4 * g + 2], v[4 * g + 3]);
               }
-            } else {
-              float* pc = P.c_hi + row * P.N + col0;
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) store4(pc + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+              cs[2 * g] += v[4 * g] + v[4 * g + 2];
+              cs[2 * g + 1] += v[4 * g + 1] + v[4 * g + 3];
             }
-          } else {
+          } else {  // TC_DW
+            float* pc = P.c_part + split * P.M * P.N;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 0.f;
-          }
-          if (P.colsum) {
-            // transpose-reduce: afterwards lane L holds the sum over this warp's 32 rows
-            // of column col0 + L
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) {
-              const bool upper = (lane & o) != 0;
-#pragma unroll
-              for (int i = 0; i < o; ++i) {
-                const float send = upper ? v[i] : v[i + o];
-                const float keep = upper ? v[i + o] : v[i];
-                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-              }
+            for (int g = 0; g < 8; ++g) {
+              const int64_t col = cbase + 8 * g;
+              if (ina) store2(pc + ra * P.N + col, v[4 * g], v[4 * g + 1]);
+              if (inb) store2(pc + rb * P.N + col, v[4 * g + 2], v[4 * g + 3]);
             }
-            colacc[q * P.N + col0 + lane] += v[0];
-          }
-        } else {  // TC_DW
-          if (in) {
-            float* pc = P.c_part + split * P.M * P.N + row * P.N + col0;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) store4(pc + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
           }
         }
-      }
-      if (!last_seg) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-      tc_fence_before();
-      mbar_arrive(smem_u32(&ctl->tempty[acc]));
+        if (dx && P.colsum) {
+          // sum over the 8 threads sharing t % 4 (the warp's 32 rows); lanes 0-3 then
+          // hold columns n0 + cb + 8 g + 2 lane + {0, 1}
+#pragma unroll
+          for (int o = 4; o <= 16; o <<= 1)
+#pragma unroll
+            for (int j = 0; j < 16; ++j) cs[j] += __shfl_xor_sync(0xffffffffu, cs[j], o);
+          if (lane < 4) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              float* ca = colacc + q * P.N + n0 + cb + 8 * g + tc;
+              ca[0] += cs[2 * g];
+              ca[1] += cs[2 * g + 1];
+            }
+          }
+        }
       }
     }
     if (dx && P.colsum) {
