@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SPO_ABI_VERSION 1
+#define SPO_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define SPO_API __attribute__((visibility("default")))
@@ -238,7 +238,10 @@ SPO_API int spo_truncated_gae(spo_stream_t stream, float* adv, float* targets, c
  * Shapes: n % 128 == 0; FWD/DX: k % 32 == 0, n <= 1024 for DX; DW: m % 128 == 0.
  * colsum receives [grid][n] partials (grid from spo_tc_gemm_shape). All pointers
  * 16-byte aligned. err (optional) receives a nonzero code if a bounded wait of the
- * kernel gave up (the kernel then returns without hanging). */
+ * kernel gave up (the kernel then returns without hanging).
+ * ReLU masks packed one bit per element (row-major [m x n/32] 32-bit words, bit j of
+ * word w = column 32 w + j; 8-byte aligned): SPO_TC_FWD writes c_bits (bit = output > 0)
+ * when it is set; SPO_TC_DX* read mask_bits instead of mask when it is set. */
 #define SPO_TC_FWD 0
 #define SPO_TC_DX 1
 #define SPO_TC_DX_F32 2
@@ -257,6 +260,8 @@ typedef struct spo_tc_gemm_desc {
   float* c_part;
   float* colsum;
   int32_t* err;
+  const uint32_t* mask_bits;
+  uint32_t* c_bits;
 } spo_tc_gemm_desc;
 SPO_API int spo_tc_gemm_shape(const spo_tc_gemm_desc* desc, int32_t* grid, int32_t* splits);
 SPO_API int spo_tc_gemm(spo_stream_t stream, const spo_tc_gemm_desc* desc);

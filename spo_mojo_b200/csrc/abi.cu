@@ -234,6 +234,7 @@ struct NetPlan {
   // workspace carve-outs
   float* acts[SPO_MAX_LAYERS] = {};     // a_l, l = 0..L-2: [rows x d_{l+1}] (hi in TC mode)
   float* acts_lo[SPO_MAX_LAYERS] = {};  // TC mode: lo halves
+  uint32_t* acts_bits[SPO_MAX_LAYERS] = {};  // TC mode, 1 <= l <= L-3: a_l > 0 packed [rows x d_{l+1}/32]
   float* dz[2] = {};                    // ping-pong [rows x max_hidden] (hi in TC mode)
   float* dz_lo[2] = {};                 // TC mode
   float* dz0 = nullptr;                 // TC mode: [rows x d_1] fp32
@@ -304,6 +305,8 @@ void carve_net(NetPlan& n, Carve& c, int64_t rows) {
   for (int l = 0; l + 1 < L; ++l) {
     n.acts[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
     if (n.tc) n.acts_lo[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
+    // packed for the dX GEMM of layer l + 1 (the last hidden layer's mask is read by the head)
+    if (n.tc && l >= 1 && l + 2 < L) n.acts_bits[l] = c.take<uint32_t>((size_t)rows * (d.dims[l + 1] / 32));
   }
   for (int i = 0; i < 2; ++i) {
     n.dz[i] = c.take<float>((size_t)rows * n.max_hidden);
@@ -459,6 +462,7 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, co
     a.bias = params + n.b_off[l];
     a.c_hi = n.acts[l];
     a.c_lo = n.acts_lo[l];
+    a.c_bits = n.acts_bits[l];
     a.err = err;
     rc = tc_gemm_launch(a, s);
     if (rc) return rc;
@@ -511,6 +515,7 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, const
       x.N = kin;
       x.K = nout;
       x.mask = n.acts[l - 1];
+      x.mask_bits = n.acts_bits[l - 1];  // packed by the forward GEMM of layer l - 1 >= 1
       x.c_hi = last ? n.dz0 : n.dz[cur ^ 1];
       x.c_lo = last ? nullptr : n.dz_lo[cur ^ 1];
       x.colsum = n.db_part[l - 1];
@@ -1260,6 +1265,7 @@ static int tc_args_of(const spo_tc_gemm_desc* d, TcGemmArgs* a) {
   a->bias = d->bias; a->mask = d->mask;
   a->c_hi = d->c_hi; a->c_lo = d->c_lo; a->c_part = d->c_part; a->colsum = d->colsum;
   a->err = d->err;
+  a->mask_bits = d->mask_bits; a->c_bits = d->c_bits;
   if (a->kind == TC_DW) {
     SPO_CHECK_ARG(a->k_chunk >= 32 && a->k_chunk % 32 == 0, kErrArg, "k_chunk must be a multiple of 32");
   }

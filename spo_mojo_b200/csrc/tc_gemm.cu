@@ -24,6 +24,10 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "kernels.cuh"
 #include "tc_gemm.cuh"
 
@@ -81,6 +85,8 @@ struct KParams {
   float* c_part;
   float* colsum;
   int* err;
+  const uint32_t* mask_bits;
+  uint32_t* c_bits;
 };
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -216,7 +222,10 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 }
 
 // ---------------------------------------------------------------- the kernel
-// 10 warps share the SM's four 16K-register files 3/3/2/2: at most 168 registers a thread
+// One instantiation per epilogue (KIND) and dX mask format (BITS: packed bits instead of
+// fp32). 10 warps share the SM's four 16K-register files 3/3/2/2: at most 168 registers a
+// thread.
+template <int KIND, bool BITS>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
                const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
@@ -376,7 +385,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     const int half = (warp - 2) >> 2;        // which EPI_COLS columns of the tile
     const int cb = half * EPI_COLS;
     const int tr = lane >> 2, tc = 2 * (lane & 3);
-    const bool dx = P.kind == TC_DX || P.kind == TC_DX_F32;
+    constexpr bool dx = KIND == TC_DX || KIND == TC_DX_F32;
     if (dx)
       for (int c = lane; c < P.N; c += 32)
         if (((c / EPI_COLS) & 1) == half) colacc[q * P.N + c] = 0.f;
@@ -394,7 +403,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       const int nkb = (int)((kend - kbeg + BK - 1) / BK);
       const int nseg = (nkb + SEG - 1) / SEG;
       const int64_t wrow0 = m0 + q * 32;     // first row of this warp
-      if (dx) {
+      // packed mask words of this thread's 4 rows (16-row half hh, row t/4 + 8 j), loaded
+      // now so that they have arrived by the end of the tile
+      uint2 mw[4] = {};
+      if (dx && BITS) {
+        const int64_t wpr = P.N / 32;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t r = wrow0 + 16 * (k >> 1) + tr + 8 * (k & 1);
+          if (r < P.M) mw[k] = __ldg(reinterpret_cast<const uint2*>(P.mask_bits + r * wpr + (n0 + cb) / 32));
+        }
+      } else if (dx) {
         // the mask rows this warp reads at the end of the tile: into L2 while the MMAs run
         const int64_t r = wrow0 + lane;
         if (r < P.M) prefetch_l2(P.mask + r * P.N + n0 + cb, EPI_COLS * 4);
@@ -407,29 +426,26 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           break;
         }
         tc_fence_after();
-        uint32_t r0[32], r1[32];
         const uint32_t ta = tmem_base + lane_addr + acc * BN + cb;
-        tmem_ld16x256_x8(ta, r0);
-        tmem_ld16x256_x8(ta + (16u << 16), r1);
-        tmem_wait_tie(r0);
-        tmem_wait_tie(r1);
+        // one 16-row half at a time (32 registers in flight)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t r[32];
+          tmem_ld16x256_x8(ta + ((uint32_t)(16 * hh) << 16), r);
+          tmem_wait_tie(r);
+          float* v = rs + 32 * hh;
+          if (sg == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = v[j] + __uint_as_float(r[j]);
+          }
+        }
         // the accumulator is free for the next segment's MMAs once the loads completed
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&ctl->tempty[acc]));
-        if (sg == 0) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            rs[j] = __uint_as_float(r0[j]);
-            rs[32 + j] = __uint_as_float(r1[j]);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            rs[j] = rs[j] + __uint_as_float(r0[j]);
-            rs[32 + j] = rs[32 + j] + __uint_as_float(r1[j]);
-          }
-        }
         if (sg != nseg - 1) continue;
         float cs[16];                        // column sums (DX): [g][column pair]
 #pragma unroll
@@ -440,7 +456,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
           const bool ina = ra < P.M, inb = rb < P.M;
           const int64_t cbase = n0 + cb + tc;
-          if (P.kind == TC_FWD) {
+          if (KIND == TC_FWD) {
+            uint32_t ba0 = 0, ba1 = 0, bb0 = 0, bb1 = 0;  // bits of rows ra, rb: columns 0-31, 32-63
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
               const int64_t col = cbase + 8 * g;
@@ -458,16 +475,52 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
                 store2(P.c_hi + rb * P.N + col, h[2], h[3]);
                 store2(P.c_lo + rb * P.N + col, l[2], l[3]);
               }
+              const uint32_t sh = (8 * g + tc) & 31;
+              const uint32_t pa = (h[0] > 0.f ? 1u : 0u) | (h[1] > 0.f ? 2u : 0u);
+              const uint32_t pb = (h[2] > 0.f ? 1u : 0u) | (h[3] > 0.f ? 2u : 0u);
+              if (g < 4) {
+                ba0 |= pa << sh;
+                bb0 |= pb << sh;
+              } else {
+                ba1 |= pa << sh;
+                bb1 |= pb << sh;
+              }
+            }
+            if (P.c_bits) {
+              // the 4 threads of a row hold disjoint bits: OR them, one thread stores
+#pragma unroll
+              for (int o = 1; o <= 2; o <<= 1) {
+                ba0 |= __shfl_xor_sync(0xffffffffu, ba0, o);
+                ba1 |= __shfl_xor_sync(0xffffffffu, ba1, o);
+                bb0 |= __shfl_xor_sync(0xffffffffu, bb0, o);
+                bb1 |= __shfl_xor_sync(0xffffffffu, bb1, o);
+              }
+              if ((lane & 3) == 0) {
+                const int64_t wpr = P.N / 32, w0 = (n0 + cb) / 32;
+                if (ina) *reinterpret_cast<uint2*>(P.c_bits + ra * wpr + w0) = make_uint2(ba0, ba1);
+                if (inb) *reinterpret_cast<uint2*>(P.c_bits + rb * wpr + w0) = make_uint2(bb0, bb1);
+              }
             }
           } else if (dx) {
             float2 mk[16];
+            if (BITS) {
+              const uint2 wa = mw[2 * hh], wb = mw[2 * hh + 1];
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const int64_t col = cbase + 8 * g;
-              mk[2 * g] = ina ? __ldg(reinterpret_cast<const float2*>(P.mask + ra * P.N + col))
-                              : make_float2(0.f, 0.f);
-              mk[2 * g + 1] = inb ? __ldg(reinterpret_cast<const float2*>(P.mask + rb * P.N + col))
-                                  : make_float2(0.f, 0.f);
+              for (int g = 0; g < 8; ++g) {
+                const uint32_t sh = (8 * g + tc) & 31;
+                const uint32_t a = (g < 4 ? wa.x : wa.y) >> sh, b = (g < 4 ? wb.x : wb.y) >> sh;
+                mk[2 * g] = make_float2((float)(a & 1u), (float)((a >> 1) & 1u));
+                mk[2 * g + 1] = make_float2((float)(b & 1u), (float)((b >> 1) & 1u));
+              }
+            } else {
+#pragma unroll
+              for (int g = 0; g < 8; ++g) {
+                const int64_t col = cbase + 8 * g;
+                mk[2 * g] = ina ? __ldg(reinterpret_cast<const float2*>(P.mask + ra * P.N + col))
+                                : make_float2(0.f, 0.f);
+                mk[2 * g + 1] = inb ? __ldg(reinterpret_cast<const float2*>(P.mask + rb * P.N + col))
+                                    : make_float2(0.f, 0.f);
+              }
             }
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
@@ -476,7 +529,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
               v[4 * g + 1] = mk[2 * g].y > 0.f ? v[4 * g + 1] : 0.f;
               v[4 * g + 2] = mk[2 * g + 1].x > 0.f ? v[4 * g + 2] : 0.f;
               v[4 * g + 3] = mk[2 * g + 1].y > 0.f ? v[4 * g + 3] : 0.f;
-              if (P.kind == TC_DX) {
+              if (KIND == TC_DX) {
                 float h[4], l[4];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) tf32_split(v[4 * g + t], h[t], l[t]);
@@ -669,7 +722,11 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
                   kErrArg, "tc_gemm: null or misaligned output");
   if (a.kind == TC_FWD) SPO_CHECK_ARG(a.bias && aligned16(a.bias), kErrArg, "tc_gemm: bias");
   if (a.kind == TC_DX || a.kind == TC_DX_F32)
-    SPO_CHECK_ARG(a.mask && aligned16(a.mask), kErrArg, "tc_gemm: mask");
+    SPO_CHECK_ARG(a.mask_bits ? reinterpret_cast<uintptr_t>(a.mask_bits) % 8 == 0
+                              : (a.mask && aligned16(a.mask)),
+                  kErrArg, "tc_gemm: mask (16-byte aligned) or mask_bits (8-byte aligned)");
+  if (a.kind == TC_FWD && a.c_bits)
+    SPO_CHECK_ARG(reinterpret_cast<uintptr_t>(a.c_bits) % 8 == 0, kErrArg, "tc_gemm: c_bits alignment");
   const bool mn = a.kind == TC_DW;
   CUtensorMap m_ah, m_al, m_bh, m_bl;
   int rc;
@@ -704,15 +761,32 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.c_part = a.c_part;
   P.colsum = a.colsum;
   P.err = a.err;
+  P.mask_bits = a.kind == TC_DX || a.kind == TC_DX_F32 ? a.mask_bits : nullptr;
+  P.c_bits = a.kind == TC_FWD ? a.c_bits : nullptr;
   const int grid = tc_gemm_grid(a);
   const size_t smem = tc_smem_bytes(a.kind, a.N);
-  static bool attr_set = false;
-  if (!attr_set) {
-    SPO_CUDA_TRY(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)tc_smem_bytes(TC_DX, kMaxColsumN)));
-    attr_set = true;
+  const bool bits = P.mask_bits != nullptr;
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const KParams);
+  switch (a.kind) {
+    case TC_FWD: kern = tc_gemm_kernel<TC_FWD, false>; break;
+    case TC_DX: kern = bits ? tc_gemm_kernel<TC_DX, true> : tc_gemm_kernel<TC_DX, false>; break;
+    case TC_DX_F32: kern = bits ? tc_gemm_kernel<TC_DX_F32, true> : tc_gemm_kernel<TC_DX_F32, false>; break;
+    default: kern = tc_gemm_kernel<TC_DW, false>; break;
   }
-  tc_gemm_kernel<<<grid, kThreads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
+  // the shared-memory opt-in is a per-device attribute of each instantiation
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> opted;
+  int dev = 0;
+  SPO_CUDA_TRY(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!opted.count({dev, (const void*)kern})) {
+      SPO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)tc_smem_bytes(TC_DX, kMaxColsumN)));
+      opted.insert({dev, (const void*)kern});
+    }
+  }
+  kern<<<grid, kThreads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
   SPO_LAUNCH_CHECK();
   return kOk;
 }

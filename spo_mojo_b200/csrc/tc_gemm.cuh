@@ -42,6 +42,10 @@ struct TcGemmArgs {
   float* c_part;           // TC_DW: [splits][M x N]
   float* colsum;           // TC_DX*: [grid][N] column sums (optional)
   int* err;                // device error word (bounded waits), optional
+  // ReLU mask packed one bit per element: row-major [M x N/32] 32-bit words, bit j of
+  // word w of a row = column 32 w + j.
+  const uint32_t* mask_bits;  // TC_DX*: used instead of mask when set (bit = keep)
+  uint32_t* c_bits;           // TC_FWD: optional output, bit = (output > 0)
 };
 
 // Launch configuration queries (host).

@@ -59,7 +59,7 @@ class TcGemmDesc(ctypes.Structure):
                 ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("k_chunk", ctypes.c_int64),
                 ("bias", ctypes.c_void_p), ("mask", ctypes.c_void_p), ("c_hi", ctypes.c_void_p),
                 ("c_lo", ctypes.c_void_p), ("c_part", ctypes.c_void_p), ("colsum", ctypes.c_void_p),
-                ("err", ctypes.c_void_p)]
+                ("err", ctypes.c_void_p), ("mask_bits", ctypes.c_void_p), ("c_bits", ctypes.c_void_p)]
 
 
 TC_FWD, TC_DX, TC_DX_F32, TC_DW = 0, 1, 2, 3

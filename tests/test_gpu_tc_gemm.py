@@ -105,6 +105,65 @@ def test_dx_mask_colsum(M, Kout, Nin, kind):
     assert rel_err(cs.double().sum(0).cpu().numpy(), want.sum(0)) <= 1e-5
 
 
+def pack_mask(m):
+    """[M x N] bool -> [M x N/32] uint32, bit j of word w = column 32 w + j."""
+    return np.packbits(np.asarray(m, bool), axis=1, bitorder="little").view(np.uint32)
+
+
+@pytest.mark.parametrize("M,K,N", [(1000, 256, 256), (4096, 512, 512), (300, 1024, 1024)])
+def test_forward_writes_packed_relu_mask(M, K, N):
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(7 * M + K)
+    x = torch.randn(M, K, device="cuda", generator=g).relu_()
+    w = torch.randn(K, N, device="cuda", generator=g) / K ** 0.5
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+    xh, xl = split(x)
+    wth, wtl = split(w.t().contiguous())
+    yh, yl = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+    bits = torch.full((M + 1, N // 32), -1, dtype=torch.int32, device="cuda")  # + a guard row
+    d = f.TcGemmDesc(kind=f.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wth.data_ptr(),
+                     b_lo=wtl.data_ptr(), m=M, n=N, k=K, bias=b.data_ptr(), c_hi=yh.data_ptr(),
+                     c_lo=yl.data_ptr(), c_bits=bits.data_ptr())
+    run(d)
+    got = bits.cpu().numpy().view(np.uint32)
+    assert np.array_equal(got[:M], pack_mask(yh.cpu().numpy() > 0))
+    assert np.all(got[M] == 0xFFFFFFFF)
+
+
+@pytest.mark.parametrize("M,Kout,Nin", [(1000, 512, 512), (2048, 1024, 512), (129, 128, 256)])
+@pytest.mark.parametrize("kind", ["dx", "dx_f32"])
+def test_dx_packed_mask_equals_float_mask(M, Kout, Nin, kind):
+    """The dX epilogue reading the packed mask gives bit-identical outputs and column sums."""
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(M + 3 * Kout + Nin)
+    dy = torch.randn(M, Kout, device="cuda", generator=g) * 1e-3
+    w = torch.randn(Nin, Kout, device="cuda", generator=g) / Kout ** 0.5
+    act = torch.randn(M, Nin, device="cuda", generator=g).relu_()
+    ah, _ = split(act)
+    bits = torch.from_numpy(pack_mask(ah.cpu().numpy() > 0).view(np.int32)).cuda()
+    dyh, dyl = split(dy)
+    wh, wl = split(w)
+    outs = []
+    for use_bits in (False, True):
+        out_h = torch.full((M, Nin), float("nan"), device="cuda")
+        out_l = torch.full((M, Nin), float("nan"), device="cuda")
+        desc = f.TcGemmDesc(kind=f.TC_DX if kind == "dx" else f.TC_DX_F32, a_hi=dyh.data_ptr(),
+                            a_lo=dyl.data_ptr(), b_hi=wh.data_ptr(), b_lo=wl.data_ptr(), m=M, n=Nin,
+                            k=Kout, mask=None if use_bits else ah.data_ptr(),
+                            mask_bits=bits.data_ptr() if use_bits else None, c_hi=out_h.data_ptr(),
+                            c_lo=out_l.data_ptr() if kind == "dx" else None)
+        grid = ctypes.c_int32()
+        f.call("spo_tc_gemm_shape", ctypes.byref(desc), ctypes.byref(grid), None)
+        cs = torch.full((grid.value, Nin), float("nan"), device="cuda")
+        desc.colsum = cs.data_ptr()
+        run(desc)
+        outs.append((out_h.cpu(), out_l.cpu() if kind == "dx" else None, cs.cpu()))
+    (h0, l0, c0), (h1, l1, c1) = outs
+    assert torch.equal(h0, h1) and torch.equal(c0, c1)
+    if kind == "dx":
+        assert torch.equal(l0, l1)
+
+
 @pytest.mark.parametrize("rows,Kin,N,chunk", [(4096, 512, 512, 1024), (1000, 128, 128, 256),
                                                (65536, 256, 256, 4096), (777, 1024, 1024, 224)])
 def test_dw_split_partials(rows, Kin, N, chunk):
