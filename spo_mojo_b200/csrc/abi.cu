@@ -135,7 +135,8 @@ DwCfg dw_cfg(int64_t k_in, int64_t n_out, int64_t rows) {
 int64_t dw_parts_bound(int64_t k_in, int64_t n_out) {
   // parts <= ceil(target / tiles) with the smaller tile count of the two shapes
   const int64_t tiles = ceil_div(k_in, 128) * ceil_div(n_out, 128);
-  return std::max<int64_t>(1, ceil_div(target_ctas(), tiles));
+  const int64_t simt = std::max<int64_t>(1, ceil_div(target_ctas(), tiles));
+  return dw_skinny_ok(k_in, n_out) ? std::max(simt, dw_skinny_max_parts()) : simt;
 }
 
 int gemm_fwd(cudaStream_t s, float* y, const float* x, const float* w, const float* b,
@@ -168,6 +169,8 @@ int gemm_dx(cudaStream_t s, float* dx, const float* dy, const float* w, const fl
 // dW partials: part[z][k x n] = sum over rows of chunk z of x^T dY.
 int gemm_dw(cudaStream_t s, float* part, const float* x, const float* dy, int64_t rows,
             int64_t k, int64_t n, int* parts) {
+  if (dw_skinny_ok(k, n) && aligned16(dy) && aligned16(part))
+    return dw_skinny_launch(x, dy, rows, k, n, part, parts, s);
   DwCfg c = dw_cfg(k, n, rows);
   if (parts) *parts = c.parts;
   if (c.parts == 0) return kOk;

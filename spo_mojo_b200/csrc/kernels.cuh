@@ -128,6 +128,13 @@ int value_grad_launch(float* dv, const float* v, const float* t, int64_t n, floa
 int relu_launch(float* a, int64_t n, cudaStream_t s);
 int relu_bwd_launch(float* g, const float* act, int64_t n, cudaStream_t s);
 // part[c][n] = sum of rows [c*per, (c+1)*per) of x [rows x n], per = ceil(rows / chunks).
+// dW = x^T dY for inputs at most 32 wide (dw_skinny.cu): per-chunk partials
+// part[chunk][k x n], *parts chunks (at most dw_skinny_max_parts()).
+bool dw_skinny_ok(int64_t k, int64_t n);
+int64_t dw_skinny_max_parts();
+int dw_skinny_launch(const float* x, const float* dy, int64_t rows, int64_t k, int64_t n, float* part,
+                     int* parts, cudaStream_t s);
+
 int colsum_part_launch(const float* x, int64_t rows, int64_t n, int64_t chunks, float* part,
                        cudaStream_t s);
 int gae_launch(float* adv, float* targets, const float* r, const float* discount,
