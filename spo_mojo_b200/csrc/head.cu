@@ -14,10 +14,14 @@
 //   loss_row += alpha * sum_{pi_old > 0} pi_old (log pi_old - log pi)
 //   dz       += alpha * (pi - pi_old) * scale,   alpha = softplus(log_alpha)
 //
-// Work split. A CTA walks row tiles of R rows (grid-stride). For each tile:
-//   1. the post-ReLU activations act[R x H] are staged in shared memory (float4);
-//   2. one warp per row computes z = act W + b (lanes split H, butterfly sum), then
-//      lane 0 evaluates the masked softmax, the loss terms and dz for that row;
+// Work split. A CTA walks row tiles of R rows (grid-stride), two CTAs per SM. For each tile:
+//   1. the activations act[R x H] (and their lo halves) are copied into shared memory
+//      with cp.async (all 16-byte copies in flight at once);
+//   2. one warp per row computes z = act W + b: lane l takes h = l + 32 m, W rows come
+//      from shared memory padded to AP = 12 columns (three conflict-free float4 reads),
+//      and a transpose-reduce leaves z_a in lane a. Lanes 0..A-1 then evaluate the
+//      masked softmax, the loss terms and dz of action a together (shuffle reductions
+//      over the actions), and the lane writes the combined act (hi + lo) back in place;
 //   3. each thread owns fixed columns h of act and, over the R rows, accumulates
 //      dW[h, :] += act[r, h] dz[r, :] and writes dX[r, h] = (dz[r] . W[h, :]) * [act > 0],
 //      accumulating the column sums of dX (the bias gradient of the layer below).
@@ -32,38 +36,66 @@ namespace {
 
 constexpr int kHeadThreads = 256;
 constexpr int kHeadMaxHJ = 4;  // H <= 1024
+constexpr int kNW = kHeadThreads / 32;
+
+template <int A>
+__host__ __device__ constexpr int padded_actions() { return A == 1 ? 1 : (A + 3) & ~3; }
 
 __device__ __forceinline__ float softplus_f(float x) {
   return log1pf(expf(-fabsf(x))) + fmaxf(x, 0.f);
 }
 
-template <int A>
-__global__ void __launch_bounds__(kHeadThreads)
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+// Max / sum over the 16 lanes of each half-warp (lanes 16-31 mirror lanes 0-15).
+__device__ __forceinline__ float half_max(float v) {
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float half_sum(float v) {
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int A, int NJ>
+__global__ void __launch_bounds__(kHeadThreads, 2)
 head_kernel(const HeadParams p) {
+  constexpr int AP = padded_actions<A>();
   extern __shared__ __align__(16) float sm[];
   const int H = p.H;
   const int R = p.rows_per_tile;
-  float* Ws = sm;                          // [H][A]
-  float* as = Ws + ((H * A + 3) & ~3);     // [R][H]
-  float* dzs = as + R * H;                 // [R][A]
-  float* red = dzs + R * A;                // scratch for the final reductions
+  const bool has_lo = p.act_lo != nullptr;
+  float* Ws = sm;                          // [H][AP]
+  float* ahi = Ws + H * AP;                // [R][H] (act; hi + lo after phase 2)
+  float* alo = ahi + R * H;                // [R][H] lo halves
+  float* dzs = alo + (has_lo ? R * H : 0);  // [R][AP]
+  float* red = dzs + R * AP;               // [kNW][AP + kStats]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int NW = kHeadThreads / 32;
 
-  for (int i = tid; i < H * A; i += kHeadThreads) Ws[i] = __ldg(p.W + i);
-  float bias[A];
-#pragma unroll
-  for (int a = 0; a < A; ++a) bias[a] = __ldg(p.b + a);
+  for (int i = tid; i < H * AP; i += kHeadThreads) {
+    const int h = i / AP, a = i % AP;
+    Ws[i] = a < A ? __ldg(p.W + (int64_t)h * A + a) : 0.f;
+  }
+  // phase 2 lane roles: action a of this lane (A == 9: lanes 0-8 and their mirrors 16-24)
+  const int la = lane & 15;
+  const bool lvalid = la < A;
+  const float lbias = A == 1 ? __ldg(p.b) : (lvalid ? __ldg(p.b + la) : 0.f);
   float alpha = p.alpha_host;
   if (p.log_alpha != nullptr) alpha = softplus_f(__ldg(p.log_alpha));
 
   // Thread-owned columns h = tid + 256 j.
-  float wreg[kHeadMaxHJ][A];
-  float dw[kHeadMaxHJ][A];
-  float dbx[kHeadMaxHJ];
+  float wreg[NJ][A];
+  float dw[NJ][A];
+  float dbx[NJ];
 #pragma unroll
-  for (int j = 0; j < kHeadMaxHJ; ++j) {
+  for (int j = 0; j < NJ; ++j) {
     const int h = tid + j * kHeadThreads;
     dbx[j] = 0.f;
 #pragma unroll
@@ -72,145 +104,197 @@ head_kernel(const HeadParams p) {
       dw[j][a] = 0.f;
     }
   }
-  // Per-warp (lane 0) accumulators: db of the last layer and the loss statistics.
-  float dbl[A];
-#pragma unroll
-  for (int a = 0; a < A; ++a) dbl[a] = 0.f;
+  float dbl = 0.f;  // db of action la (A == 9) or of the output (A == 1, lane 0)
   float st[kStats];
 #pragma unroll
   for (int s = 0; s < kStats; ++s) st[s] = 0.f;
 
   const int64_t tiles = (p.M + R - 1) / R;
-  const int hv = H / 4;
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
     const int64_t r0 = t * R;
     const int rows = (int)min((int64_t)R, p.M - r0);
-    __syncthreads();  // previous tile fully consumed
+    __syncthreads();  // previous tile fully consumed (and W staged, first time)
     {
-      const float4* src = reinterpret_cast<const float4*>(p.act + r0 * H);
-      float4* dst = reinterpret_cast<float4*>(as);
-      const int n4 = rows * hv;
-      if (p.act_lo) {
-        const float4* slo = reinterpret_cast<const float4*>(p.act_lo + r0 * H);
-        for (int i = tid; i < n4; i += kHeadThreads) {
-          float4 a = __ldg(src + i);
-          const float4 b = __ldg(slo + i);
-          a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-          dst[i] = a;
-        }
-      } else {
-        for (int i = tid; i < n4; i += kHeadThreads) dst[i] = __ldg(src + i);
+      const int n4 = rows * H / 4;
+      const float* src = p.act + r0 * H;
+      for (int i = tid; i < n4; i += kHeadThreads) cp_async16(ahi + 4 * i, src + 4 * i);
+      if (has_lo) {
+        const float* slo = p.act_lo + r0 * H;
+        for (int i = tid; i < n4; i += kHeadThreads) cp_async16(alo + 4 * i, slo + 4 * i);
       }
+      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
 
     // 2. One warp per row: logits, loss, dz.
-    for (int r = warp; r < rows; r += NW) {
-      float z[A];
-#pragma unroll
-      for (int a = 0; a < A; ++a) z[a] = 0.f;
-      const float* arow = as + r * H;
-      for (int h = lane; h < H; h += 32) {
-        const float av = arow[h];
-#pragma unroll
-        for (int a = 0; a < A; ++a) z[a] = fmaf(av, Ws[h * A + a], z[a]);
-      }
-#pragma unroll
-      for (int a = 0; a < A; ++a) z[a] = warp_sum(z[a]) + bias[a];
-
-      if (lane == 0) {
-        const int64_t row = r0 + r;
-        float dz[A];
-        if (p.mode == kHeadCritic) {
-#pragma unroll
-          for (int a = 0; a < A; ++a) {
-            const float d = z[a] - __ldg(p.target + row * A + a);
-            dz[a] = d * p.scale;
+    for (int r = warp; r < rows; r += kNW) {
+      float* arow = ahi + r * H;
+      const float* lrow = alo + r * H;
+      const int64_t row = r0 + r;
+      if constexpr (A == 1) {
+        float z = 0.f;
+        for (int h = lane; h < H; h += 32) {
+          float av = arow[h];
+          if (has_lo) {
+            av += lrow[h];
+            arow[h] = av;
+          }
+          z = fmaf(av, Ws[h], z);
+        }
+        z = warp_sum(z) + lbias;
+        if (lane == 0) {
+          float dz;
+          if (p.mode == kHeadCritic) {
+            const float d = z - __ldg(p.target + row);
+            dz = d * p.scale;
             st[kStatCriticLoss] += 0.5f * d * d * p.scale;
-            if (p.out_logits) p.out_logits[row * A + a] = z[a];
-          }
-        } else {
-          float mk[A], q[A], zm[A];
-          float mx = kNegInf;
-#pragma unroll
-          for (int a = 0; a < A; ++a) {
-            mk[a] = p.mask ? __ldg(p.mask + row * A + a) : 1.f;
-            q[a] = __ldg(p.q + row * A + a);
-            zm[a] = mk[a] == 0.f ? kNegInf : z[a];
-            mx = fmaxf(mx, zm[a]);
-          }
-          float e[A], s = 0.f;
-#pragma unroll
-          for (int a = 0; a < A; ++a) { e[a] = expf(zm[a] - mx); s += e[a]; }
-          const float inv_s = 1.f / s;
-          const float lse = mx + logf(s);
-          float ce = 0.f, hq = 0.f, pi[A], lp[A];
-#pragma unroll
-          for (int a = 0; a < A; ++a) {
-            pi[a] = e[a] * inv_s;
-            lp[a] = zm[a] - lse;
-            if (q[a] != 0.f) ce -= q[a] * lp[a];
-            if (q[a] > 0.f) hq -= q[a] * logf(q[a]);
-          }
-          float klo = 0.f, po[A];
-          if (p.z_old != nullptr) {
-            float zo[A], mxo = kNegInf;
-#pragma unroll
-            for (int a = 0; a < A; ++a) {
-              zo[a] = mk[a] == 0.f ? kNegInf : __ldg(p.z_old + row * A + a);
-              mxo = fmaxf(mxo, zo[a]);
-            }
-            float so = 0.f;
-#pragma unroll
-            for (int a = 0; a < A; ++a) { po[a] = expf(zo[a] - mxo); so += po[a]; }
-            const float inv_so = 1.f / so, lseo = mxo + logf(so);
-#pragma unroll
-            for (int a = 0; a < A; ++a) {
-              po[a] *= inv_so;
-              if (po[a] > 0.f) klo += po[a] * ((zo[a] - lseo) - lp[a]);
-            }
           } else {
-#pragma unroll
-            for (int a = 0; a < A; ++a) po[a] = 0.f;
+            // one action: pi = 1 where legal, log pi = 0
+            const float mk = p.mask ? __ldg(p.mask + row) : 1.f;
+            const float qv = __ldg(p.q + row);
+            const float zm = mk == 0.f ? kNegInf : z;
+            const float e = expf(zm - zm), pi = e / e, lp = zm - (zm + logf(e));
+            float po = 0.f, klo = 0.f;
+            if (p.z_old != nullptr) {
+              const float zo = mk == 0.f ? kNegInf : __ldg(p.z_old + row);
+              const float eo = expf(zo - zo);
+              po = eo / eo;
+              if (po > 0.f) klo = po * ((zo - (zo + logf(eo))) - lp);
+            }
+            const float ce = qv != 0.f ? -qv * lp : 0.f;
+            const float hq = qv > 0.f ? -qv * logf(qv) : 0.f;
+            dz = mk == 0.f ? 0.f : ((pi - qv) + alpha * (pi - po)) * p.scale;
+            st[kStatActorLoss] += (ce + alpha * klo) * p.scale;
+            st[kStatCE] += ce * p.scale;
+            st[kStatEntropy] += hq * p.scale;
+            st[kStatKLq] += (ce - hq) * p.scale;
+            st[kStatKLold] += klo * p.scale;
+            if (p.out_pi) p.out_pi[row] = pi;
+            z = zm;
           }
+          if (p.out_logits) p.out_logits[row] = z;
+          if (p.dz_out) p.dz_out[row] = dz;
+          dzs[r] = dz;
+          dbl += dz;
+        }
+      } else {
+      float zp[16];
 #pragma unroll
-          for (int a = 0; a < A; ++a)
-            dz[a] = mk[a] == 0.f ? 0.f : ((pi[a] - q[a]) + alpha * (pi[a] - po[a])) * p.scale;
+      for (int a = 0; a < 16; ++a) zp[a] = 0.f;
+      for (int h = lane; h < H; h += 32) {
+        float av = arow[h];
+        if (has_lo) {
+          av += lrow[h];
+          arow[h] = av;
+        }
+        const float4* w4 = reinterpret_cast<const float4*>(Ws + h * AP);
+#pragma unroll
+        for (int c = 0; c < AP / 4; ++c) {
+          const float4 w = w4[c];
+          zp[4 * c] = fmaf(av, w.x, zp[4 * c]);
+          zp[4 * c + 1] = fmaf(av, w.y, zp[4 * c + 1]);
+          zp[4 * c + 2] = fmaf(av, w.z, zp[4 * c + 2]);
+          zp[4 * c + 3] = fmaf(av, w.w, zp[4 * c + 3]);
+        }
+      }
+      // transpose-reduce: lane L ends with the sum of zp[L & 15] over the warp
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; ++i) {
+          const float send = upper ? zp[i] : zp[i + o];
+          const float keep = upper ? zp[i + o] : zp[i];
+          zp[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      const float zv = zp[0] + __shfl_xor_sync(0xffffffffu, zp[0], 16) + lbias;
+
+      float dz = 0.f;
+      if (p.mode == kHeadCritic) {
+        if (lvalid) {
+          const float d = zv - __ldg(p.target + row * A + la);
+          dz = d * p.scale;
+          const float l2 = half_sum(0.5f * d * d * p.scale);
+          if (lane == 0) st[kStatCriticLoss] += l2;
+          if (p.out_logits && lane < A) p.out_logits[row * A + la] = zv;
+        } else {
+          half_sum(0.f);
+        }
+      } else {
+        float mk = 1.f, qv = 0.f;
+        if (lvalid) {
+          mk = p.mask ? __ldg(p.mask + row * A + la) : 1.f;
+          qv = __ldg(p.q + row * A + la);
+        }
+        const float zm = (!lvalid || mk == 0.f) ? kNegInf : zv;
+        const float mx = half_max(zm);
+        const float e = lvalid ? expf(zm - mx) : 0.f;
+        const float s = half_sum(e);
+        const float inv_s = 1.f / s;
+        const float lse = mx + logf(s);
+        const float pi = e * inv_s;
+        const float lp = zm - lse;
+        float po = 0.f, klo_t = 0.f;
+        if (p.z_old != nullptr) {
+          const float zo = (!lvalid || mk == 0.f) ? kNegInf : __ldg(p.z_old + row * A + la);
+          const float mxo = half_max(zo);
+          const float eo = lvalid ? expf(zo - mxo) : 0.f;
+          const float so = half_sum(eo);
+          const float inv_so = 1.f / so, lseo = mxo + logf(so);
+          po = eo * inv_so;
+          if (lvalid && po > 0.f) klo_t = po * ((zo - lseo) - lp);
+        }
+        const float ce = half_sum((lvalid && qv != 0.f) ? -qv * lp : 0.f);
+        const float hq = half_sum((lvalid && qv > 0.f) ? -qv * logf(qv) : 0.f);
+        const float klo = half_sum(klo_t);
+        dz = (!lvalid || mk == 0.f) ? 0.f : ((pi - qv) + alpha * (pi - po)) * p.scale;
+        if (lane == 0) {
           st[kStatActorLoss] += (ce + alpha * klo) * p.scale;
           st[kStatCE] += ce * p.scale;
           st[kStatEntropy] += hq * p.scale;
           st[kStatKLq] += (ce - hq) * p.scale;
           st[kStatKLold] += klo * p.scale;
-          if (p.out_logits)
-#pragma unroll
-            for (int a = 0; a < A; ++a) p.out_logits[row * A + a] = zm[a];
-          if (p.out_pi)
-#pragma unroll
-            for (int a = 0; a < A; ++a) p.out_pi[row * A + a] = pi[a];
         }
-#pragma unroll
-        for (int a = 0; a < A; ++a) {
-          dzs[r * A + a] = dz[a];
-          dbl[a] += dz[a];
-          if (p.dz_out) p.dz_out[row * A + a] = dz[a];
+        if (lane < A) {
+          if (p.out_logits) p.out_logits[row * A + la] = zm;
+          if (p.out_pi) p.out_pi[row * A + la] = pi;
         }
+      }
+      if (lane < A) {
+        if (p.dz_out) p.dz_out[row * A + la] = dz;
+        dbl += dz;
+      }
+      if (lane < AP) dzs[r * AP + lane] = dz;  // dz is 0 on the padding lanes
       }
     }
     __syncthreads();
 
     // 3. Thread-owned columns: dW, dX (ReLU-masked), column sums of dX.
 #pragma unroll
-    for (int j = 0; j < kHeadMaxHJ; ++j) {
+    for (int j = 0; j < NJ; ++j) {
       const int h = tid + j * kHeadThreads;
       if (h >= H) continue;
       for (int r = 0; r < rows; ++r) {
-        const float av = as[r * H + h];
+        const float av = ahi[r * H + h];
+        float d[AP];
+        if constexpr (A == 1) {
+          d[0] = dzs[r];
+        } else {
+#pragma unroll
+          for (int c = 0; c < AP / 4; ++c) {
+            const float4 v = reinterpret_cast<const float4*>(dzs + r * AP)[c];
+            d[4 * c] = v.x;
+            d[4 * c + 1] = v.y;
+            d[4 * c + 2] = v.z;
+            d[4 * c + 3] = v.w;
+          }
+        }
         float g = 0.f;
 #pragma unroll
         for (int a = 0; a < A; ++a) {
-          const float d = dzs[r * A + a];
-          dw[j][a] = fmaf(av, d, dw[j][a]);
-          g = fmaf(d, wreg[j][a], g);
+          dw[j][a] = fmaf(av, d[a], dw[j][a]);
+          g = fmaf(d[a], wreg[j][a], g);
         }
         g = av > 0.f ? g : 0.f;
         if (p.dX_lo) {
@@ -229,7 +313,7 @@ head_kernel(const HeadParams p) {
   // Per-CTA partials.
   const int64_t cta = blockIdx.x;
 #pragma unroll
-  for (int j = 0; j < kHeadMaxHJ; ++j) {
+  for (int j = 0; j < NJ; ++j) {
     const int h = tid + j * kHeadThreads;
     if (h >= H) continue;
 #pragma unroll
@@ -237,31 +321,44 @@ head_kernel(const HeadParams p) {
     if (p.dbx_part) p.dbx_part[cta * H + h] = dbx[j];
   }
   __syncthreads();
-  if (lane == 0) {
+  constexpr int RW = AP + kStats;
+  if (lane < A) red[warp * RW + lane] = dbl;
+  if (lane == 0)
 #pragma unroll
-    for (int a = 0; a < A; ++a) red[warp * (A + kStats) + a] = dbl[a];
-#pragma unroll
-    for (int s = 0; s < kStats; ++s) red[warp * (A + kStats) + A + s] = st[s];
-  }
+    for (int s = 0; s < kStats; ++s) red[warp * RW + AP + s] = st[s];
   __syncthreads();
-  if (tid < A + kStats) {
+  if (tid < A) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) v += red[w * (A + kStats) + tid];
-    if (tid < A) p.db_part[cta * A + tid] = v;
-    else if (p.stats_part) p.stats_part[cta * kStats + (tid - A)] = v;
+    for (int w = 0; w < kNW; ++w) v += red[w * RW + tid];
+    p.db_part[cta * A + tid] = v;
+  } else if (tid >= AP && tid < AP + kStats && p.stats_part) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) v += red[w * RW + tid];
+    p.stats_part[cta * kStats + (tid - AP)] = v;
   }
+}
+
+template <int A>
+int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
+  void (*k)(const HeadParams);
+  const int nj = (p.H + kHeadThreads - 1) / kHeadThreads;
+  k = nj <= 1 ? head_kernel<A, 1> : (nj == 2 ? head_kernel<A, 2> : head_kernel<A, 4>);
+  SPO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k<<<grid, kHeadThreads, smem, s>>>(p);
+  SPO_LAUNCH_CHECK();
+  return kOk;
 }
 
 }  // namespace
 
-int head_rows_per_tile(int H) { return H > 512 ? 16 : (H > 256 ? 32 : 64); }
+int head_rows_per_tile(int H) { return H > 512 ? 8 : (H > 256 ? 16 : 32); }
 
 size_t head_smem_bytes(int H, int A) {
   const int R = head_rows_per_tile(H);
-  const int NW = kHeadThreads / 32;
-  return sizeof(float) * ((size_t)((H * A + 3) & ~3) + (size_t)R * H + (size_t)R * A +
-                          (size_t)NW * (A + kStats));
+  const int AP = A == 1 ? 1 : (A + 3) & ~3;
+  return sizeof(float) * ((size_t)H * AP + 2 * (size_t)R * H + (size_t)R * AP + (size_t)kNW * (AP + kStats));
 }
 
 int head_grid(int64_t M, int H) {
@@ -282,15 +379,7 @@ int head_launch(HeadParams p, int grid, cudaStream_t s) {
   p.rows_per_tile = head_rows_per_tile(p.H);
   const size_t smem = head_smem_bytes(p.H, p.A);
   if (p.M == 0) return kOk;
-  if (p.A == 9) {
-    SPO_CUDA_TRY(cudaFuncSetAttribute(head_kernel<9>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    head_kernel<9><<<grid, kHeadThreads, smem, s>>>(p);
-  } else {
-    SPO_CUDA_TRY(cudaFuncSetAttribute(head_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    head_kernel<1><<<grid, kHeadThreads, smem, s>>>(p);
-  }
-  SPO_LAUNCH_CHECK();
-  return kOk;
+  return p.A == 9 ? launch_a<9>(p, grid, smem, s) : launch_a<1>(p, grid, smem, s);
 }
 
 }  // namespace spo
