@@ -35,17 +35,28 @@ namespace spo {
 
 namespace {
 
-constexpr int BM = 128;
+constexpr int BM = 128;                                  // output rows per CTA
 constexpr int BN = 128;
 constexpr int BK = 32;
-constexpr int STAGES = 3;
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int EPI_COLS = BN / 2;                         // columns per epilogue warp
 constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
-constexpr uint32_t B_TILE = BN * BK * 4;                 // 16 KB
-constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 64 KB
+constexpr int STAGES_MAX = 4;
+
+// Operand staging of one CTA. Single CTA: A [128 x 32] and B [128 x 32] hi/lo per
+// k-block, 3 stages. CTA pair (cta_group::2, 256 x 128 output tile per pair): each CTA
+// stages its own 128 rows of A and one half (64 rows) of B, 4 stages; the MMA issued by
+// the pair's first CTA reads both CTAs' shared memory.
+template <bool PAIR>
+struct Geo {
+  static constexpr int STAGES = PAIR ? 4 : 3;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr uint32_t B_TILE = B_ROWS * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB pair, 64 KB single
+  static constexpr int UNIT_M = PAIR ? 2 * BM : BM;                // output rows per unit
+};
 // The tensor core's accumulation into TMEM is not exact fp32: its error grows with the
 // number of MMAs summed into one accumulator. Folding every 2 k-blocks (64 reduction
 // elements) keeps learner outputs near 1e-6 relative; 8 k-blocks measured 3-5e-6, enough
@@ -63,8 +74,8 @@ constexpr int kMaxColsumN = 1024;
 enum WaitCode : int { kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, kErrWaitTFull = 4 };
 
 struct __align__(64) Ctl {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[STAGES_MAX];
+  uint64_t empty[STAGES_MAX];
   uint64_t tfull[NACC];
   uint64_t tempty[NACC];
   uint64_t drain;
@@ -125,14 +136,28 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait. Returns false when this CTA aborted (another role gave up) or after
 // kWaitNs, in which case it raises the abort flag and records `code` in *err.
+template <bool CLUSTER = false>
 __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
                           int code) {
-  if (mbar_try(bar, parity)) return true;
+  auto poll = [&]() { return CLUSTER ? mbar_try_cluster(bar, parity) : mbar_try(bar, parity); };
+  if (poll()) return true;
   const uint64_t t0 = now_ns();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (poll()) return true;
     if (*abort_flag) return false;
     if (now_ns() - t0 > kWaitNs) {
       *abort_flag = 1;
@@ -180,6 +205,58 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                : "memory");
 }
 
+// ---- CTA-pair forms (cta_group::2; the cluster is the pair)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// every thread of both CTAs; threads may arrive from divergent paths (no .aligned)
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on an mbarrier of the
+// pair (here: the first CTA's). No multicast: every CTA loads its own operand halves.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t cluster_bar,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on the mbarrier at this shared-memory offset in both CTAs of the pair once the
+// MMAs issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((unsigned short)3)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 // tcgen05.ld.16x256b.x8 without its wait: 16 TMEM lanes (rows) x 64 columns. Register
 // r[4g + i] of thread t holds row (t / 4) + 8 (i / 2), column 8 g + 2 (t % 4) + (i % 2),
 // relative to the lane and column of taddr (the layout of an mma accumulator fragment).
@@ -225,11 +302,15 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 // One instantiation per epilogue (KIND) and dX mask format (BITS: packed bits instead of
 // fp32). 10 warps share the SM's four 16K-register files 3/3/2/2: at most 168 registers a
 // thread.
-template <int KIND, bool BITS>
+template <int KIND, bool BITS, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
                const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
                const KParams P) {
+  using G = Geo<PAIR>;
+  constexpr int STAGES = G::STAGES;
+  constexpr uint32_t STAGE_BYTES = G::STAGE_BYTES;
+  constexpr uint32_t B_TILE = G::B_TILE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -239,6 +320,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t smem0 = smem_u32(smem);
+  // CTA pair: rank 0 issues the MMAs of both CTAs and owns the operand-full and
+  // accumulator-empty barriers; each CTA loads and stores its own 128 rows.
+  const uint32_t rank = PAIR ? cluster_rank() : 0;
+  const bool leader = rank == 0;
+  const int64_t first_unit = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
+  const int64_t unit_step = PAIR ? (gridDim.x >> 1) : gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -247,7 +334,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(smem_u32(&ctl->tfull[a]), 1);
-      mbar_init(smem_u32(&ctl->tempty[a]), kEpiWarps);
+      mbar_init(smem_u32(&ctl->tempty[a]), PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
@@ -255,13 +342,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
   }
   if (warp == 1) {
     __syncwarp();
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&ctl->tmem_base)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&ctl->tmem_base)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&ctl->tmem_base)),
+                   "r"(TMEM_COLS));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // the peer's barriers are initialised before anyone signals them
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
 
@@ -271,10 +368,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     // ------------------------------------------------ TMA producer
     uint32_t it = 0;
     bool ok = true;
-    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
+    for (int64_t u = first_unit; u < P.units && ok; u += unit_step) {
       const int64_t split = u / per_split, rem = u % per_split;
-      const int32_t m0 = (int32_t)((rem / P.n_tiles) * BM);
-      const int32_t n0 = (int32_t)((rem % P.n_tiles) * BN);
+      const int32_t m0 = (int32_t)((rem / P.n_tiles) * G::UNIT_M + rank * BM);
+      const int32_t n0 = (int32_t)((rem % P.n_tiles) * BN + rank * G::B_ROWS);
       const int64_t kbeg = split * P.k_chunk;
       const int64_t kend = min(P.K, kbeg + P.k_chunk);
       const int nkb = (int)((kend - kbeg + BK - 1) / BK);
@@ -285,95 +382,129 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           break;
         }
         const uint32_t bar = smem_u32(&ctl->full[s]);
-        mbar_expect_tx(bar, STAGE_BYTES);
+        // the pair's transfers (both CTAs) complete on the first CTA's barrier
+        if (leader) mbar_expect_tx(bar, PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
+        const uint32_t cbar = PAIR ? map_to_rank(bar, 0) : bar;
+        auto load = [&](uint32_t dst, const CUtensorMap* m, int32_t x, int32_t y) {
+          if constexpr (PAIR)
+            tma_load_2d_pair(dst, m, cbar, x, y);
+          else
+            tma_load_2d(dst, m, bar, x, y);
+        };
         const int32_t k0 = (int32_t)(kbeg + (int64_t)kb * BK);
         const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
         const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
         if (P.a_mn) {
 #pragma unroll
           for (int j = 0; j < BM / 32; ++j) {
-            tma_load_2d(a_hi + j * 4096, &tm_ah, bar, m0 + 32 * j, k0);
-            tma_load_2d(a_lo + j * 4096, &tm_al, bar, m0 + 32 * j, k0);
+            load(a_hi + j * 4096, &tm_ah, m0 + 32 * j, k0);
+            load(a_lo + j * 4096, &tm_al, m0 + 32 * j, k0);
           }
         } else {
-          tma_load_2d(a_hi, &tm_ah, bar, k0, m0);
-          tma_load_2d(a_lo, &tm_al, bar, k0, m0);
+          load(a_hi, &tm_ah, k0, m0);
+          load(a_lo, &tm_al, k0, m0);
         }
         if (P.b_mn) {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j) {
-            tma_load_2d(b_hi + j * 4096, &tm_bh, bar, n0 + 32 * j, k0);
-            tma_load_2d(b_lo + j * 4096, &tm_bl, bar, n0 + 32 * j, k0);
+          for (int j = 0; j < G::B_ROWS / 32; ++j) {
+            load(b_hi + j * 4096, &tm_bh, n0 + 32 * j, k0);
+            load(b_lo + j * 4096, &tm_bl, n0 + 32 * j, k0);
           }
         } else {
-          tma_load_2d(b_hi, &tm_bh, bar, k0, n0);
-          tma_load_2d(b_lo, &tm_bl, bar, k0, n0);
+          load(b_hi, &tm_bh, k0, n0);
+          load(b_lo, &tm_bl, k0, n0);
         }
       }
     }
     if (!ok) {
       // let the copies already issued land before the CTA's shared memory goes away
-      const uint32_t first = it >= (uint32_t)STAGES ? it - STAGES : 0;
-      for (uint32_t i = first; i < it; ++i)
-        mbar_drain(smem_u32(&ctl->full[i % STAGES]), (i / STAGES) & 1);
+      if (leader) {
+        const uint32_t first = it >= (uint32_t)STAGES ? it - STAGES : 0;
+        for (uint32_t i = first; i < it; ++i)
+          mbar_drain(smem_u32(&ctl->full[i % STAGES]), (i / STAGES) & 1);
+      } else {
+        // the second CTA's copies complete on the first CTA's barriers: give them time
+        const uint64_t t0 = now_ns();
+        while (now_ns() - t0 < 10000000ull) {
+        }
+      }
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------ MMA issuer
-    const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)P.a_mn << 15) |
-                           ((uint32_t)P.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
-    const uint32_t a_step = P.a_mn ? 1024u : 32u, b_step = P.b_mn ? 1024u : 32u;
-    const uint32_t a_lbo = P.a_mn ? 4096u : 16u, b_lbo = P.b_mn ? 4096u : 16u;
-    const uint32_t a_sbo = P.a_mn ? 512u : 1024u, b_sbo = P.b_mn ? 512u : 1024u;
-    const uint32_t a_lay = P.a_mn ? 1u : 2u, b_lay = P.b_mn ? 1u : 2u;
-    // Each unit's k-range is cut into segments of at most SEG k-blocks; every segment
-    // gets a fresh accumulator (round robin over NACC), which the epilogue folds into its
-    // fp32 running sum. Few accumulations per TMEM accumulator keep the sum fp32-accurate.
-    uint32_t it = 0, seg_i = 0;
-    bool ok = true;
-    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
-      const int64_t split = u / per_split;
-      const int64_t kbeg = split * P.k_chunk;
-      const int64_t kend = min(P.K, kbeg + P.k_chunk);
-      const int nkb = (int)((kend - kbeg + BK - 1) / BK);
-      for (int kb0 = 0; kb0 < nkb && ok; kb0 += SEG, ++seg_i) {
-        const uint32_t acc = seg_i % NACC;
-        if (!mbar_wait(smem_u32(&ctl->tempty[acc]), ((seg_i / NACC) & 1) ^ 1, abort_flag, P.err,
-                       kErrWaitTEmpty)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem_base + acc * BN;
-        const int kb1 = min(nkb, kb0 + SEG);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-          if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull)) {
+    if (leader) {
+      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)P.a_mn << 15) |
+                             ((uint32_t)P.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(G::UNIT_M >> 4) << 24);
+      const uint32_t a_step = P.a_mn ? 1024u : 32u, b_step = P.b_mn ? 1024u : 32u;
+      const uint32_t a_lbo = P.a_mn ? 4096u : 16u, b_lbo = P.b_mn ? 4096u : 16u;
+      const uint32_t a_sbo = P.a_mn ? 512u : 1024u, b_sbo = P.b_mn ? 512u : 1024u;
+      const uint32_t a_lay = P.a_mn ? 1u : 2u, b_lay = P.b_mn ? 1u : 2u;
+      // Each unit's k-range is cut into segments of at most SEG k-blocks; every segment
+      // gets a fresh accumulator (round robin over NACC), which the epilogue folds into its
+      // fp32 running sum. Few accumulations per TMEM accumulator keep the sum fp32-accurate.
+      uint32_t it = 0, seg_i = 0;
+      bool ok = true;
+      for (int64_t u = first_unit; u < P.units && ok; u += unit_step) {
+        const int64_t split = u / per_split;
+        const int64_t kbeg = split * P.k_chunk;
+        const int64_t kend = min(P.K, kbeg + P.k_chunk);
+        const int nkb = (int)((kend - kbeg + BK - 1) / BK);
+        for (int kb0 = 0; kb0 < nkb && ok; kb0 += SEG, ++seg_i) {
+          const uint32_t acc = seg_i % NACC;
+          if (!mbar_wait<PAIR>(smem_u32(&ctl->tempty[acc]), ((seg_i / NACC) & 1) ^ 1, abort_flag,
+                               P.err, kErrWaitTEmpty)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
-          const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
+          const uint32_t d = tmem_base + acc * BN;
+          const int kb1 = min(nkb, kb0 + SEG);
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+            if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
+            const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
 #pragma unroll
-          for (int ks = 0; ks < BK / 8; ++ks) {
-            const uint64_t adh = make_desc(a_hi + ks * a_step, a_lbo, a_sbo, a_lay);
-            const uint64_t adl = make_desc(a_lo + ks * a_step, a_lbo, a_sbo, a_lay);
-            const uint64_t bdh = make_desc(b_hi + ks * b_step, b_lbo, b_sbo, b_lay);
-            const uint64_t bdl = make_desc(b_lo + ks * b_step, b_lbo, b_sbo, b_lay);
-            mma_tf32(d, adl, bdh, idesc, (kb > kb0 || ks > 0) ? 1u : 0u);
-            mma_tf32(d, adh, bdl, idesc, 1u);
-            mma_tf32(d, adh, bdh, idesc, 1u);
+            for (int ks = 0; ks < BK / 8; ++ks) {
+              const uint64_t adh = make_desc(a_hi + ks * a_step, a_lbo, a_sbo, a_lay);
+              const uint64_t adl = make_desc(a_lo + ks * a_step, a_lbo, a_sbo, a_lay);
+              const uint64_t bdh = make_desc(b_hi + ks * b_step, b_lbo, b_sbo, b_lay);
+              const uint64_t bdl = make_desc(b_lo + ks * b_step, b_lbo, b_sbo, b_lay);
+              const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
+              if constexpr (PAIR) {
+                mma_tf32_pair(d, adl, bdh, idesc, accum);
+                mma_tf32_pair(d, adh, bdl, idesc, 1u);
+                mma_tf32_pair(d, adh, bdh, idesc, 1u);
+              } else {
+                mma_tf32(d, adl, bdh, idesc, accum);
+                mma_tf32(d, adh, bdl, idesc, 1u);
+                mma_tf32(d, adh, bdh, idesc, 1u);
+              }
+            }
+            if constexpr (PAIR)
+              mma_commit_pair(smem_u32(&ctl->empty[s]));
+            else
+              mma_commit(smem_u32(&ctl->empty[s]));
           }
-          mma_commit(smem_u32(&ctl->empty[s]));
+          if (!ok) break;
+          if constexpr (PAIR)
+            mma_commit_pair(smem_u32(&ctl->tfull[acc]));
+          else
+            mma_commit(smem_u32(&ctl->tfull[acc]));
         }
-        if (!ok) break;
-        mma_commit(smem_u32(&ctl->tfull[acc]));
       }
+      // all MMAs issued by this thread complete before TMEM is released (in both CTAs:
+      // the second CTA passes the final cluster barrier only after this thread)
+      if constexpr (PAIR)
+        mma_commit_pair(smem_u32(&ctl->drain));
+      else
+        mma_commit(smem_u32(&ctl->drain));
+      mbar_drain(smem_u32(&ctl->drain), 0);
     }
-    // all MMAs issued by this thread complete before TMEM is released
-    mma_commit(smem_u32(&ctl->drain));
-    mbar_drain(smem_u32(&ctl->drain), 0);
   } else if (warp >= 2) {
     // ------------------------------------------------ epilogue
     // Warp w reads TMEM lanes 32 (w % 4) .. +31 (tile rows) and columns cb .. cb + 63.
@@ -394,9 +525,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     bool ok = true;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     float rs[2 * 32];                        // fp32 running sums: [16-row half][4 g + i]
-    for (int64_t u = blockIdx.x; u < P.units && ok; u += gridDim.x) {
+    // where this warp signals that it has read an accumulator: the MMA issuer's CTA
+    const uint32_t tempty0 = smem_u32(&ctl->tempty[0]);
+    const uint32_t tempty_at = PAIR ? map_to_rank(tempty0, 0) : tempty0;
+    for (int64_t u = first_unit; u < P.units && ok; u += unit_step) {
       const int64_t split = u / per_split, rem = u % per_split;
-      const int64_t m0 = (rem / P.n_tiles) * BM;
+      const int64_t m0 = (rem / P.n_tiles) * G::UNIT_M + rank * BM;
       const int64_t n0 = (rem % P.n_tiles) * BN;
       const int64_t kbeg = split * P.k_chunk;
       const int64_t kend = min(P.K, kbeg + P.k_chunk);
@@ -445,7 +579,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
         // the accumulator is free for the next segment's MMAs once the loads completed
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&ctl->tempty[acc]));
+        if (lane == 0) {
+          if (PAIR && !leader)
+            mbar_arrive_cluster(tempty_at + acc * 8);
+          else
+            mbar_arrive(tempty0 + acc * 8);
+        }
         if (sg != nseg - 1) continue;
         float cs[16];                        // column sums (DX): [g][column pair]
 #pragma unroll
@@ -586,12 +725,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // neither CTA leaves while the pair's MMAs or copies may touch it
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     __syncwarp();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(TMEM_COLS));
+    if constexpr (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(TMEM_COLS));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(TMEM_COLS));
   }
 }
 
@@ -675,18 +821,66 @@ int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, u
   return kOk;
 }
 
-size_t tc_smem_bytes(int kind, int64_t N) {
-  size_t b = 1024 + (size_t)STAGES * STAGE_BYTES + sizeof(Ctl);
+// CTA pairs (cta_group::2) for the dW products, unless built with SPO_TC_PAIR=0. Measured
+// at 1048576 x 512 x 512 on B200: dW 2.89 ms paired vs 3.26 ms single; the forward and dX
+// products run 5-10% slower paired (the pair advances at the pace of its slower CTA and
+// the mainloop is bound by shared-memory bandwidth, which pairing barely relieves), so
+// they stay on single CTAs.
+#ifndef SPO_TC_PAIR
+#define SPO_TC_PAIR 1
+#endif
+bool use_pair(int kind) { return SPO_TC_PAIR != 0 && kind == TC_DW && sm_count() >= 2; }
+
+// CTA pairs that fit on the device at once (one CTA per SM; both SMs of a pair in one
+// GPC). A persistent grid larger than this would leave pairs waiting for a second wave.
+int pair_slots_query();
+int pair_slots() {
+  static std::mutex mu;
+  static int slots[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return sm_count() / 2;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!slots[dev]) slots[dev] = pair_slots_query();
+  return slots[dev];
+}
+
+size_t tc_smem_bytes(int kind, int64_t N, bool pair) {
+  size_t b = 1024 + (pair ? (size_t)Geo<true>::STAGES * Geo<true>::STAGE_BYTES
+                          : (size_t)Geo<false>::STAGES * Geo<false>::STAGE_BYTES) +
+             sizeof(Ctl);
   if (kind == TC_DX || kind == TC_DX_F32) b += (size_t)4 * N * sizeof(float);
   return b;
 }
 
 int64_t units_of(const TcGemmArgs& a, int* splits) {
-  const int64_t mt = ceil_div(a.M, BM), nt = a.N / BN;
+  const int64_t mt = ceil_div(a.M, use_pair(a.kind) ? 2 * BM : BM), nt = a.N / BN;
   int sp = 1;
   if (a.kind == TC_DW) sp = (int)ceil_div(a.K, a.k_chunk);
   if (splits) *splits = sp;
   return mt * nt * sp;
+}
+
+int pair_slots_query() {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = tc_smem_bytes(TC_DX, kMaxColsumN, true);  // the opt-in size of every launch
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  auto kern = tc_gemm_kernel<TC_DW, false, true>;
+  int n = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)cfg.dynamicSmemBytes) != cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+    (void)cudaGetLastError();
+    n = sm_count() / 2;
+  }
+  return n;
 }
 
 }  // namespace
@@ -707,6 +901,7 @@ int tc_gemm_splits(const TcGemmArgs& a) {
 
 int tc_gemm_grid(const TcGemmArgs& a) {
   const int64_t u = units_of(a, nullptr);
+  if (use_pair(a.kind)) return 2 * (int)std::max<int64_t>(1, std::min<int64_t>(u, pair_slots()));
   return (int)std::max<int64_t>(1, std::min<int64_t>(u, sm_count()));
 }
 
@@ -728,6 +923,8 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   if (a.kind == TC_FWD && a.c_bits)
     SPO_CHECK_ARG(reinterpret_cast<uintptr_t>(a.c_bits) % 8 == 0, kErrArg, "tc_gemm: c_bits alignment");
   const bool mn = a.kind == TC_DW;
+  const bool pair = use_pair(a.kind);
+  const uint32_t b_rows = pair ? BN / 2 : BN;  // rows of B one CTA stages (K-major)
   CUtensorMap m_ah, m_al, m_bh, m_bl;
   int rc;
   if (mn) {  // A [K x M], B [K x N] row-major; boxes 32 wide (MN) x 32 deep (K)
@@ -736,12 +933,12 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
     if ((rc = make_map(&m_al, a.a_lo, a.M, a.K, 32, BK, sw))) return rc;
     if ((rc = make_map(&m_bh, a.b_hi, a.N, a.K, 32, BK, sw))) return rc;
     if ((rc = make_map(&m_bl, a.b_lo, a.N, a.K, 32, BK, sw))) return rc;
-  } else {   // A [M x K], B [N x K] row-major; boxes 32 deep (K) x 128 rows
+  } else {   // A [M x K], B [N x K] row-major; boxes 32 deep (K) x 128 (A) / b_rows (B) rows
     const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
     if ((rc = make_map(&m_ah, a.a_hi, a.K, a.M, BK, BM, sw))) return rc;
     if ((rc = make_map(&m_al, a.a_lo, a.K, a.M, BK, BM, sw))) return rc;
-    if ((rc = make_map(&m_bh, a.b_hi, a.K, a.N, BK, BN, sw))) return rc;
-    if ((rc = make_map(&m_bl, a.b_lo, a.K, a.N, BK, BN, sw))) return rc;
+    if ((rc = make_map(&m_bh, a.b_hi, a.K, a.N, BK, b_rows, sw))) return rc;
+    if ((rc = make_map(&m_bl, a.b_lo, a.K, a.N, BK, b_rows, sw))) return rc;
   }
   KParams P{};
   P.kind = a.kind;
@@ -751,7 +948,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.N = a.N;
   P.K = a.K;
   P.k_chunk = mn ? a.k_chunk : align_up_i64(a.K, BK);
-  P.m_tiles = (int)ceil_div(a.M, BM);
+  P.m_tiles = (int)ceil_div(a.M, pair ? 2 * BM : BM);
   P.n_tiles = (int)(a.N / BN);
   P.units = units_of(a, &P.splits);
   P.bias = a.bias;
@@ -764,14 +961,21 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.mask_bits = a.kind == TC_DX || a.kind == TC_DX_F32 ? a.mask_bits : nullptr;
   P.c_bits = a.kind == TC_FWD ? a.c_bits : nullptr;
   const int grid = tc_gemm_grid(a);
-  const size_t smem = tc_smem_bytes(a.kind, a.N);
+  const size_t smem = tc_smem_bytes(a.kind, a.N, pair);
   const bool bits = P.mask_bits != nullptr;
-  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const KParams);
-  switch (a.kind) {
-    case TC_FWD: kern = tc_gemm_kernel<TC_FWD, false>; break;
-    case TC_DX: kern = bits ? tc_gemm_kernel<TC_DX, true> : tc_gemm_kernel<TC_DX, false>; break;
-    case TC_DX_F32: kern = bits ? tc_gemm_kernel<TC_DX_F32, true> : tc_gemm_kernel<TC_DX_F32, false>; break;
-    default: kern = tc_gemm_kernel<TC_DW, false>; break;
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const KParams);
+  Kern kern;
+  if (pair) {
+    kern = tc_gemm_kernel<TC_DW, false, true>;  // use_pair: dW only
+  } else {
+    switch (a.kind) {
+      case TC_FWD: kern = tc_gemm_kernel<TC_FWD, false, false>; break;
+      case TC_DX: kern = bits ? tc_gemm_kernel<TC_DX, true, false> : tc_gemm_kernel<TC_DX, false, false>; break;
+      case TC_DX_F32:
+        kern = bits ? tc_gemm_kernel<TC_DX_F32, true, false> : tc_gemm_kernel<TC_DX_F32, false, false>;
+        break;
+      default: kern = tc_gemm_kernel<TC_DW, false, false>; break;
+    }
   }
   // the shared-memory opt-in is a per-device attribute of each instantiation
   static std::mutex mu;
@@ -782,11 +986,27 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
     std::lock_guard<std::mutex> lk(mu);
     if (!opted.count({dev, (const void*)kern})) {
       SPO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)tc_smem_bytes(TC_DX, kMaxColsumN)));
+                                        (int)tc_smem_bytes(TC_DX, kMaxColsumN, pair)));
       opted.insert({dev, (const void*)kern});
     }
   }
-  kern<<<grid, kThreads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
+  if (pair) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SPO_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_ah, m_al, m_bh, m_bl, P));
+  } else {
+    kern<<<grid, kThreads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
+  }
   SPO_LAUNCH_CHECK();
   return kOk;
 }
