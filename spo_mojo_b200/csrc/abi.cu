@@ -237,7 +237,7 @@ struct NetPlan {
   // workspace carve-outs
   float* acts[SPO_MAX_LAYERS] = {};     // a_l, l = 0..L-2: [rows x d_{l+1}] (hi in TC mode)
   float* acts_lo[SPO_MAX_LAYERS] = {};  // TC mode: lo halves
-  uint32_t* acts_bits[SPO_MAX_LAYERS] = {};  // TC mode, 1 <= l <= L-3: a_l > 0 packed [rows x d_{l+1}/32]
+  uint32_t* acts_bits[SPO_MAX_LAYERS] = {};  // TC mode, l <= L-3: a_l > 0 packed [rows x d_{l+1}/32]
   float* dz[2] = {};                    // ping-pong [rows x max_hidden] (hi in TC mode)
   float* dz_lo[2] = {};                 // TC mode
   float* dz0 = nullptr;                 // TC mode: [rows x d_1] fp32
@@ -308,8 +308,10 @@ void carve_net(NetPlan& n, Carve& c, int64_t rows) {
   for (int l = 0; l + 1 < L; ++l) {
     n.acts[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
     if (n.tc) n.acts_lo[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
-    // packed for the dX GEMM of layer l + 1 (the last hidden layer's mask is read by the head)
-    if (n.tc && l >= 1 && l + 2 < L) n.acts_bits[l] = c.take<uint32_t>((size_t)rows * (d.dims[l + 1] / 32));
+    // packed for the dX GEMM of layer l + 1 (the last hidden layer's mask is read by the
+    // head); layer 0's is written by the input-layer forward when its shape allows
+    const bool packs = l >= 1 || (fwd_skinny_ok(d.dims[0], d.dims[1]) && d.dims[1] % 32 == 0);
+    if (n.tc && packs && l + 2 < L) n.acts_bits[l] = c.take<uint32_t>((size_t)rows * (d.dims[l + 1] / 32));
   }
   for (int i = 0; i < 2; ++i) {
     n.dz[i] = c.take<float>((size_t)rows * n.max_hidden);
@@ -436,8 +438,11 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, co
   if (!n.tc) {
     const float* h = obs;
     for (int l = 0; l + 1 < d.num_layers; ++l) {
-      int rc = gemm_fwd(s, n.acts[l], h, params + n.w_off[l], params + n.b_off[l], rows, d.dims[l],
-                        d.dims[l + 1], true);
+      const float* w = params + n.w_off[l];
+      const float* b = params + n.b_off[l];
+      int rc = l == 0 && fwd_skinny_ok(d.dims[0], d.dims[1])
+                   ? fwd_skinny_launch(h, w, b, rows, d.dims[0], d.dims[1], n.acts[0], nullptr, nullptr, s)
+                   : gemm_fwd(s, n.acts[l], h, w, b, rows, d.dims[l], d.dims[l + 1], true);
       if (rc) return rc;
       h = n.acts[l];
     }
@@ -448,8 +453,11 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, co
                                   n.wsplit[l][1], n.wsplit[l][2], n.wsplit[l][3], s);
     if (rc) return rc;
   }
-  int rc = gemm_fwd_split(s, n.acts[0], n.acts_lo[0], obs, params + n.w_off[0], params + n.b_off[0],
-                          rows, d.dims[0], d.dims[1]);
+  int rc = fwd_skinny_ok(d.dims[0], d.dims[1])
+               ? fwd_skinny_launch(obs, params + n.w_off[0], params + n.b_off[0], rows, d.dims[0], d.dims[1],
+                                   n.acts[0], n.acts_lo[0], n.acts_bits[0], s)
+               : gemm_fwd_split(s, n.acts[0], n.acts_lo[0], obs, params + n.w_off[0], params + n.b_off[0],
+                                rows, d.dims[0], d.dims[1]);
   if (rc) return rc;
   if (rows == 0) return kOk;
   for (int l = 1; l + 1 < d.num_layers; ++l) {
@@ -518,7 +526,7 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, const
       x.N = kin;
       x.K = nout;
       x.mask = n.acts[l - 1];
-      x.mask_bits = n.acts_bits[l - 1];  // packed by the forward GEMM of layer l - 1 >= 1
+      x.mask_bits = n.acts_bits[l - 1];  // packed by the forward of layer l - 1, when it was
       x.c_hi = last ? n.dz0 : n.dz[cur ^ 1];
       x.c_lo = last ? nullptr : n.dz_lo[cur ^ 1];
       x.colsum = n.db_part[l - 1];

@@ -1,0 +1,215 @@
+// The first layer of the learner's MLPs, whose input is narrow: x [rows x k] with k <= 32
+// (the 27-wide board encoding). The CUDA-core GEMM tiles waste most of a 64- or 128-wide
+// tile on k = 27; these kernels stream the wide side once, at the HBM rate.
+//
+// Forward (linear_forward + relu, networks/linear.mojo:37-95, networks/mlp.mojo:34-46):
+// y = relu(x W + b), W [k x n]. CTA = 128 threads over 512 columns: thread t keeps its 4
+// columns of W (k x 4 values) and of b in registers and walks the rows of its CTA; the
+// rows of x are staged in shared memory and read as broadcasts. Each row's outputs leave
+// as one float4 per thread (2 KB contiguous per CTA), optionally as a TF32 hi/lo pair and
+// with the packed ReLU mask (bit j of word w = column 32 w + j).
+//
+// Weight gradient: dW[k x n] = x^T dY summed over rows, dY [rows x n].
+// CTA = 256 threads over one chunk of rows and 512 columns: thread t owns the 4 columns
+// 4 (t % 128) .. +3 of its column block and one half of the k features (t / 128), so its
+// accumulators are [half of k] x 4. Rows are walked in blocks of kRows: the block's x rows
+// are staged in shared memory (zero-padded to 32 features) and read as broadcasts, the dY
+// float4 of each row is loaded straight from global memory, 8 rows in flight per thread.
+// Each CTA writes its partial [k x n] tile to part[chunk]; a deterministic reduction adds
+// the chunks (linear_backward's dW, networks/linear.mojo:120-167).
+#include "spo_common.cuh"
+#include "kernels.cuh"
+
+namespace spo {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kCols = 512;       // columns per CTA (128 threads x float4)
+constexpr int kMaxK = 32;
+constexpr int kHalf = kMaxK / 2;  // features per thread
+constexpr int kRows = 64;        // rows staged per block
+constexpr int kUnroll = 8;
+
+__global__ void __launch_bounds__(kThreads, 2)
+dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int64_t rows, int k, int64_t n,
+                 int64_t chunk, float* __restrict__ part) {
+  __shared__ __align__(16) float xs[kRows][kMaxK];
+  const int tid = threadIdx.x;
+  const int half = tid / 128;
+  const int64_t col = (int64_t)blockIdx.y * kCols + 4 * (tid % 128);
+  const bool col_ok = col < n;
+  const int64_t r_begin = (int64_t)blockIdx.x * chunk;
+  const int64_t r_end = min(rows, r_begin + chunk);
+  const int i0 = half * kHalf;
+
+  float acc[kHalf][4];
+#pragma unroll
+  for (int i = 0; i < kHalf; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+  for (int64_t rb = r_begin; rb < r_end; rb += kRows) {
+    const int nr = (int)min((int64_t)kRows, r_end - rb);
+    __syncthreads();  // the previous block's x rows are consumed
+    for (int e = tid; e < kRows * kMaxK; e += kThreads) {
+      const int r = e / kMaxK, i = e % kMaxK;
+      xs[r][i] = (r < nr && i < k) ? __ldg(x + (rb + r) * k + i) : 0.f;
+    }
+    __syncthreads();
+    if (col_ok) {
+      for (int r0 = 0; r0 < nr; r0 += kUnroll) {
+        float4 g[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          g[u] = r0 + u < nr ? __ldg(reinterpret_cast<const float4*>(dy + (rb + r0 + u) * n + col))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const float4* xr = reinterpret_cast<const float4*>(&xs[r0 + u][i0]);
+#pragma unroll
+          for (int c = 0; c < kHalf / 4; ++c) {
+            const float4 xv = xr[c];
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              float* a = acc[4 * c + t];
+              a[0] = fmaf(xa[t], g[u].x, a[0]);
+              a[1] = fmaf(xa[t], g[u].y, a[1]);
+              a[2] = fmaf(xa[t], g[u].z, a[2]);
+              a[3] = fmaf(xa[t], g[u].w, a[3]);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (!col_ok) return;
+  float* out = part + (int64_t)blockIdx.x * k * n;
+#pragma unroll
+  for (int i = 0; i < kHalf; ++i) {
+    const int f = i0 + i;
+    if (f < k)
+      *reinterpret_cast<float4*>(out + (int64_t)f * n + col) =
+          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  }
+}
+
+constexpr int kFwdThreads = 128;
+
+__global__ void __launch_bounds__(kFwdThreads, 3)
+fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                  int64_t rows, int k, int64_t n, int64_t chunk, float* __restrict__ y,
+                  float* __restrict__ y_lo, uint32_t* __restrict__ bits) {
+  __shared__ __align__(16) float xs[kRows][kMaxK];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t col = (int64_t)blockIdx.y * kCols + 4 * tid;
+  const bool col_ok = col < n;
+  float wr[kMaxK][4];
+#pragma unroll
+  for (int i = 0; i < kMaxK; ++i) {
+    const float4 v = (col_ok && i < k) ? __ldg(reinterpret_cast<const float4*>(w + (int64_t)i * n + col))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    wr[i][0] = v.x; wr[i][1] = v.y; wr[i][2] = v.z; wr[i][3] = v.w;
+  }
+  const float4 bv = col_ok ? __ldg(reinterpret_cast<const float4*>(b + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t r_begin = (int64_t)blockIdx.x * chunk;
+  const int64_t r_end = min(rows, r_begin + chunk);
+  for (int64_t rb = r_begin; rb < r_end; rb += kRows) {
+    const int nr = (int)min((int64_t)kRows, r_end - rb);
+    __syncthreads();
+    for (int e = tid; e < kRows * kMaxK; e += kFwdThreads) {
+      const int r = e / kMaxK, i = e % kMaxK;
+      xs[r][i] = (r < nr && i < k) ? __ldg(x + (rb + r) * k + i) : 0.f;
+    }
+    __syncthreads();
+    for (int r = 0; r < nr; ++r) {
+      // products summed in k order from zero, then the bias (the CUDA-core GEMM's order)
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      const float4* xr = reinterpret_cast<const float4*>(xs[r]);
+#pragma unroll
+      for (int c = 0; c < kMaxK / 4; ++c) {
+        const float4 xv = xr[c];
+        const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          a0 = fmaf(xa[t], wr[4 * c + t][0], a0);
+          a1 = fmaf(xa[t], wr[4 * c + t][1], a1);
+          a2 = fmaf(xa[t], wr[4 * c + t][2], a2);
+          a3 = fmaf(xa[t], wr[4 * c + t][3], a3);
+        }
+      }
+      float v[4] = {a0 + bv.x, a1 + bv.y, a2 + bv.z, a3 + bv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) v[t] = v[t] > 0.f ? v[t] : 0.f;
+      const int64_t row = rb + r;
+      if (col_ok) {
+        if (y_lo) {
+          float h[4], l[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) tf32_split_pos(v[t], h[t], l[t]);
+          *reinterpret_cast<float4*>(y + row * n + col) = make_float4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<float4*>(y_lo + row * n + col) = make_float4(l[0], l[1], l[2], l[3]);
+        } else {
+          *reinterpret_cast<float4*>(y + row * n + col) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      }
+      if (bits) {
+        // 8 threads cover 32 columns: OR their nibbles, the first of them stores the word
+        uint32_t m = ((v[0] > 0.f ? 1u : 0u) | (v[1] > 0.f ? 2u : 0u) | (v[2] > 0.f ? 4u : 0u) |
+                      (v[3] > 0.f ? 8u : 0u)) << (4 * (lane & 7));
+        m |= __shfl_xor_sync(0xffffffffu, m, 1);
+        m |= __shfl_xor_sync(0xffffffffu, m, 2);
+        m |= __shfl_xor_sync(0xffffffffu, m, 4);
+        if ((lane & 7) == 0 && col_ok) bits[row * (n / 32) + col / 32] = m;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+bool dw_skinny_ok(int64_t k, int64_t n) { return k >= 1 && k <= kMaxK && n >= 4 && n % 4 == 0; }
+
+bool fwd_skinny_ok(int64_t k, int64_t n) { return k >= 1 && k <= kMaxK && n >= 4 && n % 4 == 0; }
+
+int fwd_skinny_launch(const float* x, const float* w, const float* b, int64_t rows, int64_t k, int64_t n,
+                      float* y, float* y_lo, uint32_t* bits, cudaStream_t s) {
+  SPO_CHECK_ARG(fwd_skinny_ok(k, n), kErrUnsupported, "fwd_skinny: k <= 32 and n % 4 == 0");
+  SPO_CHECK_ARG(aligned16(w) && aligned16(b) && aligned16(y) && (!y_lo || aligned16(y_lo)), kErrAlign,
+                "fwd_skinny: W, b and outputs must be 16-byte aligned");
+  SPO_CHECK_ARG(!bits || n % 32 == 0, kErrUnsupported, "fwd_skinny: packed mask needs n % 32 == 0");
+  if (rows <= 0) return kOk;
+  const int64_t col_blocks = ceil_div(n, kCols);
+  const int64_t want = std::max<int64_t>(1, 3LL * sm_count() / col_blocks);
+  const int64_t chunk = std::max<int64_t>(kRows, ceil_div(ceil_div(rows, want), kRows) * kRows);
+  dim3 grid((unsigned)ceil_div(rows, chunk), (unsigned)col_blocks);
+  fwd_skinny_kernel<<<grid, kFwdThreads, 0, s>>>(x, w, b, rows, (int)k, n, chunk, y, y_lo, bits);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
+
+int64_t dw_skinny_max_parts() { return 4LL * sm_count(); }
+
+int64_t dw_skinny_chunk(int64_t rows, int64_t n) {
+  // enough chunks for ~4 CTAs per SM, each at least a few row blocks long
+  const int64_t col_blocks = ceil_div(n, kCols);
+  const int64_t want = std::max<int64_t>(1, dw_skinny_max_parts() / col_blocks);
+  return std::max<int64_t>(4 * kRows, ceil_div(ceil_div(std::max<int64_t>(rows, 1), want), kRows) * kRows);
+}
+
+int dw_skinny_launch(const float* x, const float* dy, int64_t rows, int64_t k, int64_t n, float* part,
+                     int* parts, cudaStream_t s) {
+  SPO_CHECK_ARG(dw_skinny_ok(k, n), kErrUnsupported, "dw_skinny: k <= 32 and n % 4 == 0");
+  SPO_CHECK_ARG(aligned16(dy) && aligned16(part), kErrAlign, "dw_skinny: dY and part must be 16-byte aligned");
+  const int64_t chunk = dw_skinny_chunk(rows, n);
+  const int64_t p = rows > 0 ? ceil_div(rows, chunk) : 0;
+  if (parts) *parts = (int)p;
+  if (p == 0) return kOk;
+  dim3 grid((unsigned)p, (unsigned)ceil_div(n, kCols));
+  dw_skinny_kernel<<<grid, kThreads, 0, s>>>(x, dy, rows, (int)k, n, chunk, part);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
+
+}  // namespace spo

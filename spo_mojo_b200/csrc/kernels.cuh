@@ -128,7 +128,13 @@ int value_grad_launch(float* dv, const float* v, const float* t, int64_t n, floa
 int relu_launch(float* a, int64_t n, cudaStream_t s);
 int relu_bwd_launch(float* g, const float* act, int64_t n, cudaStream_t s);
 // part[c][n] = sum of rows [c*per, (c+1)*per) of x [rows x n], per = ceil(rows / chunks).
-// dW = x^T dY for inputs at most 32 wide (dw_skinny.cu): per-chunk partials
+// y = relu(x W + b) for inputs at most 32 wide (input_layer.cu): y fp32, or a TF32 hi/lo
+// pair (y = hi) when y_lo is set; bits (optional): packed y > 0, [rows x n/32] words.
+bool fwd_skinny_ok(int64_t k, int64_t n);
+int fwd_skinny_launch(const float* x, const float* w, const float* b, int64_t rows, int64_t k, int64_t n,
+                      float* y, float* y_lo, uint32_t* bits, cudaStream_t s);
+
+// dW = x^T dY for inputs at most 32 wide (input_layer.cu): per-chunk partials
 // part[chunk][k x n], *parts chunks (at most dw_skinny_max_parts()).
 bool dw_skinny_ok(int64_t k, int64_t n);
 int64_t dw_skinny_max_parts();
