@@ -11,7 +11,8 @@ Timed quantities (one JSON line on rank 0):
   value       samples/s with the batch already in HBM: K steps between CUDA events on
               the learner's stream, max over ranks
   e2e         the same through the public API with pinned HOST buffers: each step
-              copies its batch host->device and reads the loss statistics back
+              copies its batch host->device (HostFeed: the upload of step i+1 runs on a
+              copy stream during step i) and reads the loss statistics back
   roofline    the dominant kernel (the hidden-layer GEMM) timed with CUDA events on the
               same stream with the step's shapes; algorithmic FLOPs / duration vs the
               measured peak
@@ -266,7 +267,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
     from spo_mojo_b200 import ffi
-    from spo_mojo_b200.learner import Comm, Learner
+    from spo_mojo_b200.learner import Comm, HostFeed, Learner
 
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
@@ -343,16 +344,21 @@ def run_ours(args):
         d2h = stats_host.numel() * 4
         if world > 1:
             dist.barrier()
+        feed = HostFeed(host, dev, stream)
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         w0 = time.perf_counter()
         e0.record(stream)
+        feed.copy.wait_stream(stream)  # every upload starts inside the timed region
         with torch.cuda.stream(stream):
-            for _ in range(args.steps):
-                for k, v in host.items():
-                    batch[k].copy_(v, non_blocking=True)
-                step(batch)
+            j = feed.upload(host)
+            for i in range(args.steps):
+                b = feed.take(j)
+                nxt = feed.upload(host) if i + 1 < args.steps else None  # overlaps step i
+                step(b)
+                feed.release(j)
                 stats_host.copy_(L.stats_tensor(), non_blocking=True)
+                j = nxt
         e1.record(stream)
         e1.synchronize()
         wall = (time.perf_counter() - w0) * 1e3 / args.steps

@@ -31,10 +31,45 @@ constexpr int kHalf = kMaxK / 2;  // features per thread
 constexpr int kRows = 64;        // rows staged per block
 constexpr int kUnroll = 8;
 
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+// Double-buffered staging of the rows of x [rows x k] (k <= kMaxK) in shared memory.
+// Columns k..kMaxK-1 stay zero (cleared once); a block of kRows rows is copied with
+// 4-byte cp.async (consecutive threads take consecutive elements: coalesced), one block
+// ahead of the one being consumed.
+struct XStage {
+  float (*xs)[kRows][kMaxK];  // [2][kRows][kMaxK]
+  const float* x;
+  int k;
+  int64_t r_begin, r_end;
+  __device__ void clear(int tid, int nthreads) {
+    for (int e = tid; e < 2 * kRows * kMaxK; e += nthreads) (&xs[0][0][0])[e] = 0.f;
+  }
+  // issue the copies of block b (rows r_begin + b*kRows ..) into buffer b & 1
+  __device__ void issue(int64_t b, int tid, int nthreads) {
+    const int64_t rb = r_begin + b * kRows;
+    if (rb < r_end) {
+      const int nr = (int)min((int64_t)kRows, r_end - rb);
+      float (*buf)[kMaxK] = xs[b & 1];
+      const float* src = x + rb * k;
+      for (int e = tid; e < nr * k; e += nthreads) {
+        const int r = e / k, i = e - r * k;
+        cp_async4(&buf[r][i], src + e);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  __device__ static void wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+};
+
 __global__ void __launch_bounds__(kThreads, 2)
 dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int64_t rows, int k, int64_t n,
                  int64_t chunk, float* __restrict__ part) {
-  __shared__ __align__(16) float xs[kRows][kMaxK];
+  __shared__ __align__(16) float xs2[2][kRows][kMaxK];
   const int tid = threadIdx.x;
   const int half = tid / 128;
   const int64_t col = (int64_t)blockIdx.y * kCols + 4 * (tid % 128);
@@ -49,14 +84,17 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int6
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
-  for (int64_t rb = r_begin; rb < r_end; rb += kRows) {
+  XStage st{xs2, x, k, r_begin, r_end};
+  st.clear(tid, kThreads);
+  __syncthreads();
+  st.issue(0, tid, kThreads);
+  int64_t blk = 0;
+  for (int64_t rb = r_begin; rb < r_end; rb += kRows, ++blk) {
     const int nr = (int)min((int64_t)kRows, r_end - rb);
-    __syncthreads();  // the previous block's x rows are consumed
-    for (int e = tid; e < kRows * kMaxK; e += kThreads) {
-      const int r = e / kMaxK, i = e % kMaxK;
-      xs[r][i] = (r < nr && i < k) ? __ldg(x + (rb + r) * k + i) : 0.f;
-    }
+    st.issue(blk + 1, tid, kThreads);  // the buffer it fills was released by the last barrier
+    XStage::wait_prev();
     __syncthreads();
+    float (*xs)[kMaxK] = xs2[blk & 1];
     if (col_ok) {
       for (int r0 = 0; r0 < nr; r0 += kUnroll) {
         float4 g[kUnroll];
@@ -83,7 +121,9 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int6
         }
       }
     }
+    __syncthreads();  // buffer blk & 1 is consumed before block blk + 2 is copied into it
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   if (!col_ok) return;
   float* out = part + (int64_t)blockIdx.x * k * n;
 #pragma unroll
@@ -101,7 +141,7 @@ __global__ void __launch_bounds__(kFwdThreads, 3)
 fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
                   int64_t rows, int k, int64_t n, int64_t chunk, float* __restrict__ y,
                   float* __restrict__ y_lo, uint32_t* __restrict__ bits) {
-  __shared__ __align__(16) float xs[kRows][kMaxK];
+  __shared__ __align__(16) float xs2[2][kRows][kMaxK];
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t col = (int64_t)blockIdx.y * kCols + 4 * tid;
   const bool col_ok = col < n;
@@ -115,14 +155,17 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ w, cons
   const float4 bv = col_ok ? __ldg(reinterpret_cast<const float4*>(b + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const int64_t r_begin = (int64_t)blockIdx.x * chunk;
   const int64_t r_end = min(rows, r_begin + chunk);
-  for (int64_t rb = r_begin; rb < r_end; rb += kRows) {
+  XStage st{xs2, x, k, r_begin, r_end};
+  st.clear(tid, kFwdThreads);
+  __syncthreads();
+  st.issue(0, tid, kFwdThreads);
+  int64_t blk = 0;
+  for (int64_t rb = r_begin; rb < r_end; rb += kRows, ++blk) {
     const int nr = (int)min((int64_t)kRows, r_end - rb);
+    st.issue(blk + 1, tid, kFwdThreads);
+    XStage::wait_prev();
     __syncthreads();
-    for (int e = tid; e < kRows * kMaxK; e += kFwdThreads) {
-      const int r = e / kMaxK, i = e % kMaxK;
-      xs[r][i] = (r < nr && i < k) ? __ldg(x + (rb + r) * k + i) : 0.f;
-    }
-    __syncthreads();
+    float (*xs)[kMaxK] = xs2[blk & 1];
     for (int r = 0; r < nr; ++r) {
       // products summed in k order from zero, then the bias (the CUDA-core GEMM's order)
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
@@ -164,7 +207,9 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ w, cons
         if ((lane & 7) == 0 && col_ok) bits[row * (n / 32) + col / 32] = m;
       }
     }
+    __syncthreads();  // buffer blk & 1 is consumed before block blk + 2 is copied into it
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 }  // namespace

@@ -211,6 +211,51 @@ class Learner:
                    dual=wl.dual, device=device, **kw)
 
 
+class HostFeed:
+    """Feeds host (pinned) batches to the learner through two device buffers: the upload of
+    the next step's inputs runs on a copy stream while the current step's kernels run on
+    the compute stream (events order each buffer's upload before its step, and the step
+    before the buffer's next upload).
+
+        feed = HostFeed(host_batch, device, stream)
+        j = feed.upload(host_batch)              # inputs of step 0
+        for i in range(steps):
+            b = feed.take(j)                     # the compute stream waits for the upload
+            if i + 1 < steps:
+                nxt = feed.upload(next_host_batch)
+            learner.step(b, stream=stream)
+            feed.release(j)                      # the buffer may be refilled after the step
+            j = nxt
+    """
+
+    def __init__(self, like, device, compute_stream):
+        self.device = torch.device(device) if not isinstance(device, torch.device) else device
+        self.compute = compute_stream
+        self.copy = torch.cuda.Stream(self.device)
+        self.bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=self.device) for k, v in like.items()}
+                     for _ in range(2)]
+        self.ready = [torch.cuda.Event() for _ in range(2)]
+        self.free = [torch.cuda.Event() for _ in range(2)]
+        self._next = 0
+
+    def upload(self, host_batch):
+        j = self._next
+        self._next ^= 1
+        self.copy.wait_event(self.free[j])  # a never-recorded event does not block
+        with torch.cuda.stream(self.copy):
+            for k, v in host_batch.items():
+                self.bufs[j][k].copy_(v, non_blocking=True)
+        self.ready[j].record(self.copy)
+        return j
+
+    def take(self, j):
+        self.compute.wait_event(self.ready[j])
+        return self.bufs[j]
+
+    def release(self, j):
+        self.free[j].record(self.compute)
+
+
 class Comm:
     """NCCL communicator of libspo_cuda (one per rank); ids shared by the caller."""
 
