@@ -224,6 +224,25 @@ SPO_API int spo_truncated_gae(spo_stream_t stream, float* adv, float* targets, c
                       const float* discount, const float* v_tm1, const float* v_t,
                       const float* truncation, int64_t batch, int32_t t_len, float lambda);
 
+/* ------------------------------------------------------------------ replay buffer, device side
+ * TrajectoryBuffer.sample_indices rl_utils/buffer.mojo:138-152: idx[i] =
+ * rand_bits(seed, stream_id, i) % count (ops/rng.mojo:43-58), i < n, with replacement.
+ * count == 0 is rejected ("the buffer is empty"). */
+SPO_API int spo_replay_sample(spo_stream_t stream, int32_t* idx, int64_t n, int64_t count, uint32_t seed,
+                              uint32_t stream_id);
+
+/* TrajectoryBuffer.gather / gather_steps / gather_bootstrap / gather_q
+ * rl_utils/buffer.mojo:154-211: dst[k, :] = src[idx[k], :] for k < n, span floats per
+ * sequence, in the order of idx, repeats allowed. An index outside [0, count) gives a zero
+ * row and sets *err (optional) to 1 (the reference raises on the host). */
+SPO_API int spo_replay_gather(spo_stream_t stream, float* dst, const float* src, const int32_t* idx,
+                              int64_t n, int64_t span, int64_t count, int32_t* err);
+
+/* ttt_encode_obs_kernel envs/tictactoe.mojo:449-480 and ttt_legal_mask_from_obs_kernel
+ * :577-597: board cells [n x 9] coded +1 agent / -1 rival / 0 empty -> obs [n x 27], the
+ * plane-major 0/1 planes [empty | agent | rival], and mask [n x 9] (optional) = empty. */
+SPO_API int spo_encode_obs(spo_stream_t stream, float* obs, float* mask, const float* cells, int64_t n);
+
 /* ------------------------------------------------------------------ tensor-core GEMM
  * The hidden-layer products of linear_forward / linear_backward
  * (networks/linear.mojo:37-167) on sm_100a tensor cores (tcgen05, TF32 inputs, fp32

@@ -1068,6 +1068,20 @@ int spo_truncated_gae(spo_stream_t stream, float* adv, float* targets, const flo
                     S(stream));
 }
 
+int spo_replay_sample(spo_stream_t stream, int32_t* idx, int64_t n, int64_t count, uint32_t seed,
+                      uint32_t stream_id) {
+  return replay_sample_launch(idx, n, count, seed, stream_id, S(stream));
+}
+
+int spo_replay_gather(spo_stream_t stream, float* dst, const float* src, const int32_t* idx, int64_t n,
+                      int64_t span, int64_t count, int32_t* err) {
+  return replay_gather_launch(dst, src, idx, n, span, count, err, S(stream));
+}
+
+int spo_encode_obs(spo_stream_t stream, float* obs, float* mask, const float* cells, int64_t n) {
+  return encode_obs_launch(obs, mask, cells, n, S(stream));
+}
+
 // ---------------------------------------------------------------- learner
 int spo_learner_layout_of(const spo_learner_desc* desc, spo_learner_layout* out) {
   SPO_CHECK_ARG(out != nullptr, kErrArg, "null output");

@@ -143,6 +143,13 @@ int dw_skinny_launch(const float* x, const float* dy, int64_t rows, int64_t k, i
 
 int colsum_part_launch(const float* x, int64_t rows, int64_t n, int64_t chunks, float* part,
                        cudaStream_t s);
+// replay.cu: replay sampling / gather and observation encoding
+int replay_sample_launch(int32_t* idx, int64_t n, int64_t count, uint32_t seed, uint32_t stream,
+                         cudaStream_t s);
+int replay_gather_launch(float* dst, const float* src, const int32_t* idx, int64_t n, int64_t span,
+                         int64_t count, int* err, cudaStream_t s);
+int encode_obs_launch(float* obs, float* mask, const float* cells, int64_t n, cudaStream_t s);
+
 int gae_launch(float* adv, float* targets, const float* r, const float* discount,
                const float* v_tm1, const float* v_t, const float* trunc, int64_t batch,
                int t_len, float lambda, cudaStream_t s);

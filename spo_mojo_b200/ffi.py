@@ -136,6 +136,9 @@ SIGNATURES = {
     "spo_adam_flat": (INT, [P, P, P, P, P, I64, F, F, F, F, I32, F]),
     "spo_ema": (INT, [P, P, P, I64, F]),
     "spo_truncated_gae": (INT, [P, P, P, P, P, P, P, P, I64, I32, F]),
+    "spo_replay_sample": (INT, [P, P, I64, I64, ctypes.c_uint32, ctypes.c_uint32]),
+    "spo_replay_gather": (INT, [P, P, P, P, I64, I64, I64, P]),
+    "spo_encode_obs": (INT, [P, P, P, P, I64]),
     "spo_tc_gemm_shape": (INT, [ctypes.POINTER(TcGemmDesc), ctypes.POINTER(I32), ctypes.POINTER(I32)]),
     "spo_tc_gemm": (INT, [P, ctypes.POINTER(TcGemmDesc)]),
     "spo_split_tf32": (INT, [P, P, P, P, I64, I32]),
