@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SPO_ABI_VERSION 2
+#define SPO_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SPO_API __attribute__((visibility("default")))
@@ -329,6 +329,11 @@ typedef struct spo_batch {
   const float* logits_old; /* [rows x A] pi_old logits (actor, use_kl) */
   const float* target;     /* [rows] critic targets */
   int64_t rows;
+  /* Board cells [rows x 9] (+1 agent / -1 rival / 0 empty), used when obs is null: the
+   * first layers read the 27-wide [empty | agent | rival] encoding of the cells
+   * (ttt_encode_obs_kernel, envs/tictactoe.mojo:449-480) and, when mask is null too, the
+   * actor's legal mask is the empty plane (envs/tictactoe.mojo:577-597). */
+  const float* cells;
 } spo_batch;
 
 typedef struct spo_train_state {

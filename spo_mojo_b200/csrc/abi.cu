@@ -170,7 +170,7 @@ int gemm_dx(cudaStream_t s, float* dx, const float* dy, const float* w, const fl
 int gemm_dw(cudaStream_t s, float* part, const float* x, const float* dy, int64_t rows,
             int64_t k, int64_t n, int* parts) {
   if (dw_skinny_ok(k, n) && aligned16(dy) && aligned16(part))
-    return dw_skinny_launch(x, dy, rows, k, n, part, parts, s);
+    return dw_skinny_launch(LayerInput{x, nullptr}, dy, rows, k, n, part, parts, s);
   DwCfg c = dw_cfg(k, n, rows);
   if (parts) *parts = c.parts;
   if (c.parts == 0) return kOk;
@@ -432,16 +432,18 @@ int gemm_fwd_split(cudaStream_t s, float* y_hi, float* y_lo, const float* x, con
 
 // Forward of layers 0..L-2 (ReLU) into the activation cache. In tensor-core mode the
 // hidden weights are first split into TF32 hi/lo pairs (W^T for the forward, W for dX).
-int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, const float* obs,
+int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, LayerInput in,
                        int64_t rows, int* err) {
   const spo_mlp_desc& d = n.d;
+  SPO_CHECK_ARG(!in.cells || fwd_skinny_ok(d.dims[0], d.dims[1]), kErrUnsupported,
+                "board cells need a 27-wide input layer");
   if (!n.tc) {
-    const float* h = obs;
+    const float* h = in.x;
     for (int l = 0; l + 1 < d.num_layers; ++l) {
       const float* w = params + n.w_off[l];
       const float* b = params + n.b_off[l];
       int rc = l == 0 && fwd_skinny_ok(d.dims[0], d.dims[1])
-                   ? fwd_skinny_launch(h, w, b, rows, d.dims[0], d.dims[1], n.acts[0], nullptr, nullptr, s)
+                   ? fwd_skinny_launch(in, w, b, rows, d.dims[0], d.dims[1], n.acts[0], nullptr, nullptr, s)
                    : gemm_fwd(s, n.acts[l], h, w, b, rows, d.dims[l], d.dims[l + 1], true);
       if (rc) return rc;
       h = n.acts[l];
@@ -454,9 +456,9 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, co
     if (rc) return rc;
   }
   int rc = fwd_skinny_ok(d.dims[0], d.dims[1])
-               ? fwd_skinny_launch(obs, params + n.w_off[0], params + n.b_off[0], rows, d.dims[0], d.dims[1],
+               ? fwd_skinny_launch(in, params + n.w_off[0], params + n.b_off[0], rows, d.dims[0], d.dims[1],
                                    n.acts[0], n.acts_lo[0], n.acts_bits[0], s)
-               : gemm_fwd_split(s, n.acts[0], n.acts_lo[0], obs, params + n.w_off[0], params + n.b_off[0],
+               : gemm_fwd_split(s, n.acts[0], n.acts_lo[0], in.x, params + n.w_off[0], params + n.b_off[0],
                                 rows, d.dims[0], d.dims[1]);
   if (rc) return rc;
   if (rows == 0) return kOk;
@@ -484,7 +486,7 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, co
 // Backward of the hidden layers L-2..1 on the tensor cores (dW split over rows; dX with
 // the ReLU mask and the bias-gradient column sums fused), then layer 0's dW on the CUDA
 // cores from the fp32 dz0.
-int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, const float* obs,
+int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, LayerInput in,
                     int64_t rows, float* grads, ReduceParams& red, int* err) {
   const spo_mlp_desc& d = n.d;
   const int L = d.num_layers;
@@ -539,7 +541,8 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, const
     cur ^= 1;
   }
   int parts = 0;
-  rc = gemm_dw(s, n.dw_part[0], obs, n.dz0, rows, d.dims[0], d.dims[1], &parts);
+  rc = in.cells ? dw_skinny_launch(in, n.dz0, rows, d.dims[0], d.dims[1], n.dw_part[0], &parts, s)
+                : gemm_dw(s, n.dw_part[0], in.x, n.dz0, rows, d.dims[0], d.dims[1], &parts);
   if (rc) return rc;
   add_seg(red, n.dw_part[0], grads + n.w_off[0], (int64_t)d.dims[0] * d.dims[1],
           (int64_t)d.dims[0] * d.dims[1], parts);
@@ -555,7 +558,8 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
   const spo_mlp_desc& d = n.d;
   const int L = d.num_layers;
   const int64_t rows = b.rows;
-  int rc = net_forward_hidden(n, s, params, b.obs, rows, Lr->err);
+  const LayerInput in{b.obs, b.obs ? nullptr : b.cells};
+  int rc = net_forward_hidden(n, s, params, in, rows, Lr->err);
   if (rc) return rc;
 
   const int hl = d.dims[L - 1], al = d.dims[L];
@@ -577,6 +581,7 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
   if (which == 0) {
     hp.mode = kHeadActor;
     hp.mask = b.mask;
+    hp.cells = b.mask ? nullptr : b.cells;
     hp.q = b.q;
     hp.z_old = Lr->desc.use_kl ? b.logits_old : nullptr;
     hp.log_alpha = Lr->desc.use_kl ? log_alpha : nullptr;
@@ -597,16 +602,18 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
   *stats_parts = ghp;
 
   if (n.tc) {
-    rc = net_backward_tc(n, s, params, b.obs, rows, grads, red, Lr->err);
+    rc = net_backward_tc(n, s, params, in, rows, grads, red, Lr->err);
     if (rc) return rc;
     add_gap_segs(red, d, n.w_off, n.b_off, n.size, grads);
     return kOk;
   }
   int cur = 0;
   for (int l = L - 2; l >= 0; --l) {
-    const float* in = l == 0 ? b.obs : n.acts[l - 1];
+    const float* x = l == 0 ? b.obs : n.acts[l - 1];
     int parts = 0;
-    rc = gemm_dw(s, n.dw_part[l], in, n.dz[cur], rows, d.dims[l], d.dims[l + 1], &parts);
+    rc = l == 0 && in.cells
+             ? dw_skinny_launch(in, n.dz[cur], rows, d.dims[0], d.dims[1], n.dw_part[0], &parts, s)
+             : gemm_dw(s, n.dw_part[l], x, n.dz[cur], rows, d.dims[l], d.dims[l + 1], &parts);
     if (rc) return rc;
     add_seg(red, n.dw_part[l], grads + n.w_off[l], (int64_t)d.dims[l] * d.dims[l + 1],
             (int64_t)d.dims[l] * d.dims[l + 1], parts);
@@ -629,9 +636,11 @@ int learner_backward(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float 
   SPO_CHECK_ARG(b->rows >= 0 && b->rows <= Lr->desc.max_rows, kErrShape,
                 "batch rows " + std::to_string(b->rows) + " exceed the learner's max_rows " +
                     std::to_string(Lr->desc.max_rows));
-  SPO_CHECK_ARG(b->rows == 0 || b->obs != nullptr, kErrArg, "batch.obs is null");
+  SPO_CHECK_ARG(b->rows == 0 || b->obs != nullptr || b->cells != nullptr, kErrArg,
+                "batch.obs (or batch.cells) is null");
   if (Lr->net[0].present) {
-    SPO_CHECK_ARG(b->rows == 0 || (b->q && b->mask), kErrArg, "actor needs batch.q and batch.mask");
+    SPO_CHECK_ARG(b->rows == 0 || (b->q && (b->mask || (!b->obs && b->cells))), kErrArg,
+                  "actor needs batch.q and batch.mask (or batch.cells)");
     SPO_CHECK_ARG(b->rows == 0 || !Lr->desc.use_kl || b->logits_old, kErrArg,
                   "use_kl needs batch.logits_old");
   }
@@ -1183,7 +1192,7 @@ int spo_learner_forward(spo_learner_t learner, spo_stream_t stream, int32_t whic
   const NetPlan& n = learner->net[which];
   const float* p = params + n.offset;
   cudaStream_t s = S(stream);
-  int rc = net_forward_hidden(n, s, p, obs, rows, learner->err);
+  int rc = net_forward_hidden(n, s, p, LayerInput{obs, nullptr}, rows, learner->err);
   if (rc) return rc;
   const int L = n.d.num_layers;
   if (n.tc) {  // the last layer reads plain fp32: fold lo into hi (the cache is scratch here)

@@ -224,7 +224,8 @@ head_kernel(const HeadParams p) {
       } else {
         float mk = 1.f, qv = 0.f;
         if (lvalid) {
-          mk = p.mask ? __ldg(p.mask + row * A + la) : 1.f;
+          mk = p.mask ? __ldg(p.mask + row * A + la)
+                      : (p.cells ? (__ldg(p.cells + row * 9 + la) == 0.f ? 1.f : 0.f) : 1.f);
           qv = __ldg(p.q + row * A + la);
         }
         const float zm = (!lvalid || mk == 0.f) ? kNegInf : zv;

@@ -9,6 +9,11 @@
 // as one float4 per thread (2 KB contiguous per CTA), optionally as a TF32 hi/lo pair and
 // with the packed ReLU mask (bit j of word w = column 32 w + j).
 //
+// Both kernels can take board cells [rows x 9] (+1 agent / -1 rival / 0 empty) instead of
+// x: the cells are staged and expanded in shared memory into the 27-wide plane-major
+// [empty | agent | rival] rows (envs/tictactoe.mojo:449-480), the observation encoding
+// fused into the first layer's load stage.
+//
 // Weight gradient: dW[k x n] = x^T dY summed over rows, dY [rows x n].
 // CTA = 256 threads over one chunk of rows and 512 columns: thread t owns the 4 columns
 // 4 (t % 128) .. +3 of its column block and one half of the k features (t / 128), so its
@@ -30,6 +35,7 @@ constexpr int kMaxK = 32;
 constexpr int kHalf = kMaxK / 2;  // features per thread
 constexpr int kRows = 64;        // rows staged per block
 constexpr int kUnroll = 8;
+constexpr int kCells = 9;        // board cells per row (cells input)
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
@@ -43,7 +49,9 @@ __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
 // ahead of the one being consumed.
 struct XStage {
   float (*xs)[kRows][kMaxK];  // [2][kRows][kMaxK]
+  float (*cs)[kRows][kCells];  // [2][kRows][kCells] staged board cells (cells != null)
   const float* x;
+  const float* cells;
   int k;
   int64_t r_begin, r_end;
   __device__ void clear(int tid, int nthreads) {
@@ -54,22 +62,41 @@ struct XStage {
     const int64_t rb = r_begin + b * kRows;
     if (rb < r_end) {
       const int nr = (int)min((int64_t)kRows, r_end - rb);
-      float (*buf)[kMaxK] = xs[b & 1];
-      const float* src = x + rb * k;
-      for (int e = tid; e < nr * k; e += nthreads) {
-        const int r = e / k, i = e - r * k;
-        cp_async4(&buf[r][i], src + e);
+      if (cells) {
+        float* buf = &cs[b & 1][0][0];
+        const float* src = cells + rb * kCells;
+        for (int e = tid; e < nr * kCells; e += nthreads) cp_async4(buf + e, src + e);
+      } else {
+        float (*buf)[kMaxK] = xs[b & 1];
+        const float* src = x + rb * k;
+        for (int e = tid; e < nr * k; e += nthreads) {
+          const int r = e / k, i = e - r * k;
+          cp_async4(&buf[r][i], src + e);
+        }
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  // cells only: expand staged block b into its x rows (call between two barriers)
+  __device__ void expand(int64_t b, int nr, int tid, int nthreads) {
+    float (*dst)[kMaxK] = xs[b & 1];
+    const float* src = &cs[b & 1][0][0];
+    for (int e = tid; e < nr * kCells; e += nthreads) {
+      const int r = e / kCells, c = e - r * kCells;
+      const float v = src[e];
+      dst[r][c] = v == 0.f ? 1.f : 0.f;
+      dst[r][kCells + c] = v == 1.f ? 1.f : 0.f;
+      dst[r][2 * kCells + c] = v == -1.f ? 1.f : 0.f;
+    }
   }
   __device__ static void wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 };
 
 __global__ void __launch_bounds__(kThreads, 2)
-dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int64_t rows, int k, int64_t n,
-                 int64_t chunk, float* __restrict__ part) {
+dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, const float* __restrict__ dy,
+                 int64_t rows, int k, int64_t n, int64_t chunk, float* __restrict__ part) {
   __shared__ __align__(16) float xs2[2][kRows][kMaxK];
+  __shared__ __align__(16) float cs2[2][kRows][kCells];
   const int tid = threadIdx.x;
   const int half = tid / 128;
   const int64_t col = (int64_t)blockIdx.y * kCols + 4 * (tid % 128);
@@ -84,7 +111,7 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int6
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
 
-  XStage st{xs2, x, k, r_begin, r_end};
+  XStage st{xs2, cs2, x, cells, k, r_begin, r_end};
   st.clear(tid, kThreads);
   __syncthreads();
   st.issue(0, tid, kThreads);
@@ -94,6 +121,10 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int6
     st.issue(blk + 1, tid, kThreads);  // the buffer it fills was released by the last barrier
     XStage::wait_prev();
     __syncthreads();
+    if (cells) {
+      st.expand(blk, nr, tid, kThreads);
+      __syncthreads();
+    }
     float (*xs)[kMaxK] = xs2[blk & 1];
     if (col_ok) {
       for (int r0 = 0; r0 < nr; r0 += kUnroll) {
@@ -138,10 +169,11 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ dy, int6
 constexpr int kFwdThreads = 128;
 
 __global__ void __launch_bounds__(kFwdThreads, 3)
-fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
-                  int64_t rows, int k, int64_t n, int64_t chunk, float* __restrict__ y,
+fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, const float* __restrict__ w,
+                  const float* __restrict__ b, int64_t rows, int k, int64_t n, int64_t chunk, float* __restrict__ y,
                   float* __restrict__ y_lo, uint32_t* __restrict__ bits) {
   __shared__ __align__(16) float xs2[2][kRows][kMaxK];
+  __shared__ __align__(16) float cs2[2][kRows][kCells];
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t col = (int64_t)blockIdx.y * kCols + 4 * tid;
   const bool col_ok = col < n;
@@ -155,7 +187,7 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ w, cons
   const float4 bv = col_ok ? __ldg(reinterpret_cast<const float4*>(b + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
   const int64_t r_begin = (int64_t)blockIdx.x * chunk;
   const int64_t r_end = min(rows, r_begin + chunk);
-  XStage st{xs2, x, k, r_begin, r_end};
+  XStage st{xs2, cs2, x, cells, k, r_begin, r_end};
   st.clear(tid, kFwdThreads);
   __syncthreads();
   st.issue(0, tid, kFwdThreads);
@@ -165,6 +197,10 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ w, cons
     st.issue(blk + 1, tid, kFwdThreads);
     XStage::wait_prev();
     __syncthreads();
+    if (cells) {
+      st.expand(blk, nr, tid, kFwdThreads);
+      __syncthreads();
+    }
     float (*xs)[kMaxK] = xs2[blk & 1];
     for (int r = 0; r < nr; ++r) {
       // products summed in k order from zero, then the bias (the CUDA-core GEMM's order)
@@ -218,8 +254,9 @@ bool dw_skinny_ok(int64_t k, int64_t n) { return k >= 1 && k <= kMaxK && n >= 4 
 
 bool fwd_skinny_ok(int64_t k, int64_t n) { return k >= 1 && k <= kMaxK && n >= 4 && n % 4 == 0; }
 
-int fwd_skinny_launch(const float* x, const float* w, const float* b, int64_t rows, int64_t k, int64_t n,
+int fwd_skinny_launch(LayerInput in, const float* w, const float* b, int64_t rows, int64_t k, int64_t n,
                       float* y, float* y_lo, uint32_t* bits, cudaStream_t s) {
+  SPO_CHECK_ARG(!in.cells || k == 3 * kCells, kErrShape, "fwd_skinny: board cells need a 27-wide input layer");
   SPO_CHECK_ARG(fwd_skinny_ok(k, n), kErrUnsupported, "fwd_skinny: k <= 32 and n % 4 == 0");
   SPO_CHECK_ARG(aligned16(w) && aligned16(b) && aligned16(y) && (!y_lo || aligned16(y_lo)), kErrAlign,
                 "fwd_skinny: W, b and outputs must be 16-byte aligned");
@@ -229,7 +266,7 @@ int fwd_skinny_launch(const float* x, const float* w, const float* b, int64_t ro
   const int64_t want = std::max<int64_t>(1, 3LL * sm_count() / col_blocks);
   const int64_t chunk = std::max<int64_t>(kRows, ceil_div(ceil_div(rows, want), kRows) * kRows);
   dim3 grid((unsigned)ceil_div(rows, chunk), (unsigned)col_blocks);
-  fwd_skinny_kernel<<<grid, kFwdThreads, 0, s>>>(x, w, b, rows, (int)k, n, chunk, y, y_lo, bits);
+  fwd_skinny_kernel<<<grid, kFwdThreads, 0, s>>>(in.x, in.cells, w, b, rows, (int)k, n, chunk, y, y_lo, bits);
   SPO_LAUNCH_CHECK();
   return kOk;
 }
@@ -243,8 +280,9 @@ int64_t dw_skinny_chunk(int64_t rows, int64_t n) {
   return std::max<int64_t>(4 * kRows, ceil_div(ceil_div(std::max<int64_t>(rows, 1), want), kRows) * kRows);
 }
 
-int dw_skinny_launch(const float* x, const float* dy, int64_t rows, int64_t k, int64_t n, float* part,
+int dw_skinny_launch(LayerInput in, const float* dy, int64_t rows, int64_t k, int64_t n, float* part,
                      int* parts, cudaStream_t s) {
+  SPO_CHECK_ARG(!in.cells || k == 3 * kCells, kErrShape, "dw_skinny: board cells need a 27-wide input layer");
   SPO_CHECK_ARG(dw_skinny_ok(k, n), kErrUnsupported, "dw_skinny: k <= 32 and n % 4 == 0");
   SPO_CHECK_ARG(aligned16(dy) && aligned16(part), kErrAlign, "dw_skinny: dY and part must be 16-byte aligned");
   const int64_t chunk = dw_skinny_chunk(rows, n);
@@ -252,7 +290,7 @@ int dw_skinny_launch(const float* x, const float* dy, int64_t rows, int64_t k, i
   if (parts) *parts = (int)p;
   if (p == 0) return kOk;
   dim3 grid((unsigned)p, (unsigned)ceil_div(n, kCols));
-  dw_skinny_kernel<<<grid, kThreads, 0, s>>>(x, dy, rows, (int)k, n, chunk, part);
+  dw_skinny_kernel<<<grid, kThreads, 0, s>>>(in.x, in.cells, dy, rows, (int)k, n, chunk, part);
   SPO_LAUNCH_CHECK();
   return kOk;
 }

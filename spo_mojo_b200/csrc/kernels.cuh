@@ -30,6 +30,7 @@ struct HeadParams {
   int mode;                // kHeadActor / kHeadCritic
   int rows_per_tile;       // set by head_launch
   const float* mask;       // actor: [M x A] 1 legal / 0 illegal (null: all legal)
+  const float* cells;      // actor, mask null: board cells [M x 9]; legal = empty (0)
   const float* q;          // actor: [M x A] target policy
   const float* z_old;      // actor: [M x A] pi_old logits, or null (no KL term)
   const float* log_alpha;  // actor: device scalar, or null (use alpha_host)
@@ -128,17 +129,24 @@ int value_grad_launch(float* dv, const float* v, const float* t, int64_t n, floa
 int relu_launch(float* a, int64_t n, cudaStream_t s);
 int relu_bwd_launch(float* g, const float* act, int64_t n, cudaStream_t s);
 // part[c][n] = sum of rows [c*per, (c+1)*per) of x [rows x n], per = ceil(rows / chunks).
+// Rows of a first layer's input: x [rows x k] fp32, or (x null) board cells [rows x 9]
+// coded +1 agent / -1 rival / 0 empty, read as the 27-wide [empty | agent | rival] planes.
+struct LayerInput {
+  const float* x;
+  const float* cells;
+};
+
 // y = relu(x W + b) for inputs at most 32 wide (input_layer.cu): y fp32, or a TF32 hi/lo
 // pair (y = hi) when y_lo is set; bits (optional): packed y > 0, [rows x n/32] words.
 bool fwd_skinny_ok(int64_t k, int64_t n);
-int fwd_skinny_launch(const float* x, const float* w, const float* b, int64_t rows, int64_t k, int64_t n,
+int fwd_skinny_launch(LayerInput in, const float* w, const float* b, int64_t rows, int64_t k, int64_t n,
                       float* y, float* y_lo, uint32_t* bits, cudaStream_t s);
 
 // dW = x^T dY for inputs at most 32 wide (input_layer.cu): per-chunk partials
 // part[chunk][k x n], *parts chunks (at most dw_skinny_max_parts()).
 bool dw_skinny_ok(int64_t k, int64_t n);
 int64_t dw_skinny_max_parts();
-int dw_skinny_launch(const float* x, const float* dy, int64_t rows, int64_t k, int64_t n, float* part,
+int dw_skinny_launch(LayerInput in, const float* dy, int64_t rows, int64_t k, int64_t n, float* part,
                      int* parts, cudaStream_t s);
 
 int colsum_part_launch(const float* x, int64_t rows, int64_t n, int64_t chunks, float* part,

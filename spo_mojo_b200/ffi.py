@@ -85,7 +85,7 @@ class LearnerLayout(ctypes.Structure):
 class Batch(ctypes.Structure):
     _fields_ = [("obs", ctypes.c_void_p), ("mask", ctypes.c_void_p), ("q", ctypes.c_void_p),
                 ("logits_old", ctypes.c_void_p), ("target", ctypes.c_void_p),
-                ("rows", ctypes.c_int64)]
+                ("rows", ctypes.c_int64), ("cells", ctypes.c_void_p)]
 
 
 class TrainState(ctypes.Structure):

@@ -164,14 +164,16 @@ class Learner:
 
     # ------------------------------------------------------------ the step
     def _batch(self, batch, rows=None):
-        rows = int(batch["obs"].shape[0]) if rows is None else int(rows)
+        """Batch dict -> spo_batch. Inputs: "obs" [rows x d0], or "cells" [rows x 9] board
+        cells (+1 agent / -1 rival / 0 empty) encoded on the fly (then "mask" may be left
+        out: the legal mask is the empty cells); "mask", "q", "logits_old" (actor),
+        "target" (critic)."""
         g = batch.get
-        return ffi.Batch(g("obs").data_ptr(),
-                         g("mask").data_ptr() if g("mask") is not None else None,
-                         g("q").data_ptr() if g("q") is not None else None,
-                         g("logits_old").data_ptr() if g("logits_old") is not None else None,
-                         g("target").data_ptr() if g("target") is not None else None,
-                         rows)
+        first = g("obs") if g("obs") is not None else g("cells")
+        rows = int(first.shape[0]) if rows is None else int(rows)
+        ptr = lambda k: g(k).data_ptr() if g(k) is not None else None  # noqa: E731
+        return ffi.Batch(ptr("obs"), ptr("mask"), ptr("q"), ptr("logits_old"), ptr("target"), rows,
+                         ptr("cells"))
 
     def backward(self, batch, grad_scale=None, stream=None):
         b = self._batch(batch)

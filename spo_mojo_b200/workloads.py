@@ -176,6 +176,13 @@ def make_boards(rng, rows):
     return obs, mask
 
 
+def cells_of(obs):
+    """Board cells [rows, 9] coded +1 (X, the agent's plane) / -1 (O) / 0 (empty) from the
+    three-plane observation; the inverse of the encoding the learner applies to cells."""
+    obs = np.asarray(obs)
+    return (obs[:, 9:18] - obs[:, 18:27]).astype(np.float32)
+
+
 def make_q(rng, mask, concentration=0.3):
     """Dirichlet(concentration) over the legal cells (normalised gammas), 0 elsewhere."""
     g = rng.gamma(concentration, 1.0, size=mask.shape) * mask

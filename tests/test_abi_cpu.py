@@ -23,7 +23,7 @@ def test_library_loads_and_exports_every_declared_symbol():
                          text=True).stdout
     exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
     assert exported == set(declared), exported ^ set(declared)
-    assert L.spo_abi_version() == 2
+    assert L.spo_abi_version() == 3
 
 
 @pytest.mark.parametrize("dims", [(27, 128, 128, 9), (27, 512, 512, 512, 1), (18, 5, 3), (4, 5, 5, 1)])
