@@ -260,6 +260,8 @@ def count_launches(wl, clip, engine="tensor"):
         hidden = net.dims[1:-1]
         if engine == "tensor" and L >= 3 and all(h % 128 == 0 and h <= 1024 for h in hidden):
             n += L - 2                           # per-step TF32 split of the hidden weights
+            if net.dims[0] <= 32 and net.dims[1] % 128 == 0:
+                n += 2                           # first layer on tensor cores: pad/split x and W0
     return n + 1 + 1 + (1 if clip else 0)      # reduce, adam, sum of squares
 
 

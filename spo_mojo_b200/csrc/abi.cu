@@ -241,6 +241,11 @@ struct NetPlan {
   float* dz[2] = {};                    // ping-pong [rows x max_hidden] (hi in TC mode)
   float* dz_lo[2] = {};                 // TC mode
   float* dz0 = nullptr;                 // TC mode: [rows x d_1] fp32
+  // TC mode with a first layer at most 32 wide and d_1 % 128 == 0: that layer's forward
+  // runs on tensor cores too, from the input padded to 32 columns (hi/lo) and W_0^T padded
+  bool tc0 = false;
+  float* x0[2] = {};                    // [rows x 32] hi, lo
+  float* w0t[2] = {};                   // [d_1 x 32] hi, lo
   float* wsplit[SPO_MAX_LAYERS][4] = {};  // TC mode, hidden l: W^T hi, W^T lo, W hi, W lo
   float* head_dw = nullptr;          // [Gh][d_{L-1} x d_L]
   float* head_db = nullptr;          // [Gh][d_L]
@@ -319,6 +324,11 @@ void carve_net(NetPlan& n, Carve& c, int64_t rows) {
   }
   if (n.tc) {
     n.dz0 = c.take<float>((size_t)rows * d.dims[1]);
+    if (n.tc0)
+      for (int k = 0; k < 2; ++k) {
+        n.x0[k] = c.take<float>((size_t)rows * 32);
+        n.w0t[k] = c.take<float>((size_t)d.dims[1] * 32);
+      }
     for (int l = 1; l + 1 < L; ++l)
       for (int k = 0; k < 4; ++k) n.wsplit[l][k] = c.take<float>((size_t)d.dims[l] * d.dims[l + 1]);
   }
@@ -388,6 +398,7 @@ int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* b
     off += n.size;
     for (int l = 1; l < d.num_layers; ++l) n.max_hidden = std::max<int64_t>(n.max_hidden, d.dims[l]);
     n.tc = net_uses_tc(d, desc->engine);
+    n.tc0 = n.tc && d.dims[0] <= 32 && d.dims[1] % 128 == 0;
   }
   spo_learner_layout& lay = L->layout;
   lay.actor_offset = L->net[0].offset;
@@ -455,11 +466,36 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
                                   n.wsplit[l][1], n.wsplit[l][2], n.wsplit[l][3], s);
     if (rc) return rc;
   }
-  int rc = fwd_skinny_ok(d.dims[0], d.dims[1])
-               ? fwd_skinny_launch(in, params + n.w_off[0], params + n.b_off[0], rows, d.dims[0], d.dims[1],
-                                   n.acts[0], n.acts_lo[0], n.acts_bits[0], s)
-               : gemm_fwd_split(s, n.acts[0], n.acts_lo[0], in.x, params + n.w_off[0], params + n.b_off[0],
-                                rows, d.dims[0], d.dims[1]);
+  int rc;
+  if (n.tc0) {
+    rc = split_weights_t_pad_launch(params + n.w_off[0], d.dims[0], d.dims[1], n.w0t[0], n.w0t[1], s);
+    if (rc) return rc;
+    rc = pad_split_input_launch(in, d.dims[0], rows, n.x0[0], n.x0[1], s);
+    if (rc) return rc;
+    if (rows > 0) {
+      TcGemmArgs a{};
+      a.kind = TC_FWD;
+      a.a_hi = n.x0[0];
+      a.a_lo = n.x0[1];
+      a.b_hi = n.w0t[0];
+      a.b_lo = n.w0t[1];
+      a.M = rows;
+      a.N = d.dims[1];
+      a.K = 32;
+      a.bias = params + n.b_off[0];
+      a.c_hi = n.acts[0];
+      a.c_lo = n.acts_lo[0];
+      a.c_bits = n.acts_bits[0];
+      a.err = err;
+      rc = tc_gemm_launch(a, s);
+    }
+  } else {
+    rc = fwd_skinny_ok(d.dims[0], d.dims[1])
+             ? fwd_skinny_launch(in, params + n.w_off[0], params + n.b_off[0], rows, d.dims[0], d.dims[1],
+                                 n.acts[0], n.acts_lo[0], n.acts_bits[0], s)
+             : gemm_fwd_split(s, n.acts[0], n.acts_lo[0], in.x, params + n.w_off[0], params + n.b_off[0],
+                              rows, d.dims[0], d.dims[1]);
+  }
   if (rc) return rc;
   if (rows == 0) return kOk;
   for (int l = 1; l + 1 < d.num_layers; ++l) {

@@ -36,6 +36,7 @@ constexpr int kHalf = kMaxK / 2;  // features per thread
 constexpr int kRows = 64;        // rows staged per block
 constexpr int kUnroll = 8;
 constexpr int kCells = 9;        // board cells per row (cells input)
+constexpr int kPadK = 32;        // input width of the first layer on tensor cores
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
@@ -248,11 +249,68 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, 
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// Tensor-core operands of the first layer: the input rows padded to kPadK columns as TF32
+// hi/lo pairs (zeros past k), and W^T [n x kPadK] likewise. One thread per element.
+__global__ void pad_split_input_kernel(const float* __restrict__ x, const float* __restrict__ cells, int k,
+                                       int64_t rows, float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < rows * kPadK; e += gs) {
+    const int64_t r = e / kPadK;
+    const int c = (int)(e - r * kPadK);
+    float v = 0.f;
+    if (c < k) {
+      if (cells) {
+        const int cell = c % kCells, plane = c / kCells;
+        const float cv = __ldg(cells + r * kCells + cell);
+        v = (plane == 0 ? cv == 0.f : (plane == 1 ? cv == 1.f : cv == -1.f)) ? 1.f : 0.f;
+      } else {
+        v = __ldg(x + r * k + c);
+      }
+    }
+    float h, l;
+    tf32_split(v, h, l);
+    hi[e] = h;
+    lo[e] = l;
+  }
+}
+
+__global__ void split_weights_t_pad_kernel(const float* __restrict__ w, int k, int64_t n, float* __restrict__ wt_hi,
+                                           float* __restrict__ wt_lo) {
+  const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n * kPadK; e += gs) {
+    const int64_t col = e / kPadK;
+    const int i = (int)(e - col * kPadK);
+    const float v = i < k ? __ldg(w + (int64_t)i * n + col) : 0.f;
+    float h, l;
+    tf32_split(v, h, l);
+    wt_hi[e] = h;
+    wt_lo[e] = l;
+  }
+}
+
 }  // namespace
 
 bool dw_skinny_ok(int64_t k, int64_t n) { return k >= 1 && k <= kMaxK && n >= 4 && n % 4 == 0; }
 
 bool fwd_skinny_ok(int64_t k, int64_t n) { return k >= 1 && k <= kMaxK && n >= 4 && n % 4 == 0; }
+
+int pad_split_input_launch(LayerInput in, int64_t k, int64_t rows, float* hi, float* lo, cudaStream_t s) {
+  SPO_CHECK_ARG(k >= 1 && k <= kPadK, kErrUnsupported, "pad_split_input: input wider than 32");
+  SPO_CHECK_ARG(!in.cells || k == 3 * kCells, kErrShape, "pad_split_input: board cells need a 27-wide input");
+  if (rows <= 0) return kOk;
+  const int grid = (int)std::min<int64_t>(ceil_div(rows * kPadK, 256), 8LL * sm_count());
+  pad_split_input_kernel<<<grid, 256, 0, s>>>(in.x, in.cells, (int)k, rows, hi, lo);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
+
+int split_weights_t_pad_launch(const float* w, int64_t k, int64_t n, float* wt_hi, float* wt_lo, cudaStream_t s) {
+  SPO_CHECK_ARG(k >= 1 && k <= kPadK && n >= 1, kErrUnsupported, "split_weights_t_pad: bad shape");
+  const int grid = (int)std::min<int64_t>(ceil_div(n * kPadK, 256), 8LL * sm_count());
+  split_weights_t_pad_kernel<<<grid, 256, 0, s>>>(w, (int)k, n, wt_hi, wt_lo);
+  SPO_LAUNCH_CHECK();
+  return kOk;
+}
 
 int fwd_skinny_launch(LayerInput in, const float* w, const float* b, int64_t rows, int64_t k, int64_t n,
                       float* y, float* y_lo, uint32_t* bits, cudaStream_t s) {
