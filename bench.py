@@ -59,6 +59,8 @@ def parse():
                     help="tensor: tcgen05 3xTF32 for the hidden layers; cuda: fp32 FMA everywhere")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the global batch (profiling of small cases only; not a bench line)")
+    ap.add_argument("--peaks", action="store_true",
+                    help="measure the tcgen05 TF32 and FP32-FMA peaks of this GPU (not a bench line) and exit")
     return ap.parse_args()
 
 
@@ -237,6 +239,11 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
         # 3xTF32 issues three TF32 MMAs per fp32 product; TF32 runs at half the bf16 rate
         roof["tf32_mma_tflops"] = 3 * achieved
         roof["tf32_frac_of_half_bf16_peak"] = 3 * achieved / (peak / 2)
+        # and against the TF32 MMA rate measured live on this GPU (spo_measure_peaks)
+        t, f = ctypes.c_double(), ctypes.c_double()
+        ffi.call("spo_measure_peaks", stream.cuda_stream, ctypes.byref(t), ctypes.byref(f))
+        roof["tf32_mma_peak_measured_tflops"] = t.value / 1e12
+        roof["frac_of_measured_3xtf32_ceiling"] = 3 * achieved / (t.value / 1e12)
     return roof
 
 
@@ -413,8 +420,36 @@ def run_ours(args):
     return 0
 
 
+def run_peaks():
+    """The compute peaks the learner's two arithmetic paths run against (spo_measure_peaks),
+    next to the driver-measured HBM and bf16 figures."""
+    import ctypes
+    import torch
+    from spo_mojo_b200 import ffi
+    torch.cuda.set_device(0)
+    tf32, fp32 = ctypes.c_double(), ctypes.c_double()
+    rows = []
+    clocks = ClockSampler(0)
+    clocks.start()
+    for _ in range(3):
+        ffi.call("spo_measure_peaks", torch.cuda.current_stream().cuda_stream, ctypes.byref(tf32), ctypes.byref(fp32))
+        rows.append((tf32.value, fp32.value))
+    clk = clocks.stop()
+    pk, kind = peaks()
+    print(json.dumps({"peaks": {
+        "tf32_tcgen05_tflops": max(r[0] for r in rows) / 1e12,
+        "fp32_ffma2_tflops": max(r[1] for r in rows) / 1e12,
+        "three_tf32_fp32_equivalent_tflops": max(r[0] for r in rows) / 3e12,
+        "hbm_gbs": pk.get("hbm_gbs"), "bf16_tflops": pk.get("bf16_tflops"),
+        "bf16_tflops_sustained": pk.get("bf16_tflops_sustained"), "peaks_source": kind,
+        "clocks": clk}}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.peaks:
+        return run_peaks()
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

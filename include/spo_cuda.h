@@ -224,6 +224,13 @@ SPO_API int spo_truncated_gae(spo_stream_t stream, float* adv, float* targets, c
                       const float* discount, const float* v_tm1, const float* v_t,
                       const float* truncation, int64_t batch, int32_t t_len, float lambda);
 
+/* ------------------------------------------------------------------ compute peaks
+ * No reference counterpart. Measured peaks of the two arithmetic paths of this library on
+ * the current device: tf32_flops = tcgen05.mma.kind::tf32 128x128x8 issued back to back
+ * from shared memory, one CTA per SM; fp32_flops = packed FFMA2 chains on every SM.
+ * FLOP/s; a few tens of ms of GPU time. */
+SPO_API int spo_measure_peaks(spo_stream_t stream, double* tf32_flops, double* fp32_flops);
+
 /* ------------------------------------------------------------------ replay buffer, device side
  * TrajectoryBuffer.sample_indices rl_utils/buffer.mojo:138-152: idx[i] =
  * rand_bits(seed, stream_id, i) % count (ops/rng.mojo:43-58), i < n, with replacement.

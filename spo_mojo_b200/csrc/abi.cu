@@ -1113,6 +1113,11 @@ int spo_truncated_gae(spo_stream_t stream, float* adv, float* targets, const flo
                     S(stream));
 }
 
+int spo_measure_peaks(spo_stream_t stream, double* tf32_flops, double* fp32_flops) {
+  SPO_CHECK_ARG(tf32_flops && fp32_flops, kErrArg, "null output");
+  return measure_peaks(tf32_flops, fp32_flops, S(stream));
+}
+
 int spo_replay_sample(spo_stream_t stream, int32_t* idx, int64_t n, int64_t count, uint32_t seed,
                       uint32_t stream_id) {
   return replay_sample_launch(idx, n, count, seed, stream_id, S(stream));

@@ -27,6 +27,10 @@
 //      accumulating the column sums of dX (the bias gradient of the layer below).
 // Partial sums (dW, db, column sums, loss statistics) go to per-CTA slots that a
 // deterministic reduction adds up.
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "spo_common.cuh"
 #include "kernels.cuh"
 
@@ -43,6 +47,12 @@ __host__ __device__ constexpr int padded_actions() { return A == 1 ? 1 : (A + 3)
 
 __device__ __forceinline__ float softplus_f(float x) {
   return log1pf(expf(-fabsf(x))) + fmaxf(x, 0.f);
+}
+
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
 }
 
 __device__ __forceinline__ void cp_async16(float* dst, const float* src) {
@@ -72,10 +82,14 @@ head_kernel(const HeadParams p) {
   const int R = p.rows_per_tile;
   const bool has_lo = p.act_lo != nullptr;
   float* Ws = sm;                          // [H][AP]
-  float* ahi = Ws + H * AP;                // [R][H] (act; hi + lo after phase 2)
-  float* alo = ahi + R * H;                // [R][H] lo halves
-  float* dzs = alo + (has_lo ? R * H : 0);  // [R][AP]
+  // two tile buffers: the copies of the next tile land while this one is computed
+  float* abuf = Ws + H * AP;               // [2][R][H] (act; hi + lo after phase 2)
+  float* lbuf = abuf + 2 * R * H;          // [2][R][H] lo halves
+  float* dzs = lbuf + (has_lo ? 2 * R * H : 0);  // [R][AP]
   float* red = dzs + R * AP;               // [kNW][AP + kStats]
+  // per-row loss inputs of the two tile buffers, copied with the activations:
+  // [2][3][R][A] = (q or critic target, mask or board cells, pi_old logits)
+  float* rinb = red + kNW * (AP + kStats);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -110,21 +124,47 @@ head_kernel(const HeadParams p) {
   for (int s = 0; s < kStats; ++s) st[s] = 0.f;
 
   const int64_t tiles = (p.M + R - 1) / R;
-  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int64_t r0 = t * R;
-    const int rows = (int)min((int64_t)R, p.M - r0);
-    __syncthreads();  // previous tile fully consumed (and W staged, first time)
-    {
-      const int n4 = rows * H / 4;
+  // copies of tile t into buffer b (an empty group past the last tile)
+  auto issue = [&](int64_t t, int b) {
+    if (t < tiles) {
+      const int64_t r0 = t * R;
+      const int n4 = (int)min((int64_t)R, p.M - r0) * H / 4;
       const float* src = p.act + r0 * H;
-      for (int i = tid; i < n4; i += kHeadThreads) cp_async16(ahi + 4 * i, src + 4 * i);
+      float* dst = abuf + b * R * H;
+      for (int i = tid; i < n4; i += kHeadThreads) cp_async16(dst + 4 * i, src + 4 * i);
       if (has_lo) {
         const float* slo = p.act_lo + r0 * H;
-        for (int i = tid; i < n4; i += kHeadThreads) cp_async16(alo + 4 * i, slo + 4 * i);
+        float* dlo = lbuf + b * R * H;
+        for (int i = tid; i < n4; i += kHeadThreads) cp_async16(dlo + 4 * i, slo + 4 * i);
       }
-      asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+      const int ne = (int)min((int64_t)R, p.M - r0) * A;
+      float* base = rinb + b * 3 * R * A;
+      const float* s0 = p.mode == kHeadCritic ? p.target : p.q;
+      const float* s1 = p.mode == kHeadCritic ? nullptr : (p.mask ? p.mask : p.cells);
+      const float* s2 = p.mode == kHeadCritic ? nullptr : p.z_old;
+      for (int e = tid; e < ne; e += kHeadThreads) {
+        cp_async4(base + e, s0 + r0 * A + e);
+        if (s1) cp_async4(base + R * A + e, s1 + r0 * A + e);  // cells rows are 9 wide = A
+        if (s2) cp_async4(base + 2 * R * A + e, s2 + r0 * A + e);
+      }
     }
-    __syncthreads();
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  issue(blockIdx.x, 0);
+  int it = 0;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+    const int64_t r0 = t * R;
+    const int rows = (int)min((int64_t)R, p.M - r0);
+    // buffer (it + 1) & 1 was released by the barrier that ended the previous tile
+    issue(t + gridDim.x, (it + 1) & 1);
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();  // this tile's copies (every thread's) have landed; W staged
+    float* ahi = abuf + (it & 1) * R * H;
+    const float* alo = lbuf + (it & 1) * R * H;
+    const float* rq = rinb + (it & 1) * 3 * R * A;  // q (actor) / target (critic)
+    const float* rm = rq + R * A;                   // mask, or board cells
+    const float* rz = rq + 2 * R * A;               // pi_old logits
+    const bool from_cells = !p.mask && p.cells;
 
     // 2. One warp per row: logits, loss, dz.
     for (int r = warp; r < rows; r += kNW) {
@@ -145,18 +185,18 @@ head_kernel(const HeadParams p) {
         if (lane == 0) {
           float dz;
           if (p.mode == kHeadCritic) {
-            const float d = z - __ldg(p.target + row);
+            const float d = z - rq[r];
             dz = d * p.scale;
             st[kStatCriticLoss] += 0.5f * d * d * p.scale;
           } else {
             // one action: pi = 1 where legal, log pi = 0
-            const float mk = p.mask ? __ldg(p.mask + row) : 1.f;
-            const float qv = __ldg(p.q + row);
+            const float mk = p.mask ? rm[r] : (from_cells ? (rm[r] == 0.f ? 1.f : 0.f) : 1.f);
+            const float qv = rq[r];
             const float zm = mk == 0.f ? kNegInf : z;
             const float e = expf(zm - zm), pi = e / e, lp = zm - (zm + logf(e));
             float po = 0.f, klo = 0.f;
             if (p.z_old != nullptr) {
-              const float zo = mk == 0.f ? kNegInf : __ldg(p.z_old + row);
+              const float zo = mk == 0.f ? kNegInf : rz[r];
               const float eo = expf(zo - zo);
               po = eo / eo;
               if (po > 0.f) klo = po * ((zo - (zo + logf(eo))) - lp);
@@ -213,7 +253,7 @@ head_kernel(const HeadParams p) {
       float dz = 0.f;
       if (p.mode == kHeadCritic) {
         if (lvalid) {
-          const float d = zv - __ldg(p.target + row * A + la);
+          const float d = zv - rq[r * A + la];
           dz = d * p.scale;
           const float l2 = half_sum(0.5f * d * d * p.scale);
           if (lane == 0) st[kStatCriticLoss] += l2;
@@ -224,9 +264,9 @@ head_kernel(const HeadParams p) {
       } else {
         float mk = 1.f, qv = 0.f;
         if (lvalid) {
-          mk = p.mask ? __ldg(p.mask + row * A + la)
-                      : (p.cells ? (__ldg(p.cells + row * 9 + la) == 0.f ? 1.f : 0.f) : 1.f);
-          qv = __ldg(p.q + row * A + la);
+          const float m = rm[r * A + la];
+          mk = p.mask ? m : (from_cells ? (m == 0.f ? 1.f : 0.f) : 1.f);
+          qv = rq[r * A + la];
         }
         const float zm = (!lvalid || mk == 0.f) ? kNegInf : zv;
         const float mx = half_max(zm);
@@ -238,7 +278,7 @@ head_kernel(const HeadParams p) {
         const float lp = zm - lse;
         float po = 0.f, klo_t = 0.f;
         if (p.z_old != nullptr) {
-          const float zo = (!lvalid || mk == 0.f) ? kNegInf : __ldg(p.z_old + row * A + la);
+          const float zo = (!lvalid || mk == 0.f) ? kNegInf : rz[r * A + la];
           const float mxo = half_max(zo);
           const float eo = lvalid ? expf(zo - mxo) : 0.f;
           const float so = half_sum(eo);
@@ -309,7 +349,9 @@ head_kernel(const HeadParams p) {
         dbx[j] += g;
       }
     }
+    __syncthreads();  // the tile's buffer and dzs are free for the next copies / rows
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 
   // Per-CTA partials.
   const int64_t cta = blockIdx.x;
@@ -346,7 +388,20 @@ int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
   void (*k)(const HeadParams);
   const int nj = (p.H + kHeadThreads - 1) / kHeadThreads;
   k = nj <= 1 ? head_kernel<A, 1> : (nj == 2 ? head_kernel<A, 2> : head_kernel<A, 4>);
-  SPO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // opt in once per device and instantiation to the largest size any H needs, so that no
+  // attribute call happens while a stream is being captured into a graph
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> opted;
+  int dev = 0;
+  SPO_CUDA_TRY(cudaGetDevice(&dev));
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!opted.count({dev, (const void*)k})) {
+      SPO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)head_smem_bytes(kHeadThreads * kHeadMaxHJ, A)));
+      opted.insert({dev, (const void*)k});
+    }
+  }
   k<<<grid, kHeadThreads, smem, s>>>(p);
   SPO_LAUNCH_CHECK();
   return kOk;
@@ -354,12 +409,14 @@ int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
 
 }  // namespace
 
-int head_rows_per_tile(int H) { return H > 512 ? 8 : (H > 256 ? 16 : 32); }
+// 4096 activations per tile buffer (16 KB hi + 16 KB lo, double-buffered): two CTAs per SM
+int head_rows_per_tile(int H) { return std::max(1, 4096 / H); }
 
 size_t head_smem_bytes(int H, int A) {
   const int R = head_rows_per_tile(H);
   const int AP = A == 1 ? 1 : (A + 3) & ~3;
-  return sizeof(float) * ((size_t)H * AP + 2 * (size_t)R * H + (size_t)R * AP + (size_t)kNW * (AP + kStats));
+  return sizeof(float) * ((size_t)H * AP + 4 * (size_t)R * H + (size_t)R * AP + (size_t)kNW * (AP + kStats) +
+                          6 * (size_t)R * A);
 }
 
 int head_grid(int64_t M, int H) {
@@ -375,6 +432,7 @@ int head_launch(HeadParams p, int grid, cudaStream_t s) {
                 "head: activations must be 16-byte aligned");
   SPO_CHECK_ARG(!p.dX_lo || p.dX, kErrArg, "head: dX_lo needs dX");
   SPO_CHECK_ARG(p.A == 1 || p.A == 9, kErrUnsupported, "head: output width must be 1 or 9");
+  SPO_CHECK_ARG(!p.cells || p.mask || p.A == 9, kErrUnsupported, "head: board cells need 9 actions");
   SPO_CHECK_ARG(p.mode == kHeadCritic ? p.target != nullptr : p.q != nullptr, kErrArg,
                 "head: missing loss inputs");
   p.rows_per_tile = head_rows_per_tile(p.H);

@@ -106,11 +106,11 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
   const int64_t r_end = min(rows, r_begin + chunk);
   const int i0 = half * kHalf;
 
-  float acc[kHalf][4];
+  // columns (0, 1) and (2, 3) of each feature as packed pairs: one FFMA2 (two fp32 fma.rn,
+  // the same results as fmaf) per pair
+  float2 acc[kHalf][2];
 #pragma unroll
-  for (int i = 0; i < kHalf; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int i = 0; i < kHalf; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
 
   XStage st{xs2, cs2, x, cells, k, r_begin, r_end};
   st.clear(tid, kThreads);
@@ -141,13 +141,12 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
           for (int c = 0; c < kHalf / 4; ++c) {
             const float4 xv = xr[c];
             const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+            const float2 g01 = make_float2(g[u].x, g[u].y), g23 = make_float2(g[u].z, g[u].w);
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-              float* a = acc[4 * c + t];
-              a[0] = fmaf(xa[t], g[u].x, a[0]);
-              a[1] = fmaf(xa[t], g[u].y, a[1]);
-              a[2] = fmaf(xa[t], g[u].z, a[2]);
-              a[3] = fmaf(xa[t], g[u].w, a[3]);
+              const float2 xx = make_float2(xa[t], xa[t]);
+              acc[4 * c + t][0] = __ffma2_rn(xx, g01, acc[4 * c + t][0]);
+              acc[4 * c + t][1] = __ffma2_rn(xx, g23, acc[4 * c + t][1]);
             }
           }
         }
@@ -163,7 +162,7 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
     const int f = i0 + i;
     if (f < k)
       *reinterpret_cast<float4*>(out + (int64_t)f * n + col) =
-          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+          make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
   }
 }
 

@@ -156,6 +156,9 @@ int dw_skinny_launch(LayerInput in, const float* dy, int64_t rows, int64_t k, in
 
 int colsum_part_launch(const float* x, int64_t rows, int64_t n, int64_t chunks, float* part,
                        cudaStream_t s);
+// peaks.cu: measured TF32 tensor and FP32 FMA peaks (FLOP/s)
+int measure_peaks(double* tf32_flops, double* fp32_flops, cudaStream_t s);
+
 // replay.cu: replay sampling / gather and observation encoding
 int replay_sample_launch(int32_t* idx, int64_t n, int64_t count, uint32_t seed, uint32_t stream,
                          cudaStream_t s);

@@ -136,6 +136,7 @@ SIGNATURES = {
     "spo_adam_flat": (INT, [P, P, P, P, P, I64, F, F, F, F, I32, F]),
     "spo_ema": (INT, [P, P, P, I64, F]),
     "spo_truncated_gae": (INT, [P, P, P, P, P, P, P, P, I64, I32, F]),
+    "spo_measure_peaks": (INT, [P, P, P]),
     "spo_replay_sample": (INT, [P, P, I64, I64, ctypes.c_uint32, ctypes.c_uint32]),
     "spo_replay_gather": (INT, [P, P, P, P, I64, I64, I64, P]),
     "spo_encode_obs": (INT, [P, P, P, P, I64]),

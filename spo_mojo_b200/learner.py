@@ -190,6 +190,24 @@ class Learner:
         s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
         ffi.call("spo_learner_step", self._h, s, ctypes.byref(b), ctypes.byref(self._state))
 
+    def capture_step(self, batch, warmup=1):
+        """Record one learner step on `batch` (fixed device tensors) as a CUDA graph; each
+        `graph.replay()` then runs the whole step (every kernel, the device-side Adam step
+        counter included) with one launch. Refill the batch tensors in place between
+        replays. The step's kernels neither allocate nor synchronise, so the graph holds
+        only libspo_cuda launches."""
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):  # first launches set kernel attributes outside the capture
+                self.step(batch, stream=side)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.step(batch)
+        return graph
+
     def forward(self, which, obs, mask=None, stream=None):
         """Inference forward of one network: (logits or V, pi or None)."""
         dims = self.actor_dims if which == "actor" else self.critic_dims
