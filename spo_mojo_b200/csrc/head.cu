@@ -106,7 +106,8 @@ head_kernel(const HeadParams p) {
 
   // Thread-owned columns h = tid + 256 j.
   float wreg[NJ][A];
-  float dw[NJ][A];
+  constexpr int A2 = (A + 1) / 2;  // action pairs of dW (packed FFMA2)
+  float2 dw[NJ][A2];
   float dbx[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
@@ -115,7 +116,7 @@ head_kernel(const HeadParams p) {
 #pragma unroll
     for (int a = 0; a < A; ++a) {
       wreg[j][a] = h < H ? __ldg(p.W + (int64_t)h * A + a) : 0.f;
-      dw[j][a] = 0.f;
+      if (a < A2) dw[j][a] = make_float2(0.f, 0.f);
     }
   }
   float dbl = 0.f;  // db of action la (A == 9) or of the output (A == 1, lane 0)
@@ -218,24 +219,30 @@ head_kernel(const HeadParams p) {
           dbl += dz;
         }
       } else {
-      float zp[16];
+      // action pairs as packed FFMA2 (two fp32 fma.rn each: the fmaf results)
+      float2 zp2[8];
 #pragma unroll
-      for (int a = 0; a < 16; ++a) zp[a] = 0.f;
+      for (int a = 0; a < 8; ++a) zp2[a] = make_float2(0.f, 0.f);
       for (int h = lane; h < H; h += 32) {
         float av = arow[h];
         if (has_lo) {
           av += lrow[h];
           arow[h] = av;
         }
+        const float2 aa = make_float2(av, av);
         const float4* w4 = reinterpret_cast<const float4*>(Ws + h * AP);
 #pragma unroll
         for (int c = 0; c < AP / 4; ++c) {
           const float4 w = w4[c];
-          zp[4 * c] = fmaf(av, w.x, zp[4 * c]);
-          zp[4 * c + 1] = fmaf(av, w.y, zp[4 * c + 1]);
-          zp[4 * c + 2] = fmaf(av, w.z, zp[4 * c + 2]);
-          zp[4 * c + 3] = fmaf(av, w.w, zp[4 * c + 3]);
+          zp2[2 * c] = __ffma2_rn(aa, make_float2(w.x, w.y), zp2[2 * c]);
+          zp2[2 * c + 1] = __ffma2_rn(aa, make_float2(w.z, w.w), zp2[2 * c + 1]);
         }
+      }
+      float zp[16];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) {
+        zp[2 * a] = zp2[a].x;
+        zp[2 * a + 1] = zp2[a].y;
       }
       // transpose-reduce: lane L ends with the sum of zp[L & 15] over the warp
 #pragma unroll
@@ -332,11 +339,15 @@ head_kernel(const HeadParams p) {
           }
         }
         float g = 0.f;
+        if constexpr (A == 1) {
+          dw[j][0].x = fmaf(av, d[0], dw[j][0].x);
+        } else {
+          const float2 aa = make_float2(av, av);
 #pragma unroll
-        for (int a = 0; a < A; ++a) {
-          dw[j][a] = fmaf(av, d[a], dw[j][a]);
-          g = fmaf(d[a], wreg[j][a], g);
+          for (int a = 0; a < A2; ++a) dw[j][a] = __ffma2_rn(aa, make_float2(d[2 * a], d[2 * a + 1]), dw[j][a]);
         }
+#pragma unroll
+        for (int a = 0; a < A; ++a) g = fmaf(d[a], wreg[j][a], g);
         g = av > 0.f ? g : 0.f;
         if (p.dX_lo) {
           float hi, lo;
@@ -360,7 +371,8 @@ head_kernel(const HeadParams p) {
     const int h = tid + j * kHeadThreads;
     if (h >= H) continue;
 #pragma unroll
-    for (int a = 0; a < A; ++a) p.dW_part[cta * H * A + (int64_t)h * A + a] = dw[j][a];
+    for (int a = 0; a < A; ++a)
+      p.dW_part[cta * H * A + (int64_t)h * A + a] = (a & 1) ? dw[j][a / 2].y : dw[j][a / 2].x;
     if (p.dbx_part) p.dbx_part[cta * H + h] = dbx[j];
   }
   __syncthreads();
