@@ -368,8 +368,10 @@ SPO_API int spo_learner_apply(spo_learner_t learner, spo_stream_t stream, const 
 /* The activation cache of the last forward (CriticCache a1, a2, ...,
  * networks/mlp.mojo:84-102): device pointers to the post-ReLU activations of hidden layer
  * `layer` (0-based, [rows x d_{layer+1}]) of network `which` (0 actor, 1 critic). With the
- * tensor-core engine the activation is stored as a TF32 hi/lo pair (value = hi + lo) and
- * *lo is set; otherwise *lo is NULL. Valid until the next call on the learner. */
+ * tensor-core engine the activations that feed tensor-core products are stored as TF32
+ * hi/lo pairs (value = hi + lo) and *lo is set; otherwise (the CUDA-core engine, and the
+ * last hidden layer, which only the fused head reads) *lo is NULL and *hi is the plain
+ * fp32 value. Valid until the next call on the learner. */
 SPO_API int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer,
                               const float** hi, const float** lo);
 /* Reads (synchronously) and clears the learner's device error word: 0 when every

@@ -236,7 +236,7 @@ struct NetPlan {
   bool tc = false;
   // workspace carve-outs
   float* acts[SPO_MAX_LAYERS] = {};     // a_l, l = 0..L-2: [rows x d_{l+1}] (hi in TC mode)
-  float* acts_lo[SPO_MAX_LAYERS] = {};  // TC mode: lo halves
+  float* acts_lo[SPO_MAX_LAYERS] = {};  // TC mode, l <= L-3: lo halves (a_{L-2} is fp32)
   uint32_t* acts_bits[SPO_MAX_LAYERS] = {};  // TC mode, l <= L-3: a_l > 0 packed [rows x d_{l+1}/32]
   float* dz[2] = {};                    // ping-pong [rows x max_hidden] (hi in TC mode)
   float* dz_lo[2] = {};                 // TC mode
@@ -312,7 +312,8 @@ void carve_net(NetPlan& n, Carve& c, int64_t rows) {
   const int L = d.num_layers;
   for (int l = 0; l + 1 < L; ++l) {
     n.acts[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
-    if (n.tc) n.acts_lo[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
+    // the last hidden activation is read only by the fused head: plain fp32
+    if (n.tc && l + 2 < L) n.acts_lo[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
     // packed for the dX GEMM of layer l + 1 (the last hidden layer's mask is read by the
     // head); layer 0's is written by the input-layer forward when its shape allows
     const bool packs = l >= 1 || (fwd_skinny_ok(d.dims[0], d.dims[1]) && d.dims[1] % 32 == 0);
@@ -1236,7 +1237,7 @@ int spo_learner_forward(spo_learner_t learner, spo_stream_t stream, int32_t whic
   int rc = net_forward_hidden(n, s, p, LayerInput{obs, nullptr}, rows, learner->err);
   if (rc) return rc;
   const int L = n.d.num_layers;
-  if (n.tc) {  // the last layer reads plain fp32: fold lo into hi (the cache is scratch here)
+  if (n.tc && n.acts_lo[L - 2]) {  // the last layer reads plain fp32: fold lo into hi
     rc = combine_tf32_launch(n.acts[L - 2], n.acts_lo[L - 2], rows * n.d.dims[L - 1], s);
     if (rc) return rc;
   }

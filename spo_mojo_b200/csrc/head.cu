@@ -16,17 +16,22 @@
 //
 // Work split. A CTA walks row tiles of R rows (grid-stride), two CTAs per SM. For each tile:
 //   1. the activations act[R x H] (and their lo halves) are copied into shared memory
-//      with cp.async (all 16-byte copies in flight at once);
+//      with cp.async, three tiles ahead of the one being computed when act is plain fp32
+//      (one ahead with lo halves), so enough bytes are in flight to cover HBM latency;
 //   2. one warp per row computes z = act W + b: lane l takes h = l + 32 m, W rows come
 //      from shared memory padded to AP = 12 columns (three conflict-free float4 reads),
 //      and a transpose-reduce leaves z_a in lane a. Lanes 0..A-1 then evaluate the
 //      masked softmax, the loss terms and dz of action a together (shuffle reductions
 //      over the actions), and the lane writes the combined act (hi + lo) back in place;
-//   3. each thread owns fixed columns h of act and, over the R rows, accumulates
-//      dW[h, :] += act[r, h] dz[r, :] and writes dX[r, h] = (dz[r] . W[h, :]) * [act > 0],
-//      accumulating the column sums of dX (the bias gradient of the layer below).
+//   3. each thread owns a fixed pair of adjacent columns h, h+1 of act (when H < 512, the
+//      256 / (H/2) row groups of the CTA split the rows) and, over its rows, accumulates
+//      dW[h, :] += act[r, h] dz[r, :] and writes dX[r, h] = (dz[r] . W[h, :]) * [act > 0]
+//      as one 8-byte store per output (packed FFMA2 over action pairs), accumulating the
+//      column sums of dX (the bias gradient of the layer below). Row groups' partial sums
+//      are added in group order at the end.
 // Partial sums (dW, db, column sums, loss statistics) go to per-CTA slots that a
 // deterministic reduction adds up.
+#include <algorithm>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -44,6 +49,8 @@ constexpr int kNW = kHeadThreads / 32;
 
 template <int A>
 __host__ __device__ constexpr int padded_actions() { return A == 1 ? 1 : (A + 3) & ~3; }
+
+__host__ __device__ constexpr int head_buffers(bool has_lo) { return has_lo ? 2 : 4; }
 
 __device__ __forceinline__ float softplus_f(float x) {
   return log1pf(expf(-fabsf(x))) + fmaxf(x, 0.f);
@@ -81,14 +88,14 @@ head_kernel(const HeadParams p) {
   const int H = p.H;
   const int R = p.rows_per_tile;
   const bool has_lo = p.act_lo != nullptr;
+  const int NB = head_buffers(has_lo);     // tile buffers: copies run NB - 1 tiles ahead
   float* Ws = sm;                          // [H][AP]
-  // two tile buffers: the copies of the next tile land while this one is computed
-  float* abuf = Ws + H * AP;               // [2][R][H] (act; hi + lo after phase 2)
-  float* lbuf = abuf + 2 * R * H;          // [2][R][H] lo halves
+  float* abuf = Ws + H * AP;               // [NB][R][H] (act; hi + lo after phase 2)
+  float* lbuf = abuf + NB * R * H;         // [2][R][H] lo halves (NB == 2)
   float* dzs = lbuf + (has_lo ? 2 * R * H : 0);  // [R][AP]
   float* red = dzs + R * AP;               // [kNW][AP + kStats]
-  // per-row loss inputs of the two tile buffers, copied with the activations:
-  // [2][3][R][A] = (q or critic target, mask or board cells, pi_old logits)
+  // per-row loss inputs of the tile buffers, copied with the activations:
+  // [NB][3][R][A] = (q or critic target, mask or board cells, pi_old logits)
   float* rinb = red + kNW * (AP + kStats);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -104,20 +111,30 @@ head_kernel(const HeadParams p) {
   float alpha = p.alpha_host;
   if (p.log_alpha != nullptr) alpha = softplus_f(__ldg(p.log_alpha));
 
-  // Thread-owned columns h = tid + 256 j.
-  float wreg[NJ][A];
-  constexpr int A2 = (A + 1) / 2;  // action pairs of dW (packed FFMA2)
-  float2 dw[NJ][A2];
-  float dbx[NJ];
+  // Phase 3 ownership: column pair c = cp0 + 256 j (columns 2c, 2c + 1) in row group rg.
+  const int G2 = H >> 1;
+  const int RG = G2 >= kHeadThreads ? 1 : kHeadThreads / G2;
+  const int rg = G2 >= kHeadThreads ? 0 : tid / G2;
+  const int cp0 = G2 >= kHeadThreads ? tid : tid % G2;
+  const bool p3 = rg < RG;
+  constexpr int A2 = (A + 1) / 2;  // action pairs (packed FFMA2); the odd one pads with 0
+  float2 wp[NJ][2][A2];            // W[h + c][2 i], W[h + c][2 i + 1]
+  float2 dw[NJ][2][A2];
+  float2 dbx[NJ];
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
-    const int h = tid + j * kHeadThreads;
-    dbx[j] = 0.f;
+    const int h = 2 * (cp0 + j * kHeadThreads);
+    dbx[j] = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int a = 0; a < A; ++a) {
-      wreg[j][a] = h < H ? __ldg(p.W + (int64_t)h * A + a) : 0.f;
-      if (a < A2) dw[j][a] = make_float2(0.f, 0.f);
-    }
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int i = 0; i < A2; ++i) {
+        const bool ok = p3 && h + c < H;
+        const float w0 = ok ? __ldg(p.W + (int64_t)(h + c) * A + 2 * i) : 0.f;
+        const float w1 = ok && 2 * i + 1 < A ? __ldg(p.W + (int64_t)(h + c) * A + 2 * i + 1) : 0.f;
+        wp[j][c][i] = make_float2(w0, w1);
+        dw[j][c][i] = make_float2(0.f, 0.f);
+      }
   }
   float dbl = 0.f;  // db of action la (A == 9) or of the output (A == 1, lane 0)
   float st[kStats];
@@ -151,18 +168,23 @@ head_kernel(const HeadParams p) {
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  issue(blockIdx.x, 0);
+  for (int i = 0; i + 1 < NB; ++i) issue(blockIdx.x + (int64_t)i * gridDim.x, i);
   int it = 0;
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
     const int64_t r0 = t * R;
     const int rows = (int)min((int64_t)R, p.M - r0);
-    // buffer (it + 1) & 1 was released by the barrier that ended the previous tile
-    issue(t + gridDim.x, (it + 1) & 1);
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    // buffer (it + NB - 1) % NB was released by the barrier that ended the previous tile
+    issue(t + (int64_t)(NB - 1) * gridDim.x, (it + NB - 1) % NB);
+    // this tile's group is complete when at most NB - 1 younger groups are pending
+    if (NB == 4)
+      asm volatile("cp.async.wait_group 3;" ::: "memory");
+    else
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
     __syncthreads();  // this tile's copies (every thread's) have landed; W staged
-    float* ahi = abuf + (it & 1) * R * H;
+    const int bi = it % NB;
+    float* ahi = abuf + bi * R * H;
     const float* alo = lbuf + (it & 1) * R * H;
-    const float* rq = rinb + (it & 1) * 3 * R * A;  // q (actor) / target (critic)
+    const float* rq = rinb + bi * 3 * R * A;  // q (actor) / target (critic)
     const float* rm = rq + R * A;                   // mask, or board cells
     const float* rz = rq + 2 * R * A;               // pi_old logits
     const bool from_cells = !p.mask && p.cells;
@@ -318,13 +340,13 @@ head_kernel(const HeadParams p) {
     }
     __syncthreads();
 
-    // 3. Thread-owned columns: dW, dX (ReLU-masked), column sums of dX.
+    // 3. Column pairs: dW, dX (ReLU-masked), column sums of dX.
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
-      const int h = tid + j * kHeadThreads;
-      if (h >= H) continue;
-      for (int r = 0; r < rows; ++r) {
-        const float av = ahi[r * H + h];
+      const int h = 2 * (cp0 + j * kHeadThreads);
+      if (!p3 || h >= H) continue;
+      for (int r = rg; r < rows; r += RG) {
+        const float2 av = *reinterpret_cast<const float2*>(ahi + r * H + h);
         float d[AP];
         if constexpr (A == 1) {
           d[0] = dzs[r];
@@ -338,42 +360,100 @@ head_kernel(const HeadParams p) {
             d[4 * c + 3] = v.w;
           }
         }
-        float g = 0.f;
-        if constexpr (A == 1) {
-          dw[j][0].x = fmaf(av, d[0], dw[j][0].x);
-        } else {
-          const float2 aa = make_float2(av, av);
+        float g[2];
 #pragma unroll
-          for (int a = 0; a < A2; ++a) dw[j][a] = __ffma2_rn(aa, make_float2(d[2 * a], d[2 * a + 1]), dw[j][a]);
+        for (int c = 0; c < 2; ++c) {
+          const float a = c ? av.y : av.x;
+          if constexpr (A == 1) {
+            dw[j][c][0].x = fmaf(a, d[0], dw[j][c][0].x);
+            g[c] = d[0] * wp[j][c][0].x;
+          } else {
+            const float2 aa = make_float2(a, a);
+            float2 gg = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < A2; ++i) {
+              const float2 dd = make_float2(d[2 * i], d[2 * i + 1]);
+              dw[j][c][i] = __ffma2_rn(aa, dd, dw[j][c][i]);
+              gg = __ffma2_rn(dd, wp[j][c][i], gg);
+            }
+            g[c] = gg.x + gg.y;
+          }
+          g[c] = a > 0.f ? g[c] : 0.f;
         }
-#pragma unroll
-        for (int a = 0; a < A; ++a) g = fmaf(d[a], wreg[j][a], g);
-        g = av > 0.f ? g : 0.f;
+        dbx[j].x += g[0];
+        dbx[j].y += g[1];
+        const int64_t o = (r0 + r) * H + h;
         if (p.dX_lo) {
-          float hi, lo;
-          tf32_split(g, hi, lo);
-          p.dX[(r0 + r) * H + h] = hi;
-          p.dX_lo[(r0 + r) * H + h] = lo;
+          float h0, l0, h1, l1;
+          tf32_split(g[0], h0, l0);
+          tf32_split(g[1], h1, l1);
+          *reinterpret_cast<float2*>(p.dX + o) = make_float2(h0, h1);
+          *reinterpret_cast<float2*>(p.dX_lo + o) = make_float2(l0, l1);
         } else if (p.dX) {
-          p.dX[(r0 + r) * H + h] = g;
+          *reinterpret_cast<float2*>(p.dX + o) = make_float2(g[0], g[1]);
         }
-        dbx[j] += g;
       }
     }
     __syncthreads();  // the tile's buffer and dzs are free for the next copies / rows
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 
-  // Per-CTA partials.
+  // Per-CTA partials. Row groups 1.. hand their sums to group 0 through shared memory,
+  // one group at a time (fixed order).
+  __syncthreads();
+  float* xs = abuf;  // [H x A] dW, then [H] column sums
+  for (int gsrc = 1; gsrc < RG; ++gsrc) {
+    if (rg == gsrc) {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int h = 2 * (cp0 + j * kHeadThreads);
+        if (h >= H) continue;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int a = 0; a < A; ++a) xs[(h + c) * A + a] = (a & 1) ? dw[j][c][a / 2].y : dw[j][c][a / 2].x;
+          xs[H * A + h + c] = c ? dbx[j].y : dbx[j].x;
+        }
+      }
+    }
+    __syncthreads();
+    if (rg == 0) {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) {
+        const int h = 2 * (cp0 + j * kHeadThreads);
+        if (h >= H) continue;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int a = 0; a < A; ++a) {
+            if (a & 1)
+              dw[j][c][a / 2].y += xs[(h + c) * A + a];
+            else
+              dw[j][c][a / 2].x += xs[(h + c) * A + a];
+          }
+          if (c)
+            dbx[j].y += xs[H * A + h + c];
+          else
+            dbx[j].x += xs[H * A + h + c];
+        }
+      }
+    }
+    __syncthreads();
+  }
   const int64_t cta = blockIdx.x;
+  if (rg == 0) {
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) {
-    const int h = tid + j * kHeadThreads;
-    if (h >= H) continue;
+    for (int j = 0; j < NJ; ++j) {
+      const int h = 2 * (cp0 + j * kHeadThreads);
+      if (h >= H) continue;
 #pragma unroll
-    for (int a = 0; a < A; ++a)
-      p.dW_part[cta * H * A + (int64_t)h * A + a] = (a & 1) ? dw[j][a / 2].y : dw[j][a / 2].x;
-    if (p.dbx_part) p.dbx_part[cta * H + h] = dbx[j];
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int a = 0; a < A; ++a)
+          p.dW_part[cta * H * A + (int64_t)(h + c) * A + a] = (a & 1) ? dw[j][c][a / 2].y : dw[j][c][a / 2].x;
+        if (p.dbx_part) p.dbx_part[cta * H + h + c] = c ? dbx[j].y : dbx[j].x;
+      }
+    }
   }
   __syncthreads();
   constexpr int RW = AP + kStats;
@@ -398,8 +478,8 @@ head_kernel(const HeadParams p) {
 template <int A>
 int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
   void (*k)(const HeadParams);
-  const int nj = (p.H + kHeadThreads - 1) / kHeadThreads;
-  k = nj <= 1 ? head_kernel<A, 1> : (nj == 2 ? head_kernel<A, 2> : head_kernel<A, 4>);
+  const int nj = (p.H / 2 + kHeadThreads - 1) / kHeadThreads;  // column pairs per thread
+  k = nj <= 1 ? head_kernel<A, 1> : head_kernel<A, 2>;
   // opt in once per device and instantiation to the largest size any H needs, so that no
   // attribute call happens while a stream is being captured into a graph
   static std::mutex mu;
@@ -409,8 +489,10 @@ int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!opted.count({dev, (const void*)k})) {
-      SPO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)head_smem_bytes(kHeadThreads * kHeadMaxHJ, A)));
+      size_t most = 0;
+      for (int h = 4; h <= kHeadThreads * kHeadMaxHJ; h += 4)
+        most = std::max({most, head_smem_bytes(h, A, true), head_smem_bytes(h, A, false)});
+      SPO_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most));
       opted.insert({dev, (const void*)k});
     }
   }
@@ -421,14 +503,16 @@ int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
 
 }  // namespace
 
-// 4096 activations per tile buffer (16 KB hi + 16 KB lo, double-buffered): two CTAs per SM
-int head_rows_per_tile(int H) { return std::max(1, 4096 / H); }
+// 4096 activations per tile buffer (16 KB), at most 64 rows (the per-row loss inputs of
+// narrow layers stay small): two CTAs per SM
+int head_rows_per_tile(int H) { return std::max(1, std::min(64, 4096 / H)); }
 
-size_t head_smem_bytes(int H, int A) {
+size_t head_smem_bytes(int H, int A, bool has_lo) {
   const int R = head_rows_per_tile(H);
   const int AP = A == 1 ? 1 : (A + 3) & ~3;
-  return sizeof(float) * ((size_t)H * AP + 4 * (size_t)R * H + (size_t)R * AP + (size_t)kNW * (AP + kStats) +
-                          6 * (size_t)R * A);
+  const size_t nb = head_buffers(has_lo);
+  return sizeof(float) * ((size_t)H * AP + (nb + (has_lo ? 2 : 0)) * (size_t)R * H + (size_t)R * AP +
+                          (size_t)kNW * (AP + kStats) + 3 * nb * (size_t)R * A);
 }
 
 int head_grid(int64_t M, int H) {
@@ -443,12 +527,14 @@ int head_launch(HeadParams p, int grid, cudaStream_t s) {
   SPO_CHECK_ARG(aligned16(p.act) && (!p.act_lo || aligned16(p.act_lo)), kErrAlign,
                 "head: activations must be 16-byte aligned");
   SPO_CHECK_ARG(!p.dX_lo || p.dX, kErrArg, "head: dX_lo needs dX");
+  SPO_CHECK_ARG(reinterpret_cast<uintptr_t>(p.dX) % 8 == 0 && reinterpret_cast<uintptr_t>(p.dX_lo) % 8 == 0,
+                kErrAlign, "head: dX must be 8-byte aligned");
   SPO_CHECK_ARG(p.A == 1 || p.A == 9, kErrUnsupported, "head: output width must be 1 or 9");
   SPO_CHECK_ARG(!p.cells || p.mask || p.A == 9, kErrUnsupported, "head: board cells need 9 actions");
   SPO_CHECK_ARG(p.mode == kHeadCritic ? p.target != nullptr : p.q != nullptr, kErrArg,
                 "head: missing loss inputs");
   p.rows_per_tile = head_rows_per_tile(p.H);
-  const size_t smem = head_smem_bytes(p.H, p.A);
+  const size_t smem = head_smem_bytes(p.H, p.A, p.act_lo != nullptr);
   if (p.M == 0) return kOk;
   return p.A == 9 ? launch_a<9>(p, grid, smem, s) : launch_a<1>(p, grid, smem, s);
 }

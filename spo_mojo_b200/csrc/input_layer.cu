@@ -106,11 +106,14 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
   const int64_t r_end = min(rows, r_begin + chunk);
   const int i0 = half * kHalf;
 
-  // columns (0, 1) and (2, 3) of each feature as packed pairs: one FFMA2 (two fp32 fma.rn,
-  // the same results as fmaf) per pair
-  float2 acc[kHalf][2];
+  // per column, adjacent features as packed pairs: one FFMA2 (two fp32 fma.rn, the same
+  // results as fmaf) per pair; the x pairs come straight from the staged float4 reads and
+  // only the dY value is broadcast into a pair
+  float2 acc[4][kHalf / 2];
 #pragma unroll
-  for (int i = 0; i < kHalf; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int i = 0; i < kHalf / 2; ++i) acc[q][i] = make_float2(0.f, 0.f);
 
   XStage st{xs2, cs2, x, cells, k, r_begin, r_end};
   st.clear(tid, kThreads);
@@ -137,16 +140,15 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const float4* xr = reinterpret_cast<const float4*>(&xs[r0 + u][i0]);
+          const float gv[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
 #pragma unroll
-          for (int c = 0; c < kHalf / 4; ++c) {
-            const float4 xv = xr[c];
-            const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-            const float2 g01 = make_float2(g[u].x, g[u].y), g23 = make_float2(g[u].z, g[u].w);
+          for (int q = 0; q < 4; ++q) {
+            const float2 gg = make_float2(gv[q], gv[q]);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const float2 xx = make_float2(xa[t], xa[t]);
-              acc[4 * c + t][0] = __ffma2_rn(xx, g01, acc[4 * c + t][0]);
-              acc[4 * c + t][1] = __ffma2_rn(xx, g23, acc[4 * c + t][1]);
+            for (int c = 0; c < kHalf / 4; ++c) {
+              const float4 xv = xr[c];
+              acc[q][2 * c] = __ffma2_rn(make_float2(xv.x, xv.y), gg, acc[q][2 * c]);
+              acc[q][2 * c + 1] = __ffma2_rn(make_float2(xv.z, xv.w), gg, acc[q][2 * c + 1]);
             }
           }
         }
@@ -160,9 +162,10 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
 #pragma unroll
   for (int i = 0; i < kHalf; ++i) {
     const int f = i0 + i;
-    if (f < k)
-      *reinterpret_cast<float4*>(out + (int64_t)f * n + col) =
-          make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
+    if (f < k) {
+      auto pick = [&](int q) { return (i & 1) ? acc[q][i / 2].y : acc[q][i / 2].x; };
+      *reinterpret_cast<float4*>(out + (int64_t)f * n + col) = make_float4(pick(0), pick(1), pick(2), pick(3));
+    }
   }
 }
 

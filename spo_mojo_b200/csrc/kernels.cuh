@@ -49,7 +49,7 @@ struct HeadParams {
 };
 
 int head_rows_per_tile(int H);
-size_t head_smem_bytes(int H, int A);
+size_t head_smem_bytes(int H, int A, bool has_lo);
 int head_grid(int64_t M, int H);
 int head_launch(HeadParams p, int grid, cudaStream_t s);
 

@@ -64,7 +64,21 @@ struct Geo {
 #ifndef SPO_TC_SEG
 #define SPO_TC_SEG 2
 #endif
-constexpr int SEG = SPO_TC_SEG;                          // k-blocks per TMEM accumulation
+#ifndef SPO_TC_SEG_DX
+#define SPO_TC_SEG_DX 8
+#endif
+// k-blocks per TMEM accumulation: the forward (whose outputs decide ReLU masks) and dW
+// (long split-K sums with cancellation) fold every 2; the dX products, which decide
+// nothing and whose 3-5e-6 stays far inside the gradients' 1e-4 tolerance, every 8, which
+// saves three of every four accumulator reads (each one stalls the tensor pipe briefly).
+// Kernel-internal epilogue: the forward written as plain fp32 (TC_FWD with c_lo == null,
+// for an activation that no tensor-core product reads), without the mask bits.
+constexpr int kFwdF32 = 4;
+
+template <int KIND>
+__host__ __device__ constexpr int seg_of() {
+  return (KIND == 1 || KIND == 2) ? SPO_TC_SEG_DX : SPO_TC_SEG;
+}
 constexpr int NACC = 4;                                  // TMEM accumulators in flight
 constexpr uint32_t TMEM_COLS = NACC * BN;                // 512: the whole TMEM of the SM
 constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
@@ -308,6 +322,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
                const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
                const KParams P) {
   using G = Geo<PAIR>;
+  constexpr int SEG = seg_of<KIND>();
   constexpr int STAGES = G::STAGES;
   constexpr uint32_t STAGE_BYTES = G::STAGE_BYTES;
   constexpr uint32_t B_TILE = G::B_TILE;
@@ -595,7 +610,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
           const bool ina = ra < P.M, inb = rb < P.M;
           const int64_t cbase = n0 + cb + tc;
-          if (KIND == TC_FWD) {
+          if (KIND == kFwdF32) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              const int64_t col = cbase + 8 * g;
+              const float2 b2 = __ldg(reinterpret_cast<const float2*>(P.bias + col));
+              const float x0 = v[4 * g] + b2.x, x1 = v[4 * g + 1] + b2.y;
+              const float x2 = v[4 * g + 2] + b2.x, x3 = v[4 * g + 3] + b2.y;
+              if (ina) store2(P.c_hi + ra * P.N + col, x0 > 0.f ? x0 : 0.f, x1 > 0.f ? x1 : 0.f);
+              if (inb) store2(P.c_hi + rb * P.N + col, x2 > 0.f ? x2 : 0.f, x3 > 0.f ? x3 : 0.f);
+            }
+          } else if (KIND == TC_FWD) {
             uint32_t ba0 = 0, ba1 = 0, bb0 = 0, bb1 = 0;  // bits of rows ra, rb: columns 0-31, 32-63
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
@@ -913,7 +938,8 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
     SPO_CHECK_ARG(a.k_chunk >= BK && a.k_chunk % BK == 0 && a.c_part, kErrArg,
                   "tc_gemm: dW needs c_part and k_chunk a multiple of 32");
   else
-    SPO_CHECK_ARG(a.c_hi && aligned16(a.c_hi) && (a.kind == TC_DX_F32 || (a.c_lo && aligned16(a.c_lo))),
+    SPO_CHECK_ARG(a.c_hi && aligned16(a.c_hi) &&
+                      (a.kind == TC_DX_F32 || (a.c_lo ? aligned16(a.c_lo) : a.kind == TC_FWD)),
                   kErrArg, "tc_gemm: null or misaligned output");
   if (a.kind == TC_FWD) SPO_CHECK_ARG(a.bias && aligned16(a.bias), kErrArg, "tc_gemm: bias");
   if (a.kind == TC_DX || a.kind == TC_DX_F32)
@@ -959,7 +985,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.colsum = a.colsum;
   P.err = a.err;
   P.mask_bits = a.kind == TC_DX || a.kind == TC_DX_F32 ? a.mask_bits : nullptr;
-  P.c_bits = a.kind == TC_FWD ? a.c_bits : nullptr;
+  P.c_bits = a.kind == TC_FWD && a.c_lo ? a.c_bits : nullptr;
   const int grid = tc_gemm_grid(a);
   const size_t smem = tc_smem_bytes(a.kind, a.N, pair);
   const bool bits = P.mask_bits != nullptr;
@@ -969,7 +995,9 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
     kern = tc_gemm_kernel<TC_DW, false, true>;  // use_pair: dW only
   } else {
     switch (a.kind) {
-      case TC_FWD: kern = tc_gemm_kernel<TC_FWD, false, false>; break;
+      case TC_FWD:
+        kern = a.c_lo ? tc_gemm_kernel<TC_FWD, false, false> : tc_gemm_kernel<kFwdF32, false, false>;
+        break;
       case TC_DX: kern = bits ? tc_gemm_kernel<TC_DX, true, false> : tc_gemm_kernel<TC_DX, false, false>; break;
       case TC_DX_F32:
         kern = bits ? tc_gemm_kernel<TC_DX_F32, true, false> : tc_gemm_kernel<TC_DX_F32, false, false>;

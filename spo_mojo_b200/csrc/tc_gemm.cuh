@@ -38,7 +38,7 @@ struct TcGemmArgs {
   const float* bias;       // TC_FWD: [N]
   const float* mask;       // TC_DX*: [M x N] (pitch N), keep where > 0
   float* c_hi;             // [M x N] (pitch N): hi or fp32 result
-  float* c_lo;             // [M x N] (pitch N): lo (TC_FWD, TC_DX)
+  float* c_lo;             // [M x N] (pitch N): lo (TC_DX; TC_FWD: null = fp32 into c_hi)
   float* c_part;           // TC_DW: [splits][M x N]
   float* colsum;           // TC_DX*: [grid][N] column sums (optional)
   int* err;                // device error word (bounded waits), optional
