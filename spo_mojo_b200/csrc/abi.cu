@@ -287,18 +287,18 @@ int64_t tc_dw_splits_max(int64_t rows) {
   return std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 32) / 64, 4LL * sm_count()));
 }
 
-// Row splits S of a tensor-core dW product with `tiles` output tiles: at least 64
-// k-blocks (2048 rows) per unit, and the smallest S whose tiles*S units fill the SMs in
-// whole waves (>= 95% of the last wave busy), else the best such fill.
-int64_t tc_dw_splits(int64_t tiles, int64_t rows) {
-  const int64_t sms = sm_count();
+// Row splits S of a tensor-core dW product whose unit grid has `tiles` output tiles per
+// split and `slots` units running at once: at least 64 k-blocks (2048 rows) per unit, and
+// the smallest S whose tiles*S units fill the slots in whole waves (>= 95% of the last
+// wave busy), else the best such fill.
+int64_t tc_dw_splits(int64_t tiles, int64_t slots, int64_t rows) {
   const int64_t smax = tc_dw_splits_max(rows);
   int64_t best = 1;
   double best_eff = -1.0;
   for (int64_t S = 1; S <= smax; ++S) {
     const int64_t units = tiles * S;
-    const double eff = (double)units / (double)(ceil_div(units, sms) * sms);
-    if (units >= sms && eff >= 0.95) return S;
+    const double eff = (double)units / (double)(ceil_div(units, slots) * slots);
+    if (units >= slots && eff >= 0.95) return S;
     if (eff > best_eff + 1e-9) {
       best_eff = eff;
       best = S;
@@ -542,7 +542,7 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, Layer
       w.M = kin;
       w.N = nout;
       w.K = rows;
-      const int64_t S = tc_dw_splits((kin / 128) * (nout / 128), rows);
+      const int64_t S = tc_dw_splits(tc_gemm_tiles(TC_DW, kin, nout), tc_gemm_slots(TC_DW, nout), rows);
       w.k_chunk = align_up(ceil_div(ceil_div(rows, 32), S), 1) * 32;
       w.c_part = n.dw_part[l];
       w.err = err;

@@ -36,26 +36,35 @@ namespace spo {
 namespace {
 
 constexpr int BM = 128;                                  // output rows per CTA
-constexpr int BN = 128;
 constexpr int BK = 32;
-constexpr int kEpiWarps = 8;
-constexpr int kEpiThreads = 32 * kEpiWarps;
-constexpr int kThreads = 64 + kEpiThreads;
-constexpr int EPI_COLS = BN / 2;                         // columns per epilogue warp
+constexpr int EPI_COLS = 64;                             // columns per epilogue warp
 constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
 constexpr int STAGES_MAX = 4;
+constexpr int NACC_MAX = 4;
+constexpr uint32_t TMEM_COLS = 512;                      // the whole TMEM of the SM
 
-// Operand staging of one CTA. Single CTA: A [128 x 32] and B [128 x 32] hi/lo per
-// k-block, 3 stages. CTA pair (cta_group::2, 256 x 128 output tile per pair): each CTA
-// stages its own 128 rows of A and one half (64 rows) of B, 4 stages; the MMA issued by
-// the pair's first CTA reads both CTAs' shared memory.
-template <bool PAIR>
+// Geometry of one instantiation: PAIR = CTA pair (cta_group::2), TBN = output columns per
+// tile (128, or 256 when N allows: one 128 x 256 MMA per k-step reads A once for twice the
+// columns, and the per-k-block TMA refill and accumulator hand-offs are amortised over
+// twice the work). Single CTA: A [128 x 32] and B [TBN x 32] hi/lo per k-block. CTA pair
+// (256 x TBN output tile per pair): each CTA stages its own 128 rows of A and one half of B;
+// the MMA issued by the pair's first CTA reads both CTAs' shared memory. The ring takes as
+// many stages as fit in ~200 KB; TMEM holds 512 / TBN accumulators; the epilogue has one
+// warp per (TMEM lane quadrant, 64-column group).
+template <bool PAIR, int TBN>
 struct Geo {
-  static constexpr int STAGES = PAIR ? 4 : 3;
+  static constexpr int BN = TBN;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
   static constexpr uint32_t B_TILE = B_ROWS * BK * 4;
-  static constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB pair, 64 KB single
+  static constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
+  static constexpr int STAGES = (200u * 1024u) / STAGE_BYTES < (uint32_t)STAGES_MAX
+                                    ? (int)((200u * 1024u) / STAGE_BYTES)
+                                    : STAGES_MAX;
   static constexpr int UNIT_M = PAIR ? 2 * BM : BM;                // output rows per unit
+  static constexpr int NACC = (int)(TMEM_COLS / BN);
+  static constexpr int EPI_WARPS = 4 * (BN / EPI_COLS);
+  static constexpr int EPI_THREADS = 32 * EPI_WARPS;
+  static constexpr int THREADS = 64 + EPI_THREADS;
 };
 // The tensor core's accumulation into TMEM is not exact fp32: its error grows with the
 // number of MMAs summed into one accumulator. Folding every 2 k-blocks (64 reduction
@@ -79,8 +88,6 @@ template <int KIND>
 __host__ __device__ constexpr int seg_of() {
   return (KIND == 1 || KIND == 2) ? SPO_TC_SEG_DX : SPO_TC_SEG;
 }
-constexpr int NACC = 4;                                  // TMEM accumulators in flight
-constexpr uint32_t TMEM_COLS = NACC * BN;                // 512: the whole TMEM of the SM
 constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
 constexpr uint64_t kDrainNs = 500000000ull;              // 0.5 s
 constexpr int kMaxColsumN = 1024;
@@ -90,8 +97,8 @@ enum WaitCode : int { kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, k
 struct __align__(64) Ctl {
   uint64_t full[STAGES_MAX];
   uint64_t empty[STAGES_MAX];
-  uint64_t tfull[NACC];
-  uint64_t tempty[NACC];
+  uint64_t tfull[NACC_MAX];
+  uint64_t tempty[NACC_MAX];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -285,6 +292,24 @@ __device__ __forceinline__ void tmem_ld16x256_x8(uint32_t taddr, uint32_t (&r)[3
       : "r"(taddr));
 }
 
+// The same shape repeated 4 times: 16 lanes x 32 columns; r[4 g + i] as above, g < 4.
+__device__ __forceinline__ void tmem_ld16x256_x4(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_tie16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_tie(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
@@ -316,12 +341,16 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 // One instantiation per epilogue (KIND) and dX mask format (BITS: packed bits instead of
 // fp32). 10 warps share the SM's four 16K-register files 3/3/2/2: at most 168 registers a
 // thread.
-template <int KIND, bool BITS, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int KIND, bool BITS, bool PAIR, int TBN>
+__global__ void __launch_bounds__(Geo<PAIR, TBN>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
                const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
                const KParams P) {
-  using G = Geo<PAIR>;
+  using G = Geo<PAIR, TBN>;
+  constexpr int BN = G::BN;
+  constexpr int NACC = G::NACC;
+  constexpr int kEpiWarps = G::EPI_WARPS;
+  constexpr int kEpiThreads = G::EPI_THREADS;
   constexpr int SEG = seg_of<KIND>();
   constexpr int STAGES = G::STAGES;
   constexpr uint32_t STAGE_BYTES = G::STAGE_BYTES;
@@ -528,13 +557,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     // instruction are then written 32 contiguous bytes each (4 threads x float2): whole
     // sectors, with no shared-memory staging.
     const int q = warp & 3;                  // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;        // which EPI_COLS columns of the tile
-    const int cb = half * EPI_COLS;
+    const int cgrp = (warp - 2) >> 2;        // which EPI_COLS columns of the tile
+    const int cb = cgrp * EPI_COLS;
     const int tr = lane >> 2, tc = 2 * (lane & 3);
     constexpr bool dx = KIND == TC_DX || KIND == TC_DX_F32;
     if (dx)
       for (int c = lane; c < P.N; c += 32)
-        if (((c / EPI_COLS) & 1) == half) colacc[q * P.N + c] = 0.f;
+        if ((c / EPI_COLS) % (BN / EPI_COLS) == cgrp) colacc[q * P.N + c] = 0.f;
     __syncwarp();
     uint32_t seg_i = 0;
     bool ok = true;
@@ -576,19 +605,38 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
         }
         tc_fence_after();
         const uint32_t ta = tmem_base + lane_addr + acc * BN + cb;
-        // one 16-row half at a time (32 registers in flight)
+        if constexpr (kEpiWarps <= 8) {
+          // one 16-row half at a time (32 registers in flight)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t r[32];
-          tmem_ld16x256_x8(ta + ((uint32_t)(16 * hh) << 16), r);
-          tmem_wait_tie(r);
-          float* v = rs + 32 * hh;
-          if (sg == 0) {
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t r[32];
+            tmem_ld16x256_x8(ta + ((uint32_t)(16 * hh) << 16), r);
+            tmem_wait_tie(r);
+            float* v = rs + 32 * hh;
+            if (sg == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          } else {
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = v[j] + __uint_as_float(r[j]);
+              for (int j = 0; j < 32; ++j) v[j] = v[j] + __uint_as_float(r[j]);
+            }
+          }
+        } else {
+          // 16 epilogue warps share the register file 5/5/4/4 per scheduler (at most 96
+          // registers a thread): 32 columns of one 16-row half at a time (16 in flight)
+#pragma unroll
+          for (int hq = 0; hq < 4; ++hq) {
+            uint32_t r[16];
+            tmem_ld16x256_x4(ta + ((uint32_t)(16 * (hq >> 1)) << 16) + 32 * (hq & 1), r);
+            tmem_wait_tie16(r);
+            float* v = rs + 32 * (hq >> 1) + 16 * (hq & 1);
+            if (sg == 0) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = v[j] + __uint_as_float(r[j]);
+            }
           }
         }
         // the accumulator is free for the next segment's MMAs once the loads completed
@@ -601,140 +649,140 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
             mbar_arrive(tempty0 + acc * 8);
         }
         if (sg != nseg - 1) continue;
-        float cs[16];                        // column sums (DX): [g][column pair]
+        // Final epilogue, one 8-column group g at a time over both 16-row halves, so that
+        // only a few values besides the running sums are live at once.
+        const int64_t cbase = n0 + cb + tc;
+        if constexpr (KIND == kFwdF32) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) cs[j] = 0.f;
+          for (int g = 0; g < 8; ++g) {
+            const int64_t col = cbase + 8 * g;
+            const float2 b2 = __ldg(reinterpret_cast<const float2*>(P.bias + col));
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float* v = rs + 32 * hh;
-          const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
-          const bool ina = ra < P.M, inb = rb < P.M;
-          const int64_t cbase = n0 + cb + tc;
-          if (KIND == kFwdF32) {
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const int64_t col = cbase + 8 * g;
-              const float2 b2 = __ldg(reinterpret_cast<const float2*>(P.bias + col));
+            for (int hh = 0; hh < 2; ++hh) {
+              const float* v = rs + 32 * hh;
+              const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
               const float x0 = v[4 * g] + b2.x, x1 = v[4 * g + 1] + b2.y;
               const float x2 = v[4 * g + 2] + b2.x, x3 = v[4 * g + 3] + b2.y;
-              if (ina) store2(P.c_hi + ra * P.N + col, x0 > 0.f ? x0 : 0.f, x1 > 0.f ? x1 : 0.f);
-              if (inb) store2(P.c_hi + rb * P.N + col, x2 > 0.f ? x2 : 0.f, x3 > 0.f ? x3 : 0.f);
+              if (ra < P.M) store2(P.c_hi + ra * P.N + col, x0 > 0.f ? x0 : 0.f, x1 > 0.f ? x1 : 0.f);
+              if (rb < P.M) store2(P.c_hi + rb * P.N + col, x2 > 0.f ? x2 : 0.f, x3 > 0.f ? x3 : 0.f);
             }
-          } else if (KIND == TC_FWD) {
-            uint32_t ba0 = 0, ba1 = 0, bb0 = 0, bb1 = 0;  // bits of rows ra, rb: columns 0-31, 32-63
+          }
+        } else if constexpr (KIND == TC_FWD) {
+          uint32_t bw[2][4] = {};  // [hh]: bits of rows ra, rb, columns 0-31 / 32-63
 #pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const int64_t col = cbase + 8 * g;
-              const float2 b2 = __ldg(reinterpret_cast<const float2*>(P.bias + col));
+          for (int g = 0; g < 8; ++g) {
+            const int64_t col = cbase + 8 * g;
+            const float2 b2 = __ldg(reinterpret_cast<const float2*>(P.bias + col));
+            const uint32_t sh = (8 * g + tc) & 31;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const float* v = rs + 32 * hh;
+              const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
               const float x[4] = {v[4 * g] + b2.x, v[4 * g + 1] + b2.y, v[4 * g + 2] + b2.x,
                                   v[4 * g + 3] + b2.y};
               float h[4], l[4];
 #pragma unroll
               for (int t = 0; t < 4; ++t) tf32_split_pos(x[t] > 0.f ? x[t] : 0.f, h[t], l[t]);
-              if (ina) {
+              if (ra < P.M) {
                 store2(P.c_hi + ra * P.N + col, h[0], h[1]);
                 store2(P.c_lo + ra * P.N + col, l[0], l[1]);
               }
-              if (inb) {
+              if (rb < P.M) {
                 store2(P.c_hi + rb * P.N + col, h[2], h[3]);
                 store2(P.c_lo + rb * P.N + col, l[2], l[3]);
               }
-              const uint32_t sh = (8 * g + tc) & 31;
               const uint32_t pa = (h[0] > 0.f ? 1u : 0u) | (h[1] > 0.f ? 2u : 0u);
               const uint32_t pb = (h[2] > 0.f ? 1u : 0u) | (h[3] > 0.f ? 2u : 0u);
-              if (g < 4) {
-                ba0 |= pa << sh;
-                bb0 |= pb << sh;
-              } else {
-                ba1 |= pa << sh;
-                bb1 |= pb << sh;
-              }
-            }
-            if (P.c_bits) {
-              // the 4 threads of a row hold disjoint bits: OR them, one thread stores
-#pragma unroll
-              for (int o = 1; o <= 2; o <<= 1) {
-                ba0 |= __shfl_xor_sync(0xffffffffu, ba0, o);
-                ba1 |= __shfl_xor_sync(0xffffffffu, ba1, o);
-                bb0 |= __shfl_xor_sync(0xffffffffu, bb0, o);
-                bb1 |= __shfl_xor_sync(0xffffffffu, bb1, o);
-              }
-              if ((lane & 3) == 0) {
-                const int64_t wpr = P.N / 32, w0 = (n0 + cb) / 32;
-                if (ina) *reinterpret_cast<uint2*>(P.c_bits + ra * wpr + w0) = make_uint2(ba0, ba1);
-                if (inb) *reinterpret_cast<uint2*>(P.c_bits + rb * wpr + w0) = make_uint2(bb0, bb1);
-              }
-            }
-          } else if (dx) {
-            float2 mk[16];
-            if (BITS) {
-              const uint2 wa = mw[2 * hh], wb = mw[2 * hh + 1];
-#pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                const uint32_t sh = (8 * g + tc) & 31;
-                const uint32_t a = (g < 4 ? wa.x : wa.y) >> sh, b = (g < 4 ? wb.x : wb.y) >> sh;
-                mk[2 * g] = make_float2((float)(a & 1u), (float)((a >> 1) & 1u));
-                mk[2 * g + 1] = make_float2((float)(b & 1u), (float)((b >> 1) & 1u));
-              }
-            } else {
-#pragma unroll
-              for (int g = 0; g < 8; ++g) {
-                const int64_t col = cbase + 8 * g;
-                mk[2 * g] = ina ? __ldg(reinterpret_cast<const float2*>(P.mask + ra * P.N + col))
-                                : make_float2(0.f, 0.f);
-                mk[2 * g + 1] = inb ? __ldg(reinterpret_cast<const float2*>(P.mask + rb * P.N + col))
-                                    : make_float2(0.f, 0.f);
-              }
-            }
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const int64_t col = cbase + 8 * g;
-              v[4 * g] = mk[2 * g].x > 0.f ? v[4 * g] : 0.f;
-              v[4 * g + 1] = mk[2 * g].y > 0.f ? v[4 * g + 1] : 0.f;
-              v[4 * g + 2] = mk[2 * g + 1].x > 0.f ? v[4 * g + 2] : 0.f;
-              v[4 * g + 3] = mk[2 * g + 1].y > 0.f ? v[4 * g + 3] : 0.f;
-              if (KIND == TC_DX) {
-                float h[4], l[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) tf32_split(v[4 * g + t], h[t], l[t]);
-                if (ina) {
-                  store2(P.c_hi + ra * P.N + col, h[0], h[1]);
-                  store2(P.c_lo + ra * P.N + col, l[0], l[1]);
-                }
-                if (inb) {
-                  store2(P.c_hi + rb * P.N + col, h[2], h[3]);
-                  store2(P.c_lo + rb * P.N + col, l[2], l[3]);
-                }
-              } else {
-                if (ina) store2(P.c_hi + ra * P.N + col, v[4 * g], v[4 * g + 1]);
-                if (inb) store2(P.c_hi + rb * P.N + col, v[4 * g + 2], v[4 * g + 3]);
-              }
-              cs[2 * g] += v[4 * g] + v[4 * g + 2];
-              cs[2 * g + 1] += v[4 * g + 1] + v[4 * g + 3];
-            }
-          } else {  // TC_DW
-            float* pc = P.c_part + split * P.M * P.N;
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              const int64_t col = cbase + 8 * g;
-              if (ina) store2(pc + ra * P.N + col, v[4 * g], v[4 * g + 1]);
-              if (inb) store2(pc + rb * P.N + col, v[4 * g + 2], v[4 * g + 3]);
+              bw[hh][(g < 4 ? 0 : 1)] |= pa << sh;
+              bw[hh][(g < 4 ? 2 : 3)] |= pb << sh;
             }
           }
-        }
-        if (dx && P.colsum) {
-          // sum over the 8 threads sharing t % 4 (the warp's 32 rows); lanes 0-3 then
-          // hold columns n0 + cb + 8 g + 2 lane + {0, 1}
+          if (P.c_bits) {
+            // the 4 threads of a row hold disjoint bits: OR them, one thread stores
 #pragma unroll
-          for (int o = 4; o <= 16; o <<= 1)
+            for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) cs[j] += __shfl_xor_sync(0xffffffffu, cs[j], o);
-          if (lane < 4) {
+              for (int o = 1; o <= 2; o <<= 1)
+#pragma unroll
+                for (int w = 0; w < 4; ++w) bw[hh][w] |= __shfl_xor_sync(0xffffffffu, bw[hh][w], o);
+              const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
+              if ((lane & 3) == 0) {
+                const int64_t wpr = P.N / 32, w0 = (n0 + cb) / 32;
+                if (ra < P.M) *reinterpret_cast<uint2*>(P.c_bits + ra * wpr + w0) = make_uint2(bw[hh][0], bw[hh][1]);
+                if (rb < P.M) *reinterpret_cast<uint2*>(P.c_bits + rb * wpr + w0) = make_uint2(bw[hh][2], bw[hh][3]);
+              }
+            }
+          }
+        } else if constexpr (dx) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            const int64_t col = cbase + 8 * g;
+            const uint32_t sh = (8 * g + tc) & 31;
+            float c0 = 0.f, c1 = 0.f;  // column sums of this thread's two columns
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              float* v = rs + 32 * hh;
+              const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
+              const bool ina = ra < P.M, inb = rb < P.M;
+              float2 ma, mb;
+              if constexpr (BITS) {
+                const uint2 wa = mw[2 * hh], wb = mw[2 * hh + 1];
+                const uint32_t xa = (g < 4 ? wa.x : wa.y) >> sh, xb = (g < 4 ? wb.x : wb.y) >> sh;
+                ma = make_float2((float)(xa & 1u), (float)((xa >> 1) & 1u));
+                mb = make_float2((float)(xb & 1u), (float)((xb >> 1) & 1u));
+              } else {
+                ma = ina ? __ldg(reinterpret_cast<const float2*>(P.mask + ra * P.N + col)) : make_float2(0.f, 0.f);
+                mb = inb ? __ldg(reinterpret_cast<const float2*>(P.mask + rb * P.N + col)) : make_float2(0.f, 0.f);
+              }
+              const float y0 = ma.x > 0.f ? v[4 * g] : 0.f, y1 = ma.y > 0.f ? v[4 * g + 1] : 0.f;
+              const float y2 = mb.x > 0.f ? v[4 * g + 2] : 0.f, y3 = mb.y > 0.f ? v[4 * g + 3] : 0.f;
+              if constexpr (KIND == TC_DX) {
+                float h0, l0, h1, l1, h2, l2, h3, l3;
+                tf32_split(y0, h0, l0);
+                tf32_split(y1, h1, l1);
+                tf32_split(y2, h2, l2);
+                tf32_split(y3, h3, l3);
+                if (ina) {
+                  store2(P.c_hi + ra * P.N + col, h0, h1);
+                  store2(P.c_lo + ra * P.N + col, l0, l1);
+                }
+                if (inb) {
+                  store2(P.c_hi + rb * P.N + col, h2, h3);
+                  store2(P.c_lo + rb * P.N + col, l2, l3);
+                }
+              } else {
+                if (ina) store2(P.c_hi + ra * P.N + col, y0, y1);
+                if (inb) store2(P.c_hi + rb * P.N + col, y2, y3);
+              }
+              c0 += y0 + y2;
+              c1 += y1 + y3;
+            }
+            if (P.colsum) {
+              // sum over the 8 threads sharing t % 4 (the warp's 32 rows); lanes 0-3 then
+              // hold columns n0 + cb + 8 g + 2 lane + {0, 1}
+#pragma unroll
+              for (int o = 4; o <= 16; o <<= 1) {
+                c0 += __shfl_xor_sync(0xffffffffu, c0, o);
+                c1 += __shfl_xor_sync(0xffffffffu, c1, o);
+              }
+              if (lane < 4) {
+                float* ca = colacc + q * P.N + n0 + cb + 8 * g + tc;
+                ca[0] += c0;
+                ca[1] += c1;
+              }
+            }
+          }
+        } else {  // TC_DW
+          float* pc = P.c_part + split * P.M * P.N;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float* v = rs + 32 * hh;
+            const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
-              float* ca = colacc + q * P.N + n0 + cb + 8 * g + tc;
-              ca[0] += cs[2 * g];
-              ca[1] += cs[2 * g + 1];
+              const int64_t col = cbase + 8 * g;
+              if (ra < P.M) store2(pc + ra * P.N + col, v[4 * g], v[4 * g + 1]);
+              if (rb < P.M) store2(pc + rb * P.N + col, v[4 * g + 2], v[4 * g + 3]);
             }
           }
         }
@@ -856,40 +904,85 @@ int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, u
 #endif
 bool use_pair(int kind) { return SPO_TC_PAIR != 0 && kind == TC_DW && sm_count() >= 2; }
 
-// CTA pairs that fit on the device at once (one CTA per SM; both SMs of a pair in one
-// GPC). A persistent grid larger than this would leave pairs waiting for a second wave.
-int pair_slots_query();
-int pair_slots() {
-  static std::mutex mu;
-  static int slots[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return sm_count() / 2;
-  std::lock_guard<std::mutex> lk(mu);
-  if (!slots[dev]) slots[dev] = pair_slots_query();
-  return slots[dev];
+#ifndef SPO_TC_BN256
+#define SPO_TC_BN256 1
+#endif
+// Output columns per tile: 256 for the epilogues that are light per element (dW partials,
+// the plain fp32 forward) when N allows it, else 128. The hi/lo forward and the dX products
+// keep 128: their final epilogue (split, masks, column sums, twice the stored bytes) must
+// finish within the slack of four 128-column accumulators, which two 256-column ones do
+// not give.
+int tile_n(int kind, bool fp32_fwd, int64_t N) {
+  const bool light = kind == TC_DW || (kind == TC_FWD && fp32_fwd);
+  return (SPO_TC_BN256 != 0 && light && N % 256 == 0) ? 256 : 128;
+}
+int tile_of(const TcGemmArgs& a) { return tile_n(a.kind, a.c_lo == nullptr, a.N); }
+
+int threads_of(bool pair, int bn) {
+  return bn == 256 ? (pair ? Geo<true, 256>::THREADS : Geo<false, 256>::THREADS)
+                   : (pair ? Geo<true, 128>::THREADS : Geo<false, 128>::THREADS);
 }
 
-size_t tc_smem_bytes(int kind, int64_t N, bool pair) {
-  size_t b = 1024 + (pair ? (size_t)Geo<true>::STAGES * Geo<true>::STAGE_BYTES
-                          : (size_t)Geo<false>::STAGES * Geo<false>::STAGE_BYTES) +
-             sizeof(Ctl);
+size_t ring_bytes(bool pair, int bn) {
+  if (bn == 256)
+    return pair ? (size_t)Geo<true, 256>::STAGES * Geo<true, 256>::STAGE_BYTES
+                : (size_t)Geo<false, 256>::STAGES * Geo<false, 256>::STAGE_BYTES;
+  return pair ? (size_t)Geo<true, 128>::STAGES * Geo<true, 128>::STAGE_BYTES
+              : (size_t)Geo<false, 128>::STAGES * Geo<false, 128>::STAGE_BYTES;
+}
+
+size_t tc_smem_bytes(int kind, int64_t N, bool pair, int bn) {
+  size_t b = 1024 + ring_bytes(pair, bn) + sizeof(Ctl);
   if (kind == TC_DX || kind == TC_DX_F32) b += (size_t)4 * N * sizeof(float);
   return b;
 }
 
-int64_t units_of(const TcGemmArgs& a, int* splits) {
-  const int64_t mt = ceil_div(a.M, use_pair(a.kind) ? 2 * BM : BM), nt = a.N / BN;
-  int sp = 1;
-  if (a.kind == TC_DW) sp = (int)ceil_div(a.K, a.k_chunk);
-  if (splits) *splits = sp;
-  return mt * nt * sp;
+using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const KParams);
+
+template <int TBN>
+Kern pick_kernel(int kind, bool pair, bool bits, bool has_lo) {
+  if (pair) return tc_gemm_kernel<TC_DW, false, true, TBN>;  // use_pair: dW only
+  switch (kind) {
+    case TC_FWD: return has_lo ? tc_gemm_kernel<TC_FWD, false, false, TBN> : tc_gemm_kernel<kFwdF32, false, false, TBN>;
+    case TC_DX: return bits ? tc_gemm_kernel<TC_DX, true, false, TBN> : tc_gemm_kernel<TC_DX, false, false, TBN>;
+    case TC_DX_F32:
+      return bits ? tc_gemm_kernel<TC_DX_F32, true, false, TBN> : tc_gemm_kernel<TC_DX_F32, false, false, TBN>;
+    default: return tc_gemm_kernel<TC_DW, false, false, TBN>;
+  }
 }
 
-int pair_slots_query() {
+// 256-column tiles exist for the light epilogues only (tile_n).
+Kern pick(int kind, bool pair, bool bits, bool has_lo, int bn) {
+  if (bn == 256) {
+    if (pair) return tc_gemm_kernel<TC_DW, false, true, 256>;
+    return kind == TC_DW ? tc_gemm_kernel<TC_DW, false, false, 256> : tc_gemm_kernel<kFwdF32, false, false, 256>;
+  }
+  return pick_kernel<128>(kind, pair, bits, has_lo);
+}
+
+// Opt an instantiation in to its shared memory once per device (never while a stream is
+// being captured: the first launch of each shape happens uncaptured).
+int opt_in(Kern kern, bool pair, int bn) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> opted;
+  int dev = 0;
+  SPO_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (!opted.count({dev, (const void*)kern})) {
+    SPO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)tc_smem_bytes(TC_DX, kMaxColsumN, pair, bn)));
+    opted.insert({dev, (const void*)kern});
+  }
+  return kOk;
+}
+
+// CTA pairs that fit on the device at once (one CTA per SM; both SMs of a pair in one
+// GPC). A persistent grid larger than this would leave pairs waiting for a second wave.
+int pair_slots_query(int bn) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = tc_smem_bytes(TC_DX, kMaxColsumN, true);  // the opt-in size of every launch
+  cfg.blockDim = dim3(threads_of(true, bn));
+  cfg.dynamicSmemBytes = tc_smem_bytes(TC_DX, kMaxColsumN, true, bn);  // the opt-in size of every launch
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -897,25 +990,55 @@ int pair_slots_query() {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  auto kern = tc_gemm_kernel<TC_DW, false, true>;
+  Kern kern = pick(TC_DW, true, false, true, bn);
   int n = 0;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)cfg.dynamicSmemBytes) != cudaSuccess ||
-      cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+  if (opt_in(kern, true, bn) != kOk || cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
     (void)cudaGetLastError();
     n = sm_count() / 2;
   }
   return n;
 }
 
+int pair_slots(int bn) {
+  static std::mutex mu;
+  static int slots[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return sm_count() / 2;
+  const int k = bn == 256 ? 1 : 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (slots[dev][k]) return slots[dev][k];
+  }
+  const int n = pair_slots_query(bn);
+  std::lock_guard<std::mutex> lk(mu);
+  slots[dev][k] = n;
+  return n;
+}
+
+int64_t units_of(const TcGemmArgs& a, int* splits) {
+  const int64_t mt = ceil_div(a.M, use_pair(a.kind) ? 2 * BM : BM), nt = a.N / tile_of(a);
+  int sp = 1;
+  if (a.kind == TC_DW) sp = (int)ceil_div(a.K, a.k_chunk);
+  if (splits) *splits = sp;
+  return mt * nt * sp;
+}
+
 }  // namespace
 
 bool tc_gemm_supported(int kind, int64_t M, int64_t N, int64_t K) {
-  if (M < 1 || N < 1 || K < 1 || N % BN != 0) return false;
+  if (M < 1 || N < 1 || K < 1 || N % 128 != 0) return false;
   if (kind == TC_DW) return M % BM == 0 && M <= (1 << 20) && N <= (1 << 20);
   if (K % BK != 0) return false;
   if ((kind == TC_DX || kind == TC_DX_F32) && N > kMaxColsumN) return false;
   return M < (int64_t(1) << 31);
+}
+
+int64_t tc_gemm_tiles(int kind, int64_t M, int64_t N) {
+  return ceil_div(M, use_pair(kind) ? 2 * BM : BM) * (N / tile_n(kind, false, N));
+}
+
+int tc_gemm_slots(int kind, int64_t N) {
+  return use_pair(kind) ? pair_slots(tile_n(kind, false, N)) : sm_count();
 }
 
 int tc_gemm_splits(const TcGemmArgs& a) {
@@ -926,7 +1049,7 @@ int tc_gemm_splits(const TcGemmArgs& a) {
 
 int tc_gemm_grid(const TcGemmArgs& a) {
   const int64_t u = units_of(a, nullptr);
-  if (use_pair(a.kind)) return 2 * (int)std::max<int64_t>(1, std::min<int64_t>(u, pair_slots()));
+  if (use_pair(a.kind)) return 2 * (int)std::max<int64_t>(1, std::min<int64_t>(u, pair_slots(tile_of(a))));
   return (int)std::max<int64_t>(1, std::min<int64_t>(u, sm_count()));
 }
 
@@ -950,7 +1073,8 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
     SPO_CHECK_ARG(reinterpret_cast<uintptr_t>(a.c_bits) % 8 == 0, kErrArg, "tc_gemm: c_bits alignment");
   const bool mn = a.kind == TC_DW;
   const bool pair = use_pair(a.kind);
-  const uint32_t b_rows = pair ? BN / 2 : BN;  // rows of B one CTA stages (K-major)
+  const int bn = tile_of(a);
+  const uint32_t b_rows = pair ? bn / 2 : bn;  // rows of B one CTA stages (K-major)
   CUtensorMap m_ah, m_al, m_bh, m_bl;
   int rc;
   if (mn) {  // A [K x M], B [K x N] row-major; boxes 32 wide (MN) x 32 deep (K)
@@ -975,7 +1099,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.K = a.K;
   P.k_chunk = mn ? a.k_chunk : align_up_i64(a.K, BK);
   P.m_tiles = (int)ceil_div(a.M, pair ? 2 * BM : BM);
-  P.n_tiles = (int)(a.N / BN);
+  P.n_tiles = (int)(a.N / bn);
   P.units = units_of(a, &P.splits);
   P.bias = a.bias;
   P.mask = a.mask;
@@ -987,41 +1111,14 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.mask_bits = a.kind == TC_DX || a.kind == TC_DX_F32 ? a.mask_bits : nullptr;
   P.c_bits = a.kind == TC_FWD && a.c_lo ? a.c_bits : nullptr;
   const int grid = tc_gemm_grid(a);
-  const size_t smem = tc_smem_bytes(a.kind, a.N, pair);
-  const bool bits = P.mask_bits != nullptr;
-  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const KParams);
-  Kern kern;
-  if (pair) {
-    kern = tc_gemm_kernel<TC_DW, false, true>;  // use_pair: dW only
-  } else {
-    switch (a.kind) {
-      case TC_FWD:
-        kern = a.c_lo ? tc_gemm_kernel<TC_FWD, false, false> : tc_gemm_kernel<kFwdF32, false, false>;
-        break;
-      case TC_DX: kern = bits ? tc_gemm_kernel<TC_DX, true, false> : tc_gemm_kernel<TC_DX, false, false>; break;
-      case TC_DX_F32:
-        kern = bits ? tc_gemm_kernel<TC_DX_F32, true, false> : tc_gemm_kernel<TC_DX_F32, false, false>;
-        break;
-      default: kern = tc_gemm_kernel<TC_DW, false, false>; break;
-    }
-  }
-  // the shared-memory opt-in is a per-device attribute of each instantiation
-  static std::mutex mu;
-  static std::set<std::pair<int, const void*>> opted;
-  int dev = 0;
-  SPO_CUDA_TRY(cudaGetDevice(&dev));
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (!opted.count({dev, (const void*)kern})) {
-      SPO_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)tc_smem_bytes(TC_DX, kMaxColsumN, pair)));
-      opted.insert({dev, (const void*)kern});
-    }
-  }
+  const size_t smem = tc_smem_bytes(a.kind, a.N, pair, bn);
+  const int threads = threads_of(pair, bn);
+  const Kern kern = pick(a.kind, pair, P.mask_bits != nullptr, a.c_lo != nullptr, bn);
+  if ((rc = opt_in(kern, pair, bn))) return rc;
   if (pair) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -1033,7 +1130,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
     cfg.numAttrs = 1;
     SPO_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_ah, m_al, m_bh, m_bl, P));
   } else {
-    kern<<<grid, kThreads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
+    kern<<<grid, threads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
   }
   SPO_LAUNCH_CHECK();
   return kOk;

@@ -51,6 +51,8 @@ struct TcGemmArgs {
 // Launch configuration queries (host).
 int tc_gemm_grid(const TcGemmArgs& a);     // CTAs the launch will use (= colsum parts)
 int tc_gemm_splits(const TcGemmArgs& a);   // TC_DW partial count
+int64_t tc_gemm_tiles(int kind, int64_t M, int64_t N);  // output tiles (units per split)
+int tc_gemm_slots(int kind, int64_t N);     // units that run at once (SMs or CTA pairs)
 bool tc_gemm_supported(int kind, int64_t M, int64_t N, int64_t K);
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s);
 
