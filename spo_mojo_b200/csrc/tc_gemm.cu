@@ -67,27 +67,32 @@ struct Geo {
   static constexpr int THREADS = 64 + EPI_THREADS;
 };
 // The tensor core's accumulation into TMEM is not exact fp32: its error grows with the
-// number of MMAs summed into one accumulator. Folding every 2 k-blocks (64 reduction
-// elements) keeps learner outputs near 1e-6 relative; 8 k-blocks measured 3-5e-6, enough
-// to flip ReLU decisions of activations within that distance of zero.
+// number of MMAs summed into one accumulator. The epilogue therefore folds each
+// accumulator into an fp32 running sum every SEG k-blocks; every fold is a TMEM read that
+// the tensor pipe waits for, so SEG trades precision for speed per product:
+//   forward  4 k-blocks: activations within 2.3e-6 of max (1e-6 at 2, 4e-6 at 8), their
+//            ReLU decisions what decides the backward's branches
+//   dX, dW   8 k-blocks: gradients within 6e-6 of max (4.5e-6 at 2), far inside the 1e-4
+//            gradient tolerance (measured on the 27-256x3-9, 27-512x3-9 and 27-1024x4-9
+//            actors against a float64 restatement)
 #ifndef SPO_TC_SEG
-#define SPO_TC_SEG 2
+#define SPO_TC_SEG 4
 #endif
 #ifndef SPO_TC_SEG_DX
 #define SPO_TC_SEG_DX 8
 #endif
-// k-blocks per TMEM accumulation: the forward (whose outputs decide ReLU masks) and dW
-// (long split-K sums with cancellation) fold every 2; the dX products, which decide
-// nothing and whose 3-5e-6 stays far inside the gradients' 1e-4 tolerance, every 8, which
-// saves three of every four accumulator reads (each one stalls the tensor pipe briefly).
+#ifndef SPO_TC_SEG_DW
+#define SPO_TC_SEG_DW 8
+#endif
+template <int KIND>
+__host__ __device__ constexpr int seg_of() {
+  return (KIND == 1 || KIND == 2) ? SPO_TC_SEG_DX : (KIND == 3 ? SPO_TC_SEG_DW : SPO_TC_SEG);
+}
+
 // Kernel-internal epilogue: the forward written as plain fp32 (TC_FWD with c_lo == null,
 // for an activation that no tensor-core product reads), without the mask bits.
 constexpr int kFwdF32 = 4;
 
-template <int KIND>
-__host__ __device__ constexpr int seg_of() {
-  return (KIND == 1 || KIND == 2) ? SPO_TC_SEG_DX : SPO_TC_SEG;
-}
 constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
 constexpr uint64_t kDrainNs = 500000000ull;              // 0.5 s
 constexpr int kMaxColsumN = 1024;

@@ -9,8 +9,8 @@
 // memory: the published error-compensated "3xTF32" method (the scheme CUTLASS calls
 // 3xTF32; Ootomo & Yokota 2022). Products of hi/lo halves are exact in the tensor core,
 // so the result carries near-fp32 error instead of TF32's 2^-11. The accumulator is
-// folded into an fp32 running sum every SPO_TC_SEG k-blocks to bound the error of the
-// tensor memory accumulation.
+// folded into an fp32 running sum every few k-blocks (4 for the forward, 8 for dX and dW)
+// to bound the error of the tensor memory accumulation.
 #pragma once
 
 #include "spo_common.cuh"
