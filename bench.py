@@ -248,10 +248,10 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
 
 
 # DRAM bytes (read + write) of one launch of the roofline kernel at 1,048,576 rows, from an
-# ncu capture of the same kernel at 262,144 rows (1.076 GB read + 1.029 GB write) scaled by
+# ncu capture of the same kernel at 262,144 rows (1.076 GB read + 1.045 GB write) scaled by
 # the 4x rows: the kernel streams its activations once, so traffic grows with the rows.
 TRAFFIC_PER_LAUNCH = {
-    ("tensor", 512): {"bytes": 4 * (1.075956e9 + 1.029005e9),
+    ("tensor", 512): {"bytes": 4 * (1.075955e9 + 1.044996e9),
                       "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum at 262144 rows x4"},
 }
 

@@ -1,9 +1,10 @@
 // Compute peaks of this GPU for the learner's two arithmetic paths, measured rather than
 // taken from a datasheet (the driver-measured peaks cover HBM and bf16 only):
 //
-// * tcgen05 TF32: one CTA per SM issues back-to-back tcgen05.mma.kind::tf32 128x128x8 with
-//   both operands in shared memory (random data), the instruction the 3xTF32 GEMM issues,
-//   into two TMEM accumulators; ends with a commit and a bounded wait.
+// * tcgen05 TF32: one CTA per SM issues back-to-back tcgen05.mma.kind::tf32 128x256x8 with
+//   both operands in shared memory (random data) into two TMEM accumulators; ends with a
+//   commit and a bounded wait. The 256-wide shape is the faster one (it reads A once for
+//   twice the columns; 128x128x8 reaches ~87 % of its rate), so this is the ceiling.
 // * FP32 FMA: every thread runs 8 independent chains of packed FFMA2 (two fp32 fma.rn per
 //   instruction, sm_100's widest FP32 issue), enough chains to cover the FMA latency.
 //
@@ -16,7 +17,9 @@ namespace spo {
 
 namespace {
 
-constexpr int kMmaSmem = 64 * 1024;
+// A [128 x 32] + B [256 x 32] fp32 (48 KB) in a buffer above half the shared memory, so
+// that one CTA (holding all 512 TMEM columns) runs per SM
+constexpr int kMmaSmem = 120 * 1024;
 constexpr uint64_t kWaitNs = 2000000000ull;
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
@@ -49,7 +52,7 @@ __global__ void __launch_bounds__(128, 1) tf32_mma_peak_kernel(int iters, int* e
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
         static_cast<uint32_t>(__cvta_generic_to_shared(&tbase))));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
@@ -60,10 +63,10 @@ __global__ void __launch_bounds__(128, 1) tf32_mma_peak_kernel(int iters, int* e
   if (threadIdx.x == 0) {
     const uint32_t s0 = static_cast<uint32_t>(__cvta_generic_to_shared(sm));
     const uint32_t a = s0, b = s0 + 32768;
-    const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (16u << 17) | (8u << 24);  // N 128, M 128
+    const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | (32u << 17) | (8u << 24);  // N 256, M 128
     for (int i = 0; i < iters; ++i) {
       const uint64_t ad = umma_desc(a + (i & 3) * 32), bd = umma_desc(b + (i & 3) * 32);
-      const uint32_t d = tbase + (uint32_t)(i & 1) * 128;
+      const uint32_t d = tbase + (uint32_t)(i & 1) * 256;
       asm volatile(
           "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
           "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(128, 1) tf32_mma_peak_kernel(int iters, int* e
   __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tbase));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tbase));
   }
 }
 
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(256) fp32_ffma2_peak_kernel(int iters, float s
 
 }  // namespace
 
-// TF32 tensor FLOP/s (2 * 128 * 128 * 8 per MMA) and FP32 FLOP/s (4 per FFMA2).
+// TF32 tensor FLOP/s (2 * 128 * 256 * 8 per MMA) and FP32 FLOP/s (4 per FFMA2).
 int measure_peaks(double* tf32_flops, double* fp32_flops, cudaStream_t s) {
   const int sms = sm_count();
   int* err = nullptr;
@@ -134,7 +137,7 @@ int measure_peaks(double* tf32_flops, double* fp32_flops, cudaStream_t s) {
   if (!rc && (e = cudaFuncSetAttribute(tf32_mma_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kMmaSmem + 1024)) != cudaSuccess)
     fail(e, "peaks: attribute");
-  const int mma_iters = 200000, fma_iters = 20000;
+  const int mma_iters = 100000, fma_iters = 20000;
   float ms = 0.f;
   if (!rc) {
     tf32_mma_peak_kernel<<<sms, 128, kMmaSmem + 1024, s>>>(1000, err);
@@ -150,7 +153,7 @@ int measure_peaks(double* tf32_flops, double* fp32_flops, cudaStream_t s) {
   }
   if (!rc) {
     cudaEventElapsedTime(&ms, e0, e1);
-    *tf32_flops = 2.0 * 128 * 128 * 8 * (double)mma_iters * sms / (ms * 1e-3);
+    *tf32_flops = 2.0 * 128 * 256 * 8 * (double)mma_iters * sms / (ms * 1e-3);
     const int blocks = 8 * sms;
     fp32_ffma2_peak_kernel<<<blocks, 256, 0, s>>>(100, 1.f, sink);
     cudaEventRecord(e0, s);
