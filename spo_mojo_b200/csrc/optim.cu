@@ -16,23 +16,42 @@ namespace {
 constexpr int kThreads = 256;
 
 // ---------------------------------------------------------------- reduction
+// A block takes 32 consecutive elements of a segment at a time; its 8 warps split the
+// parts (warp g sums parts g, g + 8, ..., four chains), so that a segment with few
+// elements and many parts still has enough loads in flight. The 8 group sums are then
+// added in group order: the result does not depend on scheduling.
+constexpr int kRedCols = 32;
+constexpr int kRedGroups = kThreads / kRedCols;
+
 __global__ void __launch_bounds__(kThreads) reduce_kernel(const ReduceParams P) {
-  const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t gstride = (int64_t)gridDim.x * blockDim.x;
+  __shared__ float gsum[kRedGroups][kRedCols + 1];
+  const int c = threadIdx.x % kRedCols, g = threadIdx.x / kRedCols;
   for (int s = 0; s < P.nseg; ++s) {
     const ReduceSeg sg = P.seg[s];
-    for (int64_t i = gtid; i < sg.count; i += gstride) {
-      const float* src = sg.src + i;
+    const int64_t chunks = (sg.count + kRedCols - 1) / kRedCols;
+    for (int64_t ch = blockIdx.x; ch < chunks; ch += gridDim.x) {
+      const int64_t i = ch * kRedCols + c;
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      int k = 0;
-      for (; k + 4 <= sg.parts; k += 4) {
-        a0 += __ldg(src + (int64_t)(k + 0) * sg.part_stride);
-        a1 += __ldg(src + (int64_t)(k + 1) * sg.part_stride);
-        a2 += __ldg(src + (int64_t)(k + 2) * sg.part_stride);
-        a3 += __ldg(src + (int64_t)(k + 3) * sg.part_stride);
+      if (i < sg.count) {
+        const float* src = sg.src + i;
+        int k = g;
+        for (; k + 3 * kRedGroups < sg.parts; k += 4 * kRedGroups) {
+          a0 += __ldg(src + (int64_t)k * sg.part_stride);
+          a1 += __ldg(src + (int64_t)(k + kRedGroups) * sg.part_stride);
+          a2 += __ldg(src + (int64_t)(k + 2 * kRedGroups) * sg.part_stride);
+          a3 += __ldg(src + (int64_t)(k + 3 * kRedGroups) * sg.part_stride);
+        }
+        for (; k < sg.parts; k += kRedGroups) a0 += __ldg(src + (int64_t)k * sg.part_stride);
       }
-      for (; k < sg.parts; ++k) a0 += __ldg(src + (int64_t)k * sg.part_stride);
-      sg.dst[i] = (a0 + a1) + (a2 + a3);
+      gsum[g][c] = (a0 + a1) + (a2 + a3);
+      __syncthreads();
+      if (g == 0 && i < sg.count) {
+        float v = gsum[0][c];
+#pragma unroll
+        for (int q = 1; q < kRedGroups; ++q) v += gsum[q][c];
+        sg.dst[i] = v;
+      }
+      __syncthreads();
     }
   }
 }
@@ -242,7 +261,7 @@ int reduce_launch(const ReduceParams& p, cudaStream_t s) {
   int64_t total = 0;
   for (int i = 0; i < p.nseg; ++i) total = std::max<int64_t>(total, p.seg[i].count);
   if (p.nseg == 0) return kOk;
-  const int grid = (int)std::min<int64_t>(ceil_div(total, kThreads), 4LL * sm_count());
+  const int grid = (int)std::min<int64_t>(ceil_div(total, kRedCols), 4LL * sm_count());
   reduce_kernel<<<std::max(grid, 1), kThreads, 0, s>>>(p);
   SPO_LAUNCH_CHECK();
   return kOk;
