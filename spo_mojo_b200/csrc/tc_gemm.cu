@@ -1,21 +1,19 @@
 // tcgen05 3xTF32 GEMM (see tc_gemm.cuh) — persistent, warp-specialised, sm_100a.
 //
-// CTA = 10 warps:
-//   warp 0     TMA producer (one thread): hi/lo tiles of A and B into a STAGES-deep ring
-//   warp 1     TMEM allocator + MMA issuer (one thread): 3 tcgen05.mma per 8-wide k-step
-//              (lo.hi, hi.lo, hi.hi) into one of NACC fp32 TMEM accumulators
-//   warps 2-9  epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (= tile rows) and one half
-//              of the tile's columns; it folds each accumulator into an fp32 running sum
-//              held in registers, releases the accumulator as soon as its tcgen05.ld has
-//              completed, and on the unit's last segment applies the fused bias/ReLU/mask/
-//              column sums, hi/lo split and stores to global memory
-// Tiles are 128 x 128 outputs; k-blocks are 32 fp32 (one 128-byte swizzle row). Operand
-// tiles are written by TMA with 128-byte swizzling; K-major operands are read by the
-// UMMA descriptors with SBO = 1024 B (8-row atoms) and a 32-byte start advance per
-// k-step, MN-major operands (the dW products) are loaded as 32-element-wide boxes with
-// LBO = 4096 B between boxes; TF32 MN-major operands need the 128-byte swizzle with
-// 32-byte atoms (TMA SWIZZLE_128B_ATOM_32B, descriptor layout type 1), whose k-groups
-// are 4 rows: SBO = 512 B.
+// CTA = warp 0 (TMA producer, one thread: hi/lo tiles of A and B into a STAGES-deep ring),
+// warp 1 (TMEM allocator + MMA issuer, one thread: 3 tcgen05.mma per 8-wide k-step —
+// lo.hi, hi.lo, hi.hi — into one of NACC fp32 TMEM accumulators) and 4 x (TBN / 64)
+// epilogue warps: warp w reads TMEM lanes 32*(w%4)..+31 (= tile rows) and 64 of the
+// tile's columns; it folds each accumulator into an fp32 running sum held in registers,
+// releases the accumulator as soon as its tcgen05.ld has completed, and on the unit's
+// last segment applies the fused bias/ReLU/mask/column sums, hi/lo split and stores to
+// global memory. Tiles are 128 x TBN outputs (TBN = 128 or 256); k-blocks are 32 fp32
+// (one 128-byte swizzle row). Operand tiles are written by TMA with 128-byte swizzling;
+// K-major operands are read by the UMMA descriptors with SBO = 1024 B (8-row atoms) and a
+// 32-byte start advance per k-step, MN-major operands (the dW products) are loaded as
+// 32-element-wide boxes with LBO = 4096 B between boxes; TF32 MN-major operands need the
+// 128-byte swizzle with 32-byte atoms (TMA SWIZZLE_128B_ATOM_32B, descriptor layout type
+// 1), whose k-groups are 4 rows: SBO = 512 B.
 //
 // Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA sets an abort
 // flag and the caller's error word, the producer waits (bounded) for its copies in
@@ -481,13 +479,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------ MMA issuer
     if (leader) {
-      const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)P.a_mn << 15) |
-                             ((uint32_t)P.b_mn << 16) | ((uint32_t)(BN >> 3) << 17) |
-                             ((uint32_t)(G::UNIT_M >> 4) << 24);
-      const uint32_t a_step = P.a_mn ? 1024u : 32u, b_step = P.b_mn ? 1024u : 32u;
-      const uint32_t a_lbo = P.a_mn ? 4096u : 16u, b_lbo = P.b_mn ? 4096u : 16u;
-      const uint32_t a_sbo = P.a_mn ? 512u : 1024u, b_sbo = P.b_mn ? 512u : 1024u;
-      const uint32_t a_lay = P.a_mn ? 1u : 2u, b_lay = P.b_mn ? 1u : 2u;
+      // dW reads both operands MN-major, every other product K-major
+      constexpr bool MN = KIND == TC_DW;
+      constexpr uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)MN << 15) |
+                                 ((uint32_t)MN << 16) | ((uint32_t)(BN >> 3) << 17) |
+                                 ((uint32_t)(G::UNIT_M >> 4) << 24);
+      constexpr uint32_t k_step = MN ? 1024u : 32u;  // bytes between 8-wide k-steps
+      constexpr uint32_t lbo = MN ? 4096u : 16u, sbo = MN ? 512u : 1024u, lay = MN ? 1u : 2u;
+      // Descriptors of stage 0, k-step 0. The start-address field is the low 14 bits of
+      // the low word ((shared address) >> 4, every operand below 256 KB), so the
+      // descriptor of another stage, half or k-step is the same high word and a low word
+      // plus ((byte offset) >> 4): one add per descriptor in the loop.
+      const uint64_t da0 = make_desc(smem0, lbo, sbo, lay);
+      const uint64_t db0 = make_desc(smem0 + 2 * A_TILE, lbo, sbo, lay);
+      const uint32_t da_lo = (uint32_t)da0, db_lo = (uint32_t)db0;
+      const uint64_t d_hi = da0 & 0xFFFFFFFF00000000ull;  // equal for A and B
       // Each unit's k-range is cut into segments of at most SEG k-blocks; every segment
       // gets a fresh accumulator (round robin over NACC), which the epilogue folds into its
       // fp32 running sum. Few accumulations per TMEM accumulator keep the sum fp32-accurate.
@@ -515,14 +521,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
               break;
             }
             tc_fence_after();
-            const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
-            const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
+            const uint32_t so = s * (STAGE_BYTES >> 4);
 #pragma unroll
             for (int ks = 0; ks < BK / 8; ++ks) {
-              const uint64_t adh = make_desc(a_hi + ks * a_step, a_lbo, a_sbo, a_lay);
-              const uint64_t adl = make_desc(a_lo + ks * a_step, a_lbo, a_sbo, a_lay);
-              const uint64_t bdh = make_desc(b_hi + ks * b_step, b_lbo, b_sbo, b_lay);
-              const uint64_t bdl = make_desc(b_lo + ks * b_step, b_lbo, b_sbo, b_lay);
+              const uint32_t ah = da_lo + so + ks * (k_step >> 4), bh = db_lo + so + ks * (k_step >> 4);
+              const uint64_t adh = d_hi | ah, adl = d_hi | (ah + (A_TILE >> 4));
+              const uint64_t bdh = d_hi | bh, bdl = d_hi | (bh + (B_TILE >> 4));
               const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
               if constexpr (PAIR) {
                 mma_tf32_pair(d, adl, bdh, idesc, accum);
