@@ -50,7 +50,11 @@ constexpr int kNW = kHeadThreads / 32;
 template <int A>
 __host__ __device__ constexpr int padded_actions() { return A == 1 ? 1 : (A + 3) & ~3; }
 
-__host__ __device__ constexpr int head_buffers(bool has_lo) { return has_lo ? 2 : 4; }
+// Tile buffers: the copies run NB - 1 tiles ahead. With lo halves 2 (the lo buffers take
+// the room); fp32 input: the critic (one output) 4 tiles of 4096 activations, the actor 2
+// of 8192 (two rows per warp in its logits phase; measured 2.11 vs 2.78 ms at c3's H = 512
+// against 4 x 4096, while the critic measured 1.05 vs 1.13 ms the other way round).
+__host__ __device__ constexpr int head_buffers(bool has_lo, int A) { return has_lo ? 2 : (A == 1 ? 4 : 2); }
 
 __device__ __forceinline__ float softplus_f(float x) {
   return log1pf(expf(-fabsf(x))) + fmaxf(x, 0.f);
@@ -88,7 +92,7 @@ head_kernel(const HeadParams p) {
   const int H = p.H;
   const int R = p.rows_per_tile;
   const bool has_lo = p.act_lo != nullptr;
-  const int NB = head_buffers(has_lo);     // tile buffers: copies run NB - 1 tiles ahead
+  const int NB = head_buffers(has_lo, A);  // tile buffers: copies run NB - 1 tiles ahead
   float* Ws = sm;                          // [H][AP]
   float* abuf = Ws + H * AP;               // [NB][R][H] (act; hi + lo after phase 2)
   float* lbuf = abuf + NB * R * H;         // [2][R][H] lo halves (NB == 2)
@@ -189,12 +193,14 @@ head_kernel(const HeadParams p) {
     const float* rz = rq + 2 * R * A;               // pi_old logits
     const bool from_cells = !p.mask && p.cells;
 
-    // 2. One warp per row: logits, loss, dz.
-    for (int r = warp; r < rows; r += kNW) {
-      float* arow = ahi + r * H;
-      const float* lrow = alo + r * H;
-      const int64_t row = r0 + r;
-      if constexpr (A == 1) {
+    // 2. Logits, loss and dz per row. A == 1: one warp per row. Otherwise a warp takes two
+    //    rows (r, r + 8) per pass, so each W read from shared memory serves both rows (the
+    //    W reads, three float4 per column and lane, are what bounds this phase).
+    if constexpr (A == 1) {
+      for (int r = warp; r < rows; r += kNW) {
+        float* arow = ahi + r * H;
+        const float* lrow = alo + r * H;
+        const int64_t row = r0 + r;
         float z = 0.f;
         for (int h = lane; h < H; h += 32) {
           float av = arow[h];
@@ -240,31 +246,50 @@ head_kernel(const HeadParams p) {
           dzs[r] = dz;
           dbl += dz;
         }
-      } else {
-      // action pairs as packed FFMA2 (two fp32 fma.rn each: the fmaf results)
-      float2 zp2[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) zp2[a] = make_float2(0.f, 0.f);
-      for (int h = lane; h < H; h += 32) {
-        float av = arow[h];
-        if (has_lo) {
-          av += lrow[h];
-          arow[h] = av;
-        }
-        const float2 aa = make_float2(av, av);
-        const float4* w4 = reinterpret_cast<const float4*>(Ws + h * AP);
-#pragma unroll
-        for (int c = 0; c < AP / 4; ++c) {
-          const float4 w = w4[c];
-          zp2[2 * c] = __ffma2_rn(aa, make_float2(w.x, w.y), zp2[2 * c]);
-          zp2[2 * c + 1] = __ffma2_rn(aa, make_float2(w.z, w.w), zp2[2 * c + 1]);
-        }
       }
+    } else {
+      for (int r = warp; r < rows; r += 2 * kNW) {
+        const int r2 = r + kNW;
+        const bool two = r2 < rows;  // warp-uniform
+        float* arow0 = ahi + r * H;
+        float* arow1 = ahi + (two ? r2 : r) * H;
+        const float* lrow0 = alo + r * H;
+        const float* lrow1 = alo + (two ? r2 : r) * H;
+        // action pairs as packed FFMA2 (two fp32 fma.rn each: the fmaf results)
+        float2 zp2[2][8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) zp2[0][a] = zp2[1][a] = make_float2(0.f, 0.f);
+        for (int h = lane; h < H; h += 32) {
+          float av0 = arow0[h], av1 = arow1[h];
+          if (has_lo) {
+            av0 += lrow0[h];
+            av1 += lrow1[h];
+            arow0[h] = av0;
+            if (two) arow1[h] = av1;
+          }
+          const float2 aa0 = make_float2(av0, av0), aa1 = make_float2(av1, av1);
+          const float4* w4 = reinterpret_cast<const float4*>(Ws + h * AP);
+#pragma unroll
+          for (int c = 0; c < AP / 4; ++c) {
+            const float4 w = w4[c];
+            const float2 wa = make_float2(w.x, w.y), wb = make_float2(w.z, w.w);
+            zp2[0][2 * c] = __ffma2_rn(aa0, wa, zp2[0][2 * c]);
+            zp2[0][2 * c + 1] = __ffma2_rn(aa0, wb, zp2[0][2 * c + 1]);
+            zp2[1][2 * c] = __ffma2_rn(aa1, wa, zp2[1][2 * c]);
+            zp2[1][2 * c + 1] = __ffma2_rn(aa1, wb, zp2[1][2 * c + 1]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (k == 1 && !two) break;
+          const int rr = k ? r2 : r;
+          const int64_t row = r0 + rr;
+          const float2* zk = zp2[k];
       float zp[16];
 #pragma unroll
       for (int a = 0; a < 8; ++a) {
-        zp[2 * a] = zp2[a].x;
-        zp[2 * a + 1] = zp2[a].y;
+        zp[2 * a] = zk[a].x;
+        zp[2 * a + 1] = zk[a].y;
       }
       // transpose-reduce: lane L ends with the sum of zp[L & 15] over the warp
 #pragma unroll
@@ -282,7 +307,7 @@ head_kernel(const HeadParams p) {
       float dz = 0.f;
       if (p.mode == kHeadCritic) {
         if (lvalid) {
-          const float d = zv - rq[r * A + la];
+          const float d = zv - rq[rr * A + la];
           dz = d * p.scale;
           const float l2 = half_sum(0.5f * d * d * p.scale);
           if (lane == 0) st[kStatCriticLoss] += l2;
@@ -293,9 +318,9 @@ head_kernel(const HeadParams p) {
       } else {
         float mk = 1.f, qv = 0.f;
         if (lvalid) {
-          const float m = rm[r * A + la];
+          const float m = rm[rr * A + la];
           mk = p.mask ? m : (from_cells ? (m == 0.f ? 1.f : 0.f) : 1.f);
-          qv = rq[r * A + la];
+          qv = rq[rr * A + la];
         }
         const float zm = (!lvalid || mk == 0.f) ? kNegInf : zv;
         const float mx = half_max(zm);
@@ -307,7 +332,7 @@ head_kernel(const HeadParams p) {
         const float lp = zm - lse;
         float po = 0.f, klo_t = 0.f;
         if (p.z_old != nullptr) {
-          const float zo = (!lvalid || mk == 0.f) ? kNegInf : rz[r * A + la];
+          const float zo = (!lvalid || mk == 0.f) ? kNegInf : rz[rr * A + la];
           const float mxo = half_max(zo);
           const float eo = lvalid ? expf(zo - mxo) : 0.f;
           const float so = half_sum(eo);
@@ -335,7 +360,9 @@ head_kernel(const HeadParams p) {
         if (p.dz_out) p.dz_out[row * A + la] = dz;
         dbl += dz;
       }
-      if (lane < AP) dzs[r * AP + lane] = dz;  // dz is 0 on the padding lanes
+      if (lane < AP) dzs[rr * AP + lane] = dz;  // dz is 0 on the padding lanes
+
+        }
       }
     }
     __syncthreads();
@@ -503,20 +530,23 @@ int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
 
 }  // namespace
 
-// 4096 activations per tile buffer (16 KB), at most 64 rows (the per-row loss inputs of
-// narrow layers stay small): two CTAs per SM
-int head_rows_per_tile(int H) { return std::max(1, std::min(64, 4096 / H)); }
+// Activations per tile buffer: 4096 (16 KB), or 8192 (32 KB, two rows per warp in the
+// logits phase at H = 512) for the actor's fp32 input; at most 64 rows (the per-row loss
+// inputs of narrow layers stay small): two CTAs per SM
+int head_rows_per_tile(int H, bool has_lo, int A) {
+  return std::max(1, std::min(64, (has_lo || A == 1 ? 4096 : 8192) / H));
+}
 
 size_t head_smem_bytes(int H, int A, bool has_lo) {
-  const int R = head_rows_per_tile(H);
+  const int R = head_rows_per_tile(H, has_lo, A);
   const int AP = A == 1 ? 1 : (A + 3) & ~3;
-  const size_t nb = head_buffers(has_lo);
+  const size_t nb = head_buffers(has_lo, A);
   return sizeof(float) * ((size_t)H * AP + (nb + (has_lo ? 2 : 0)) * (size_t)R * H + (size_t)R * AP +
                           (size_t)kNW * (AP + kStats) + 3 * nb * (size_t)R * A);
 }
 
 int head_grid(int64_t M, int H) {
-  const int64_t tiles = ceil_div(M, head_rows_per_tile(H));
+  const int64_t tiles = ceil_div(M, head_rows_per_tile(H, true, 1));  // the smaller tiles: an upper bound
   const int64_t cap = 2LL * sm_count();
   return (int)std::max<int64_t>(1, std::min<int64_t>(tiles, cap));
 }
@@ -533,7 +563,7 @@ int head_launch(HeadParams p, int grid, cudaStream_t s) {
   SPO_CHECK_ARG(!p.cells || p.mask || p.A == 9, kErrUnsupported, "head: board cells need 9 actions");
   SPO_CHECK_ARG(p.mode == kHeadCritic ? p.target != nullptr : p.q != nullptr, kErrArg,
                 "head: missing loss inputs");
-  p.rows_per_tile = head_rows_per_tile(p.H);
+  p.rows_per_tile = head_rows_per_tile(p.H, p.act_lo != nullptr, p.A);
   const size_t smem = head_smem_bytes(p.H, p.A, p.act_lo != nullptr);
   if (p.M == 0) return kOk;
   return p.A == 9 ? launch_a<9>(p, grid, smem, s) : launch_a<1>(p, grid, smem, s);

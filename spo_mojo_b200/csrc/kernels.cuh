@@ -48,7 +48,7 @@ struct HeadParams {
   float* stats_part;       // optional [grid][kStats]
 };
 
-int head_rows_per_tile(int H);
+int head_rows_per_tile(int H, bool has_lo, int A);
 size_t head_smem_bytes(int H, int A, bool has_lo);
 int head_grid(int64_t M, int H);
 int head_launch(HeadParams p, int grid, cudaStream_t s);
