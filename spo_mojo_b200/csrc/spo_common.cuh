@@ -89,10 +89,11 @@ __device__ __forceinline__ float tf32_rna(float x) {
 
 // Both halves are rounded to nearest and are exact TF32 values, so the tensor core sees
 // them unchanged: hi = rna(v), lo = rna(v - hi) (v - hi is exact in fp32). The part
-// dropped, v - hi - lo, is below 2^-22 |v| and unbiased.
+// dropped, v - hi - lo, is below 2^-22 |v| and unbiased. v - hi is finite whenever v is,
+// so lo skips the Inf/NaN test (for a non-finite v, hi carries it).
 __device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
   hi = tf32_rna(v);
-  lo = tf32_rna(v - hi);
+  lo = __uint_as_float((__float_as_uint(v - hi) + 0x1000u) & 0xffffe000u);
 }
 
 // Split of a ReLU output: a positive value never maps to hi == 0 (tiny subnormals keep
