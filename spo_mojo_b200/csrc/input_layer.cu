@@ -16,8 +16,8 @@
 //
 // Weight gradient: dW[k x n] = x^T dY summed over rows, dY [rows x n].
 // CTA = 256 threads over one chunk of rows and 512 columns: thread t owns the 4 columns
-// 4 (t % 128) .. +3 of its column block and one half of the k features (t / 128), so its
-// accumulators are [half of k] x 4. Rows are walked in blocks of kRows: the block's x rows
+// 4 (t % 128) .. +3 of its column block and one half of the k features (t / 128: 16
+// feature slots, or 14 when k <= 28), so its accumulators are [half of k] x 4. Rows are walked in blocks of kRows: the block's x rows
 // are staged in shared memory (zero-padded to 32 features) and read as broadcasts, the dY
 // float4 of each row is loaded straight from global memory, 8 rows in flight per thread.
 // Each CTA writes its partial [k x n] tile to part[chunk]; a deterministic reduction adds
@@ -32,7 +32,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kCols = 512;       // columns per CTA (128 threads x float4)
 constexpr int kMaxK = 32;
-constexpr int kHalf = kMaxK / 2;  // features per thread
 constexpr int kRows = 64;        // rows staged per block
 constexpr int kUnroll = 8;
 constexpr int kCells = 9;        // board cells per row (cells input)
@@ -93,6 +92,10 @@ struct XStage {
   __device__ static void wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 };
 
+// KH features per thread: 16 (any k <= 32), or 14 when k <= 28 (the 27-wide board input:
+// 28 feature slots instead of 32, one in eight packed FMAs fewer; the x pairs of the
+// second half start at feature 14 and are read as float2).
+template <int KH>
 __global__ void __launch_bounds__(kThreads, 2)
 dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, const float* __restrict__ dy,
                  int64_t rows, int k, int64_t n, int64_t chunk, float* __restrict__ part) {
@@ -104,16 +107,16 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
   const bool col_ok = col < n;
   const int64_t r_begin = (int64_t)blockIdx.x * chunk;
   const int64_t r_end = min(rows, r_begin + chunk);
-  const int i0 = half * kHalf;
+  const int i0 = half * KH;
 
   // per column, adjacent features as packed pairs: one FFMA2 (two fp32 fma.rn, the same
   // results as fmaf) per pair; the x pairs come straight from the staged float4 reads and
   // only the dY value is broadcast into a pair
-  float2 acc[4][kHalf / 2];
+  float2 acc[4][KH / 2];
 #pragma unroll
   for (int q = 0; q < 4; ++q)
 #pragma unroll
-    for (int i = 0; i < kHalf / 2; ++i) acc[q][i] = make_float2(0.f, 0.f);
+    for (int i = 0; i < KH / 2; ++i) acc[q][i] = make_float2(0.f, 0.f);
 
   XStage st{xs2, cs2, x, cells, k, r_begin, r_end};
   st.clear(tid, kThreads);
@@ -139,16 +142,26 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
                              : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-          const float4* xr = reinterpret_cast<const float4*>(&xs[r0 + u][i0]);
           const float gv[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
+          if constexpr (KH == 16) {
+            const float4* xr = reinterpret_cast<const float4*>(&xs[r0 + u][i0]);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 gg = make_float2(gv[q], gv[q]);
+            for (int q = 0; q < 4; ++q) {
+              const float2 gg = make_float2(gv[q], gv[q]);
 #pragma unroll
-            for (int c = 0; c < kHalf / 4; ++c) {
-              const float4 xv = xr[c];
-              acc[q][2 * c] = __ffma2_rn(make_float2(xv.x, xv.y), gg, acc[q][2 * c]);
-              acc[q][2 * c + 1] = __ffma2_rn(make_float2(xv.z, xv.w), gg, acc[q][2 * c + 1]);
+              for (int c = 0; c < KH / 4; ++c) {
+                const float4 xv = xr[c];
+                acc[q][2 * c] = __ffma2_rn(make_float2(xv.x, xv.y), gg, acc[q][2 * c]);
+                acc[q][2 * c + 1] = __ffma2_rn(make_float2(xv.z, xv.w), gg, acc[q][2 * c + 1]);
+              }
+            }
+          } else {
+            const float2* xr = reinterpret_cast<const float2*>(&xs[r0 + u][i0]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 gg = make_float2(gv[q], gv[q]);
+#pragma unroll
+              for (int c = 0; c < KH / 2; ++c) acc[q][c] = __ffma2_rn(xr[c], gg, acc[q][c]);
             }
           }
         }
@@ -160,7 +173,7 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
   if (!col_ok) return;
   float* out = part + (int64_t)blockIdx.x * k * n;
 #pragma unroll
-  for (int i = 0; i < kHalf; ++i) {
+  for (int i = 0; i < KH; ++i) {
     const int f = i0 + i;
     if (f < k) {
       auto pick = [&](int q) { return (i & 1) ? acc[q][i / 2].y : acc[q][i / 2].x; };
@@ -350,7 +363,10 @@ int dw_skinny_launch(LayerInput in, const float* dy, int64_t rows, int64_t k, in
   if (parts) *parts = (int)p;
   if (p == 0) return kOk;
   dim3 grid((unsigned)p, (unsigned)ceil_div(n, kCols));
-  dw_skinny_kernel<<<grid, kThreads, 0, s>>>(in.x, in.cells, dy, rows, (int)k, n, chunk, part);
+  if (k <= 28)
+    dw_skinny_kernel<14><<<grid, kThreads, 0, s>>>(in.x, in.cells, dy, rows, (int)k, n, chunk, part);
+  else
+    dw_skinny_kernel<16><<<grid, kThreads, 0, s>>>(in.x, in.cells, dy, rows, (int)k, n, chunk, part);
   SPO_LAUNCH_CHECK();
   return kOk;
 }
