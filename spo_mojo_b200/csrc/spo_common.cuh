@@ -78,32 +78,31 @@ __device__ __forceinline__ float warp_max(float v) {
 // value with 10 mantissa bits.
 // Round to TF32 (10 explicit mantissa bits), to nearest with ties away from zero, on the
 // integer pattern: add half a TF32 ulp to the magnitude and clear the 13 dropped bits (a
-// carry into the exponent is the correct rounding up). Equal to cvt.rna.tf32.f32 for every
-// finite input (checked over all 2^32 patterns); Inf and NaN pass through unchanged. Two
-// integer ALU operations instead of a conversion-unit instruction.
+// carry into the exponent is the correct rounding up, to infinity past the largest TF32
+// value). Equal to cvt.rna.tf32.f32 for every finite input (checked over all 2^32
+// patterns); infinities and quiet NaNs come out unchanged (a NaN whose payload lies only
+// in the 13 dropped bits would become an infinity). Two integer ALU operations instead of
+// a conversion-unit instruction.
 __device__ __forceinline__ float tf32_rna(float x) {
-  const uint32_t u = __float_as_uint(x);
-  const uint32_t r = (u & 0x7f800000u) == 0x7f800000u ? u : ((u + 0x1000u) & 0xffffe000u);
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 
 // Both halves are rounded to nearest and are exact TF32 values, so the tensor core sees
 // them unchanged: hi = rna(v), lo = rna(v - hi) (v - hi is exact in fp32). The part
-// dropped, v - hi - lo, is below 2^-22 |v| and unbiased. v - hi is finite whenever v is,
-// so lo skips the Inf/NaN test (for a non-finite v, hi carries it).
+// dropped, v - hi - lo, is below 2^-22 |v| and unbiased.
 __device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
   hi = tf32_rna(v);
-  lo = __uint_as_float((__float_as_uint(v - hi) + 0x1000u) & 0xffffe000u);
+  lo = tf32_rna(v - hi);
 }
 
-// Split of a ReLU output: a positive value never maps to hi == 0 (tiny subnormals keep
-// their full value in hi), so the mask of the layer below can be read from hi alone.
+// Split of a ReLU output (v >= 0): a positive value never maps to hi == 0 (the tiny
+// subnormals that round to 0 keep their full value in hi, and lo = 0), so the mask of the
+// layer below can be read from hi alone.
 __device__ __forceinline__ void tf32_split_pos(float v, float& hi, float& lo) {
-  tf32_split(v, hi, lo);
-  if (hi == 0.f && v > 0.f) {
-    hi = v;
-    lo = 0.f;
-  }
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t h = (u + 0x1000u) & 0xffffe000u;
+  hi = __uint_as_float(h != 0u ? h : u);
+  lo = tf32_rna(v - hi);
 }
 
 }  // namespace spo
