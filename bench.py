@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--engine", default="tensor", choices=["tensor", "cuda"],
                     help="tensor: tcgen05 3xTF32 for the hidden layers; cuda: fp32 FMA everywhere")
+    ap.add_argument("--graph", action="store_true",
+                    help="replay each learner step as one CUDA graph (one GPU; for the small, "
+                         "launch-bound workloads)")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the global batch (profiling of small cases only; not a bench line)")
     ap.add_argument("--peaks", action="store_true",
@@ -305,16 +308,42 @@ def run_ours(args):
     stream = torch.cuda.Stream(dev)
     scale = 1.0 / B
 
-    def step(b):
+    def eager_step(b):
         L.backward(b, grad_scale=scale, stream=stream)
         if comm is not None:
             comm.allreduce_(L.grads, stream=stream)
         L.apply(stream=stream)
 
+    if args.graph and world > 1:
+        raise SystemExit("--graph runs on one GPU")
+    graphs = {}
+
+    def capture(b):
+        """One learner step on the batch tensors b recorded as a CUDA graph (the kernels
+        neither allocate nor synchronise; the Adam step counter lives on the device)."""
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            eager_step(b)
+        torch.cuda.synchronize(dev)
+        return g
+
+    def step(b):
+        if not args.graph:
+            eager_step(b)
+            return
+        key = id(b)
+        if key not in graphs:
+            graphs[key] = (capture(b), b)
+        with torch.cuda.stream(stream):
+            graphs[key][0].replay()
+
     torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            step(batch)
+            eager_step(batch)  # first launches set kernel attributes, outside any capture
+    if args.graph:
+        step(batch)  # capture (the capture records, it does not run) and one replay, untimed
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -326,16 +355,41 @@ def run_ours(args):
             gpu_index = int(vis.split(",")[local])
         except ValueError:
             gpu_index = vis.split(",")[local]
+    # A step whose inputs and activations fit in L2 is timed one step at a time, with a
+    # write of twice the L2 size between steps (outside the timed events), so no step
+    # reads what the previous one left in L2.
+    in_bytes = sum(v.nbytes for v in batch_np.values())
+    act_bytes = rows * sum(sum(n.dims[1:-1]) for n in (wl.actor, wl.critic) if n) * 4
+    flush = in_bytes + act_bytes < L2_BYTES
+    flush_buf = torch.empty(L2_BYTES // 2, dtype=torch.float32, device=dev) if flush else None
+
+    def flushed_ms(one):
+        """Average event-timed duration of one(i) over the steps, L2 flushed before each."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(stream):
+            for i, (a, b) in enumerate(evs):
+                flush_buf.fill_(float(i))
+                a.record(stream)
+                one(i)
+                b.record(stream)
+        evs[-1][1].synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / args.steps
+
     clocks = ClockSampler(gpu_index)
     clocks.start()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(dev)
-    t0.record(stream)
-    for _ in range(args.steps):
-        step(batch)
-    t1.record(stream)
-    t1.synchronize()
-    ms = t0.elapsed_time(t1) / args.steps
+    if flush:
+        ms = flushed_ms(lambda i: step(batch))
+    else:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step(batch)
+        t1.record(stream)
+        t1.synchronize()
+        ms = t0.elapsed_time(t1) / args.steps
     clk = clocks.stop()
     ms_max = ms
     if world > 1:
@@ -354,24 +408,40 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
         feed = HostFeed(host, dev, stream)
+        if args.graph:
+            for buf in feed.bufs:  # one graph per feed buffer, captured before the timed region
+                graphs[id(buf)] = (capture(buf), buf)
         torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         w0 = time.perf_counter()
-        e0.record(stream)
-        feed.copy.wait_stream(stream)  # every upload starts inside the timed region
-        with torch.cuda.stream(stream):
-            j = feed.upload(host)
-            for i in range(args.steps):
-                b = feed.take(j)
-                nxt = feed.upload(host) if i + 1 < args.steps else None  # overlaps step i
-                step(b)
-                feed.release(j)
+        if flush:
+            # one step at a time: upload on the step's stream, the step, the read-back
+            dbuf = feed.bufs[0]
+
+            def e2e_step(i):
+                for k, v in host.items():
+                    dbuf[k].copy_(v, non_blocking=True)
+                step(dbuf)
                 stats_host.copy_(L.stats_tensor(), non_blocking=True)
-                j = nxt
-        e1.record(stream)
-        e1.synchronize()
+
+            ems = flushed_ms(e2e_step)
+        else:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            feed.copy.wait_stream(stream)  # every upload starts inside the timed region
+            with torch.cuda.stream(stream):
+                j = feed.upload(host)
+                for i in range(args.steps):
+                    b = feed.take(j)
+                    nxt = feed.upload(host) if i + 1 < args.steps else None  # overlaps step i
+                    step(b)
+                    feed.release(j)
+                    stats_host.copy_(L.stats_tensor(), non_blocking=True)
+                    j = nxt
+            e1.record(stream)
+            e1.synchronize()
+            ems = e0.elapsed_time(e1) / args.steps
+        torch.cuda.synchronize(dev)
         wall = (time.perf_counter() - w0) * 1e3 / args.steps
-        ems = e0.elapsed_time(e1) / args.steps
         if world > 1:
             tm = torch.tensor([ems], device=dev)
             dist.all_reduce(tm, op=dist.ReduceOp.MAX)
@@ -405,9 +475,12 @@ def run_ours(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": wl.describe(), "global_batch": B, "rows_per_rank": rows,
                        "parallelism": f"dp{world}",
-                       "l2": "working set per step > L2 (inputs %.0f MB, activations %.1f GB); no flush"
-                             % (sum(v.nbytes for v in batch_np.values()) / 1e6,
-                                rows * sum(sum(n.dims[1:-1]) for n in (wl.actor, wl.critic) if n) * 4 / 1e9)},
+                       "launch": "CUDA graph per step" if args.graph else "stream launches",
+                       "l2": ("working set per step < L2 (inputs %.2f MB, activations %.2f MB): "
+                              "each step timed alone, a %d MB write between steps flushes L2"
+                              % (in_bytes / 1e6, act_bytes / 1e6, 2 * L2_BYTES // 2**20)) if flush else
+                             ("working set per step > L2 (inputs %.0f MB, activations %.1f GB); no flush"
+                              % (in_bytes / 1e6, act_bytes / 1e9))},
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
             "gpu_launches": count_launches(wl, clip, args.engine) * args.steps,
             "engine": args.engine,

@@ -74,30 +74,32 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // TF32 hi/lo split of an fp32 value (the operand format of the 3xTF32 tensor-core GEMM).
-// Round-to-nearest (ties away) conversion to TF32: the fp32 bit pattern of the nearest
-// value with 10 mantissa bits.
+//
 // Round to TF32 (10 explicit mantissa bits), to nearest with ties away from zero, on the
 // integer pattern: add half a TF32 ulp to the magnitude and clear the 13 dropped bits (a
 // carry into the exponent is the correct rounding up, to infinity past the largest TF32
 // value). Equal to cvt.rna.tf32.f32 for every finite input (checked over all 2^32
-// patterns); infinities and quiet NaNs come out unchanged (a NaN whose payload lies only
-// in the 13 dropped bits would become an infinity). Two integer ALU operations instead of
-// a conversion-unit instruction.
+// patterns) and for both infinities, in two integer ALU operations instead of a
+// conversion-unit instruction. Not for NaN: for the patterns 0x7ffff000-0x7fffffff (CUDA's
+// canonical NaN among them) and 0xfffff000-0xffffffff the carry runs into the sign bit or
+// out of the word and the result is -0 or +0; tf32_split below keeps NaN itself.
 __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 
 // Both halves are rounded to nearest and are exact TF32 values, so the tensor core sees
 // them unchanged: hi = rna(v), lo = rna(v - hi) (v - hi is exact in fp32). The part
-// dropped, v - hi - lo, is below 2^-22 |v| and unbiased.
+// dropped, v - hi - lo, is below 2^-22 |v| and unbiased. A NaN goes into hi unchanged (a
+// NaN gradient or weight stays NaN through the products it enters; lo is then
+// irrelevant); for an infinite v, hi carries it.
 __device__ __forceinline__ void tf32_split(float v, float& hi, float& lo) {
-  hi = tf32_rna(v);
+  hi = v == v ? tf32_rna(v) : v;
   lo = tf32_rna(v - hi);
 }
 
-// Split of a ReLU output (v >= 0): a positive value never maps to hi == 0 (the tiny
-// subnormals that round to 0 keep their full value in hi, and lo = 0), so the mask of the
-// layer below can be read from hi alone.
+// Split of a ReLU output (v >= 0, computed as v > 0 ? v : 0, so never NaN): a positive
+// value never maps to hi == 0 (the tiny subnormals that round to 0 keep their full value
+// in hi, and lo = 0), so the mask of the layer below can be read from hi alone.
 __device__ __forceinline__ void tf32_split_pos(float v, float& hi, float& lo) {
   const uint32_t u = __float_as_uint(v);
   const uint32_t h = (u + 0x1000u) & 0xffffe000u;

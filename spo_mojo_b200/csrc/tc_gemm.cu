@@ -829,10 +829,11 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
   const int64_t gs = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gs) {
     float h, l;
-    if (keep_positive)
-      tf32_split_pos(x[i], h, l);
+    const float v = x[i];
+    if (keep_positive && v == v)  // a NaN takes the general split, which keeps it
+      tf32_split_pos(v, h, l);
     else
-      tf32_split(x[i], h, l);
+      tf32_split(v, h, l);
     hi[i] = h;
     lo[i] = l;
   }

@@ -55,6 +55,26 @@ def test_split_halves_are_tf32_and_close():
     assert torch.all(err <= x.double().abs() * 2.0 ** -22)
 
 
+@pytest.mark.parametrize("keep_positive", [0, 1])
+def test_split_keeps_nan_and_infinities(keep_positive):
+    """NaN (CUDA's canonical 0x7fffffff, its negation, a quiet and a payload-only NaN) stays
+    NaN in hi, infinities stay infinite, the largest finite floats round to infinity as
+    cvt.rna does, and tiny positive subnormals keep their value in hi for ReLU outputs."""
+    f = ffi()
+    pats = [0x7FFFFFFF, 0xFFFFFFFF, 0x7FC00000, 0x7F800001, 0x7FFFF000, 0xFFFFF000,
+            0x7F800000, 0xFF800000, 0x7F7FFFFF, 0x00000001, 0x00000FFF, 0x3F800000]
+    x = torch.tensor(np.array(pats, dtype=np.uint32).view(np.int32), device="cuda").view(torch.float32)
+    hi, lo = torch.empty_like(x), torch.empty_like(x)
+    f.call("spo_split_tf32", None, hi.data_ptr(), lo.data_ptr(), x.data_ptr(), x.numel(), keep_positive)
+    torch.cuda.synchronize()
+    h = hi.cpu().numpy()
+    assert np.all(np.isnan(h[:6]))
+    assert h[6] == np.inf and h[7] == -np.inf and h[8] == np.inf
+    if keep_positive:
+        assert h[9] > 0 and h[10] > 0 and lo.cpu().numpy()[9] == 0
+    assert h[11] == 1.0 and lo.cpu().numpy()[11] == 0
+
+
 @pytest.mark.parametrize("M,K,N", [(128, 128, 128), (1000, 256, 256), (4096, 512, 512), (300, 1024, 1024)])
 def test_forward_bias_relu(M, K, N):
     f = ffi()
