@@ -626,7 +626,7 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
     hp.mode = kHeadCritic;
     hp.target = b.target;
   }
-  const int gh = head_grid(rows, hl);
+  const int gh = head_grid(hp);
   if (rows > 0) {
     rc = head_launch(hp, gh, s);
     if (rc) return rc;
@@ -1018,7 +1018,7 @@ static int head_common(cudaStream_t s, HeadParams hp, float* dw, float* db, floa
   hp.db_part = c.take<float>((size_t)(g * hp.A));
   hp.dbx_part = c.take<float>((size_t)(g * hp.H));
   hp.stats_part = c.take<float>((size_t)(g * kStats));
-  const int grid = head_grid(hp.M, hp.H);
+  const int grid = head_grid(hp);
   const int parts = hp.M > 0 ? grid : 0;
   if (hp.M > 0) {
     int rc = head_launch(hp, grid, s);

@@ -532,21 +532,33 @@ int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
 
 // Activations per tile buffer: 4096 (16 KB), or 8192 (32 KB, two rows per warp in the
 // logits phase at H = 512) for the actor's fp32 input; at most 64 rows (the per-row loss
-// inputs of narrow layers stay small): two CTAs per SM
-int head_rows_per_tile(int H, bool has_lo, int A) {
+// inputs of narrow layers stay small): two CTAs per SM. Shared memory is sized for these.
+static int head_default_rows(int H, bool has_lo, int A) {
   return std::max(1, std::min(64, (has_lo || A == 1 ? 4096 : 8192) / H));
 }
 
+// Rows per tile for a batch of M rows: the default, unless that leaves fewer tiles than
+// SMs (small batches), where a CTA would walk its tile's rows one pass after another while
+// most SMs idle; then about one tile per SM, never fewer than 8 rows for the actor (its
+// warps take rows r and r + 8 in one pass) or 2 for the critic, never more than the default.
+int head_rows_per_tile(int64_t M, int H, bool has_lo, int A) {
+  const int def = head_default_rows(H, has_lo, A);
+  const int64_t sms = sm_count();
+  if (ceil_div(std::max<int64_t>(M, 1), (int64_t)def) >= sms) return def;
+  const int64_t least = A == 1 ? 2 : 8;
+  return (int)std::min<int64_t>(def, std::max<int64_t>(least, ceil_div(M, sms)));
+}
+
 size_t head_smem_bytes(int H, int A, bool has_lo) {
-  const int R = head_rows_per_tile(H, has_lo, A);
+  const int R = head_default_rows(H, has_lo, A);
   const int AP = A == 1 ? 1 : (A + 3) & ~3;
   const size_t nb = head_buffers(has_lo, A);
   return sizeof(float) * ((size_t)H * AP + (nb + (has_lo ? 2 : 0)) * (size_t)R * H + (size_t)R * AP +
                           (size_t)kNW * (AP + kStats) + 3 * nb * (size_t)R * A);
 }
 
-int head_grid(int64_t M, int H) {
-  const int64_t tiles = ceil_div(M, head_rows_per_tile(H, true, 1));  // the smaller tiles: an upper bound
+int head_grid(const HeadParams& p) {
+  const int64_t tiles = ceil_div(p.M, (int64_t)head_rows_per_tile(p.M, p.H, p.act_lo != nullptr, p.A));
   const int64_t cap = 2LL * sm_count();
   return (int)std::max<int64_t>(1, std::min<int64_t>(tiles, cap));
 }
@@ -563,7 +575,7 @@ int head_launch(HeadParams p, int grid, cudaStream_t s) {
   SPO_CHECK_ARG(!p.cells || p.mask || p.A == 9, kErrUnsupported, "head: board cells need 9 actions");
   SPO_CHECK_ARG(p.mode == kHeadCritic ? p.target != nullptr : p.q != nullptr, kErrArg,
                 "head: missing loss inputs");
-  p.rows_per_tile = head_rows_per_tile(p.H, p.act_lo != nullptr, p.A);
+  p.rows_per_tile = head_rows_per_tile(p.M, p.H, p.act_lo != nullptr, p.A);
   const size_t smem = head_smem_bytes(p.H, p.A, p.act_lo != nullptr);
   if (p.M == 0) return kOk;
   return p.A == 9 ? launch_a<9>(p, grid, smem, s) : launch_a<1>(p, grid, smem, s);

@@ -22,6 +22,8 @@
 // float4 of each row is loaded straight from global memory, 8 rows in flight per thread.
 // Each CTA writes its partial [k x n] tile to part[chunk]; a deterministic reduction adds
 // the chunks (linear_backward's dW, networks/linear.mojo:120-167).
+#include <cmath>
+
 #include "spo_common.cuh"
 #include "kernels.cuh"
 
@@ -337,7 +339,11 @@ int fwd_skinny_launch(LayerInput in, const float* w, const float* b, int64_t row
   if (rows <= 0) return kOk;
   const int64_t col_blocks = ceil_div(n, kCols);
   const int64_t want = std::max<int64_t>(1, 3LL * sm_count() / col_blocks);
-  const int64_t chunk = std::max<int64_t>(kRows, ceil_div(ceil_div(rows, want), kRows) * kRows);
+  int64_t chunk = std::max<int64_t>(kRows, ceil_div(ceil_div(rows, want), kRows) * kRows);
+  // A CTA walks its rows one after another: when that leaves fewer CTAs than SMs (small
+  // batches), shorter chunks of 8-row multiples spread the rows over about one CTA per SM.
+  if (ceil_div(rows, chunk) < sm_count())
+    chunk = std::max<int64_t>(8, ceil_div(ceil_div(rows, (int64_t)sm_count()), 8) * 8);
   dim3 grid((unsigned)ceil_div(rows, chunk), (unsigned)col_blocks);
   fwd_skinny_kernel<<<grid, kFwdThreads, 0, s>>>(in.x, in.cells, w, b, rows, (int)k, n, chunk, y, y_lo, bits);
   SPO_LAUNCH_CHECK();
@@ -350,7 +356,16 @@ int64_t dw_skinny_chunk(int64_t rows, int64_t n) {
   // enough chunks for ~4 CTAs per SM, each at least a few row blocks long
   const int64_t col_blocks = ceil_div(n, kCols);
   const int64_t want = std::max<int64_t>(1, dw_skinny_max_parts() / col_blocks);
-  return std::max<int64_t>(4 * kRows, ceil_div(ceil_div(std::max<int64_t>(rows, 1), want), kRows) * kRows);
+  const int64_t r = std::max<int64_t>(rows, 1);
+  const int64_t chunk = std::max<int64_t>(4 * kRows, ceil_div(ceil_div(r, want), kRows) * kRows);
+  if (ceil_div(r, chunk) >= sm_count()) return chunk;
+  // Small batches (fewer chunks than SMs): a CTA walks its rows kUnroll at a time, each
+  // step waiting on memory, while the reduction that adds the partials gets deeper with
+  // their number; chunks of about sqrt(rows / 4) rows (kUnroll multiples) balance the two.
+  // Never more than `want` partials (the workspace holds dw_skinny_max_parts()).
+  int64_t c = (int64_t)std::ceil(std::sqrt((double)r / 4.0));
+  c = std::max<int64_t>(c, ceil_div(r, want));
+  return std::max<int64_t>(kUnroll, ceil_div(c, (int64_t)kUnroll) * kUnroll);
 }
 
 int dw_skinny_launch(LayerInput in, const float* dy, int64_t rows, int64_t k, int64_t n, float* part,

@@ -48,9 +48,9 @@ struct HeadParams {
   float* stats_part;       // optional [grid][kStats]
 };
 
-int head_rows_per_tile(int H, bool has_lo, int A);
+int head_rows_per_tile(int64_t M, int H, bool has_lo, int A);
 size_t head_smem_bytes(int H, int A, bool has_lo);
-int head_grid(int64_t M, int H);
+int head_grid(const HeadParams& p);  // CTAs of the launch = partial-sum slots written
 int head_launch(HeadParams p, int grid, cudaStream_t s);
 
 // ---------------------------------------------------------------- partial-sum reduction
