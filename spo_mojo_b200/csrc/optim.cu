@@ -16,43 +16,48 @@ namespace {
 constexpr int kThreads = 256;
 
 // ---------------------------------------------------------------- reduction
-// A block takes 32 consecutive elements of a segment at a time; its 8 warps split the
-// parts (warp g sums parts g, g + 8, ..., four chains), so that a segment with few
+// The work is the segments' 32-element chunks, numbered segment after segment; block b
+// takes chunks b, b + grid, ... (so a small step's few chunks spread over many blocks
+// instead of each block walking every segment). For a chunk, the block's 8 warps split
+// the parts (warp g sums parts g, g + 8, ..., four chains), so that a segment with few
 // elements and many parts still has enough loads in flight. The 8 group sums are then
-// added in group order: the result does not depend on scheduling.
+// added in group order: the result does not depend on scheduling or on the grid.
 constexpr int kRedCols = 32;
 constexpr int kRedGroups = kThreads / kRedCols;
+
+__host__ __device__ inline int64_t red_chunks(const ReduceSeg& sg) { return (sg.count + kRedCols - 1) / kRedCols; }
 
 __global__ void __launch_bounds__(kThreads) reduce_kernel(const ReduceParams P) {
   __shared__ float gsum[kRedGroups][kRedCols + 1];
   const int c = threadIdx.x % kRedCols, g = threadIdx.x / kRedCols;
-  for (int s = 0; s < P.nseg; ++s) {
+  int s = 0;
+  int64_t base = 0;  // number of the first chunk of segment s
+  for (int64_t gch = blockIdx.x;; gch += gridDim.x) {
+    while (s < P.nseg && gch >= base + red_chunks(P.seg[s])) base += red_chunks(P.seg[s++]);
+    if (s >= P.nseg) break;  // block-uniform
     const ReduceSeg sg = P.seg[s];
-    const int64_t chunks = (sg.count + kRedCols - 1) / kRedCols;
-    for (int64_t ch = blockIdx.x; ch < chunks; ch += gridDim.x) {
-      const int64_t i = ch * kRedCols + c;
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      if (i < sg.count) {
-        const float* src = sg.src + i;
-        int k = g;
-        for (; k + 3 * kRedGroups < sg.parts; k += 4 * kRedGroups) {
-          a0 += __ldg(src + (int64_t)k * sg.part_stride);
-          a1 += __ldg(src + (int64_t)(k + kRedGroups) * sg.part_stride);
-          a2 += __ldg(src + (int64_t)(k + 2 * kRedGroups) * sg.part_stride);
-          a3 += __ldg(src + (int64_t)(k + 3 * kRedGroups) * sg.part_stride);
-        }
-        for (; k < sg.parts; k += kRedGroups) a0 += __ldg(src + (int64_t)k * sg.part_stride);
+    const int64_t i = (gch - base) * kRedCols + c;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (i < sg.count) {
+      const float* src = sg.src + i;
+      int k = g;
+      for (; k + 3 * kRedGroups < sg.parts; k += 4 * kRedGroups) {
+        a0 += __ldg(src + (int64_t)k * sg.part_stride);
+        a1 += __ldg(src + (int64_t)(k + kRedGroups) * sg.part_stride);
+        a2 += __ldg(src + (int64_t)(k + 2 * kRedGroups) * sg.part_stride);
+        a3 += __ldg(src + (int64_t)(k + 3 * kRedGroups) * sg.part_stride);
       }
-      gsum[g][c] = (a0 + a1) + (a2 + a3);
-      __syncthreads();
-      if (g == 0 && i < sg.count) {
-        float v = gsum[0][c];
-#pragma unroll
-        for (int q = 1; q < kRedGroups; ++q) v += gsum[q][c];
-        sg.dst[i] = v;
-      }
-      __syncthreads();
+      for (; k < sg.parts; k += kRedGroups) a0 += __ldg(src + (int64_t)k * sg.part_stride);
     }
+    gsum[g][c] = (a0 + a1) + (a2 + a3);
+    __syncthreads();
+    if (g == 0 && i < sg.count) {
+      float v = gsum[0][c];
+#pragma unroll
+      for (int q = 1; q < kRedGroups; ++q) v += gsum[q][c];
+      sg.dst[i] = v;
+    }
+    __syncthreads();
   }
 }
 
@@ -258,10 +263,10 @@ int grid_for(int64_t n, int per_thread = 1) {
 }  // namespace
 
 int reduce_launch(const ReduceParams& p, cudaStream_t s) {
-  int64_t total = 0;
-  for (int i = 0; i < p.nseg; ++i) total = std::max<int64_t>(total, p.seg[i].count);
+  int64_t total = 0;  // chunks over all segments
+  for (int i = 0; i < p.nseg; ++i) total += red_chunks(p.seg[i]);
   if (p.nseg == 0) return kOk;
-  const int grid = (int)std::min<int64_t>(ceil_div(total, kRedCols), 4LL * sm_count());
+  const int grid = (int)std::min<int64_t>(total, 4LL * sm_count());
   reduce_kernel<<<std::max(grid, 1), kThreads, 0, s>>>(p);
   SPO_LAUNCH_CHECK();
   return kOk;
