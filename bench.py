@@ -259,8 +259,12 @@ TRAFFIC_PER_LAUNCH = {
 }
 
 
-def count_launches(wl, clip, engine="tensor"):
-    """libspo_cuda kernel launches of one learner step."""
+TC0_MIN_ROWS = 16384  # the library runs the input layer on tensor cores from this many rows
+
+
+def count_launches(wl, clip, engine="tensor", rows=None):
+    """libspo_cuda kernel launches of one learner step on `rows` rows (per rank)."""
+    rows = wl.batch if rows is None else rows
     n = 0
     for net in (wl.actor, wl.critic):
         if net is None:
@@ -270,7 +274,7 @@ def count_launches(wl, clip, engine="tensor"):
         hidden = net.dims[1:-1]
         if engine == "tensor" and L >= 3 and all(h % 128 == 0 and h <= 1024 for h in hidden):
             n += L - 2                           # per-step TF32 split of the hidden weights
-            if net.dims[0] <= 32 and net.dims[1] % 128 == 0:
+            if net.dims[0] <= 32 and net.dims[1] % 128 == 0 and rows >= TC0_MIN_ROWS:
                 n += 2                           # first layer on tensor cores: pad/split x and W0
     return n + 1 + 1 + (1 if clip else 0)      # reduce, adam, sum of squares
 
@@ -482,7 +486,7 @@ def run_ours(args):
                              ("working set per step > L2 (inputs %.0f MB, activations %.1f GB); no flush"
                               % (in_bytes / 1e6, act_bytes / 1e9))},
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
-            "gpu_launches": count_launches(wl, clip, args.engine) * args.steps,
+            "gpu_launches": count_launches(wl, clip, args.engine, rows) * args.steps,
             "engine": args.engine,
             "stats": stats,
         }

@@ -442,6 +442,8 @@ int gemm_fwd_split(cudaStream_t s, float* y_hi, float* y_lo, const float* x, con
   return gemm_simt_launch(c.tile, OP_ROW, OP_ROW, EPI_BIAS_RELU_SPLIT, p, c.grid, s);
 }
 
+constexpr int64_t kTc0MinRows = 16384;
+
 // Forward of layers 0..L-2 (ReLU) into the activation cache. In tensor-core mode the
 // hidden weights are first split into TF32 hi/lo pairs (W^T for the forward, W for dX).
 int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, LayerInput in,
@@ -468,7 +470,10 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
     if (rc) return rc;
   }
   int rc;
-  if (n.tc0) {
+  // The input layer on tensor cores costs three launches (W_0^T and input splits, GEMM) of
+  // mostly fixed latency; below kTc0MinRows rows the one-launch CUDA-core kernel, which
+  // writes the same hi/lo pair and packed mask, is faster (c0's 256 rows: ~16 us -> ~4 us).
+  if (n.tc0 && rows >= kTc0MinRows) {
     rc = split_weights_t_pad_launch(params + n.w_off[0], d.dims[0], d.dims[1], n.w0t[0], n.w0t[1], s);
     if (rc) return rc;
     rc = pad_split_input_launch(in, d.dims[0], rows, n.x0[0], n.x0[1], s);

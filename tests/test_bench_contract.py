@@ -1,0 +1,28 @@
+"""bench.py's launch count (its gpu_launches claim) against the kernels one learner step
+launches, as the ncu launch lists of c0 (256 rows: 9 kernels) and c3 (1,048,576 rows: 28
+kernels) show them."""
+
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+from spo_mojo_b200.workloads import WORKLOADS  # noqa: E402
+
+
+def test_launch_count_matches_launch_lists():
+    # c0: W1 split, input-layer forward (CUDA cores below 16,384 rows), hidden forward,
+    # head, hidden dW, dX into the input layer, input-layer dW, reduction, Adam
+    assert bench.count_launches(WORKLOADS["c0"], clip=False) == 9
+    # c3, actor and critic: per network W1/W2 splits, W0^T and input splits, three forward
+    # GEMMs, head, two hidden dW, two dX, input-layer dW; then reduction and Adam
+    assert bench.count_launches(WORKLOADS["c3"], clip=False) == 28
+    # the same network below the input layer's tensor-core threshold: two launches fewer each
+    assert bench.count_launches(WORKLOADS["c3"], clip=False, rows=bench.TC0_MIN_ROWS - 1) == 24
+    # the CUDA-core engine has no splits
+    assert bench.count_launches(WORKLOADS["c0"], clip=False, engine="cuda") == 8
+    # a clipped step adds the grouped sum of squares
+    assert bench.count_launches(WORKLOADS["c0"], clip=True) == 10
