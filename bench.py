@@ -18,11 +18,18 @@ Timed quantities (one JSON line on rank 0):
               measured peak
   cpu_baseline the CPU restatement (float32 numpy) on a bounded sample, rank 0, N = 1
 
+L2: a workload whose inputs and activations exceed the 126 MB L2 (c2, c3, c4) is timed
+over K back-to-back steps; one that fits (c0, c1) is timed one step at a time, with a
+write of twice the L2 size between steps outside the timed events, and `value` is the
+mean of those step times. --graph (one GPU) replays each step as one CUDA graph, which
+the small, launch-latency-bound workloads want.
+
 --impl reference times the reference's computation on the host CPU (the reference
 is Mojo GPU code with no CPU path and no runnable toolchain here, so its algorithm is
 run as the float32 numpy restatement), with all host threads.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3] [--graph]
+                  [--impl ours|reference]
 """
 
 import argparse
