@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -38,6 +39,14 @@ int set_error(int code, const std::string& msg) {
 }
 
 void clear_error() { g_last_error.clear(); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SPO_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 int sm_count() {
   static int cached[64] = {0};

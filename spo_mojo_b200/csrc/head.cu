@@ -89,6 +89,8 @@ __global__ void __launch_bounds__(kHeadThreads, 2)
 head_kernel(const HeadParams p) {
   constexpr int AP = padded_actions<A>();
   extern __shared__ __align__(16) float sm[];
+  pdl_wait();
+  pdl_trigger();
   const int H = p.H;
   const int R = p.rows_per_tile;
   const bool has_lo = p.act_lo != nullptr;
@@ -523,8 +525,7 @@ int launch_a(const HeadParams& p, int grid, size_t smem, cudaStream_t s) {
       opted.insert({dev, (const void*)k});
     }
   }
-  k<<<grid, kHeadThreads, smem, s>>>(p);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(k, dim3(grid), dim3(kHeadThreads), smem, s, 0u, p));
   return kOk;
 }
 

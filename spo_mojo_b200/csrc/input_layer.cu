@@ -103,6 +103,8 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
                  int64_t rows, int k, int64_t n, int64_t chunk, float* __restrict__ part) {
   __shared__ __align__(16) float xs2[2][kRows][kMaxK];
   __shared__ __align__(16) float cs2[2][kRows][kCells];
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x;
   const int half = tid / 128;
   const int64_t col = (int64_t)blockIdx.y * kCols + 4 * (tid % 128);
@@ -192,6 +194,8 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, 
                   float* __restrict__ y_lo, uint32_t* __restrict__ bits) {
   __shared__ __align__(16) float xs2[2][kRows][kMaxK];
   __shared__ __align__(16) float cs2[2][kRows][kCells];
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t col = (int64_t)blockIdx.y * kCols + 4 * tid;
   const bool col_ok = col < n;
@@ -270,6 +274,8 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, 
 // hi/lo pairs (zeros past k), and W^T [n x kPadK] likewise. One thread per element.
 __global__ void pad_split_input_kernel(const float* __restrict__ x, const float* __restrict__ cells, int k,
                                        int64_t rows, float* __restrict__ hi, float* __restrict__ lo) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t gs = (int64_t)gridDim.x * blockDim.x;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < rows * kPadK; e += gs) {
     const int64_t r = e / kPadK;
@@ -293,6 +299,8 @@ __global__ void pad_split_input_kernel(const float* __restrict__ x, const float*
 
 __global__ void split_weights_t_pad_kernel(const float* __restrict__ w, int k, int64_t n, float* __restrict__ wt_hi,
                                            float* __restrict__ wt_lo) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t gs = (int64_t)gridDim.x * blockDim.x;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n * kPadK; e += gs) {
     const int64_t col = e / kPadK;
@@ -316,16 +324,15 @@ int pad_split_input_launch(LayerInput in, int64_t k, int64_t rows, float* hi, fl
   SPO_CHECK_ARG(!in.cells || k == 3 * kCells, kErrShape, "pad_split_input: board cells need a 27-wide input");
   if (rows <= 0) return kOk;
   const int grid = (int)std::min<int64_t>(ceil_div(rows * kPadK, 256), 8LL * sm_count());
-  pad_split_input_kernel<<<grid, 256, 0, s>>>(in.x, in.cells, (int)k, rows, hi, lo);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(pad_split_input_kernel, dim3(grid), dim3(256), 0, s, 0u, in.x, in.cells, (int)k, rows, hi,
+                          lo));
   return kOk;
 }
 
 int split_weights_t_pad_launch(const float* w, int64_t k, int64_t n, float* wt_hi, float* wt_lo, cudaStream_t s) {
   SPO_CHECK_ARG(k >= 1 && k <= kPadK && n >= 1, kErrUnsupported, "split_weights_t_pad: bad shape");
   const int grid = (int)std::min<int64_t>(ceil_div(n * kPadK, 256), 8LL * sm_count());
-  split_weights_t_pad_kernel<<<grid, 256, 0, s>>>(w, (int)k, n, wt_hi, wt_lo);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(split_weights_t_pad_kernel, dim3(grid), dim3(256), 0, s, 0u, w, (int)k, n, wt_hi, wt_lo));
   return kOk;
 }
 
@@ -345,8 +352,8 @@ int fwd_skinny_launch(LayerInput in, const float* w, const float* b, int64_t row
   if (ceil_div(rows, chunk) < sm_count())
     chunk = std::max<int64_t>(8, ceil_div(ceil_div(rows, (int64_t)sm_count()), 8) * 8);
   dim3 grid((unsigned)ceil_div(rows, chunk), (unsigned)col_blocks);
-  fwd_skinny_kernel<<<grid, kFwdThreads, 0, s>>>(in.x, in.cells, w, b, rows, (int)k, n, chunk, y, y_lo, bits);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(fwd_skinny_kernel, grid, dim3(kFwdThreads), 0, s, 0u, in.x, in.cells, w, b, rows, (int)k, n,
+                          chunk, y, y_lo, bits));
   return kOk;
 }
 
@@ -378,11 +385,8 @@ int dw_skinny_launch(LayerInput in, const float* dy, int64_t rows, int64_t k, in
   if (parts) *parts = (int)p;
   if (p == 0) return kOk;
   dim3 grid((unsigned)p, (unsigned)ceil_div(n, kCols));
-  if (k <= 28)
-    dw_skinny_kernel<14><<<grid, kThreads, 0, s>>>(in.x, in.cells, dy, rows, (int)k, n, chunk, part);
-  else
-    dw_skinny_kernel<16><<<grid, kThreads, 0, s>>>(in.x, in.cells, dy, rows, (int)k, n, chunk, part);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(k <= 28 ? dw_skinny_kernel<14> : dw_skinny_kernel<16>, grid, dim3(kThreads), 0, s, 0u, in.x,
+                          in.cells, dy, rows, (int)k, n, chunk, part));
   return kOk;
 }
 

@@ -29,6 +29,8 @@ __host__ __device__ inline int64_t red_chunks(const ReduceSeg& sg) { return (sg.
 
 __global__ void __launch_bounds__(kThreads) reduce_kernel(const ReduceParams P) {
   __shared__ float gsum[kRedGroups][kRedCols + 1];
+  pdl_wait();
+  pdl_trigger();
   const int c = threadIdx.x % kRedCols, g = threadIdx.x / kRedCols;
   int s = 0;
   int64_t base = 0;  // number of the first chunk of segment s
@@ -85,6 +87,8 @@ struct SumsqGroups {
 
 __global__ void __launch_bounds__(kThreads) sumsq_groups_kernel(const SumsqGroups P) {
   __shared__ float sh[32];
+  pdl_wait();
+  pdl_trigger();
   for (int gi = 0; gi < P.ngrp; ++gi) {
     float acc = 0.f;
     const int64_t b4 = P.begin[gi] / 4, e4 = P.end[gi] / 4;
@@ -134,6 +138,8 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const AdamParams P, int6
   __shared__ float s_clip[kMaxGroups];
   __shared__ float s_norm[kMaxGroups];
   __shared__ int s_t;
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x == 0) s_t = P.step ? (*P.step + 1) : P.host_step;
   if (threadIdx.x < kMaxGroups) {
     float clip = 1.f, norm = 0.f;
@@ -267,8 +273,7 @@ int reduce_launch(const ReduceParams& p, cudaStream_t s) {
   for (int i = 0; i < p.nseg; ++i) total += red_chunks(p.seg[i]);
   if (p.nseg == 0) return kOk;
   const int grid = (int)std::min<int64_t>(total, 4LL * sm_count());
-  reduce_kernel<<<std::max(grid, 1), kThreads, 0, s>>>(p);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(reduce_kernel, dim3(std::max(grid, 1)), dim3(kThreads), 0, s, 0u, p));
   return kOk;
 }
 
@@ -282,16 +287,14 @@ int sumsq_groups_launch(const float* g, const AdamGroup* grp, int ngrp, float* p
     P.begin[i] = grp[i].begin;
     P.end[i] = grp[i].end;
   }
-  sumsq_groups_kernel<<<kSumsqParts, kThreads, 0, s>>>(P);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(sumsq_groups_kernel, dim3(kSumsqParts), dim3(kThreads), 0, s, 0u, P));
   return kOk;
 }
 
 int adam_launch(const AdamParams& p, int64_t n, cudaStream_t s) {
   SPO_CHECK_ARG(aligned16(p.p) && aligned16(p.g) && aligned16(p.m) && aligned16(p.v), kErrAlign,
                 "adam: buffers must be 16-byte aligned");
-  adam_kernel<<<grid_for(n / 4 + 1), kThreads, 0, s>>>(p, n);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(adam_kernel, dim3(grid_for(n / 4 + 1)), dim3(kThreads), 0, s, 0u, p, n));
   return kOk;
 }
 

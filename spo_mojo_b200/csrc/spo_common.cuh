@@ -61,6 +61,48 @@ inline int64_t align_up_i64(int64_t n, int64_t a) { return (n + a - 1) / a * a; 
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Programmatic dependent launch. The learner's kernels are launched with programmatic
+// stream serialisation (launch_pdl), so a kernel may begin while the kernel before it in
+// the stream still runs: its launch and its on-chip set-up (shared-memory barriers, TMEM,
+// registers) overlap the previous kernel's last wave. Every kernel launched this way calls
+// pdl_wait() before its first access to global memory (the instruction returns once the
+// previous grid has completed and its writes are visible), then pdl_trigger(), which lets
+// the next kernel in the stream begin launching. For a kernel launched without the
+// attribute, both return at once. SPO_PDL=0 in the environment turns the attribute off.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+
+// Launch `kernel` on s with programmatic stream serialisation (when pdl_enabled()), plus an
+// optional cluster of cluster_x CTAs (0 = none).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       unsigned cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  unsigned na = 0;
+  if (cluster_x > 0) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -408,6 +408,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
+  // everything above is on-chip; global memory (operands, bias, masks, outputs) only below
+  pdl_wait();
+  pdl_trigger();
 
   const int64_t per_split = (int64_t)P.m_tiles * P.n_tiles;
 
@@ -849,6 +852,8 @@ __global__ void split_weights_kernel(const float* __restrict__ w, int64_t K, int
                                      float* __restrict__ w_hi, float* __restrict__ w_lo) {
   __shared__ float hs[32][33];
   __shared__ float ls[32][33];
+  pdl_wait();
+  pdl_trigger();
   const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
   for (int i = threadIdx.y; i < 32; i += 8) {
     const int64_t k = k0 + i, n = n0 + threadIdx.x;
@@ -1125,24 +1130,8 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   const int threads = threads_of(pair, bn);
   const Kern kern = pick(a.kind, pair, P.mask_bits != nullptr, a.c_lo != nullptr, bn);
   if ((rc = opt_in(kern, pair, bn))) return rc;
-  if (pair) {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(threads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    SPO_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_ah, m_al, m_bh, m_bl, P));
-  } else {
-    kern<<<grid, threads, smem, s>>>(m_ah, m_al, m_bh, m_bl, P);
-  }
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(kern, dim3((unsigned)grid), dim3(threads), smem, s, pair ? 2u : 0u, m_ah, m_al, m_bh,
+                          m_bl, P));
   return kOk;
 }
 
@@ -1166,9 +1155,8 @@ int combine_tf32_launch(float* hi, const float* lo, int64_t n, cudaStream_t s) {
 int split_weights_launch(const float* w, int64_t K, int64_t N, float* wt_hi, float* wt_lo,
                          float* w_hi, float* w_lo, cudaStream_t s) {
   if (K <= 0 || N <= 0) return kOk;
-  split_weights_kernel<<<dim3((unsigned)ceil_div(N, 32), (unsigned)ceil_div(K, 32)), dim3(32, 8), 0,
-                         s>>>(w, K, N, wt_hi, wt_lo, w_hi, w_lo);
-  SPO_LAUNCH_CHECK();
+  SPO_CUDA_TRY(launch_pdl(split_weights_kernel, dim3((unsigned)ceil_div(N, 32), (unsigned)ceil_div(K, 32)),
+                          dim3(32, 8), 0, s, 0u, w, K, N, wt_hi, wt_lo, w_hi, w_lo));
   return kOk;
 }
 
