@@ -261,6 +261,7 @@ struct NetPlan {
   float* head_dbx = nullptr;         // [Gh][d_{L-1}]
   float* head_stats = nullptr;       // [Gh][kStats]
   float* dw_part[SPO_MAX_LAYERS] = {};
+  int64_t dw_part_cap[SPO_MAX_LAYERS] = {};  // partials dw_part[l] holds
   float* db_part[SPO_MAX_LAYERS] = {};  // column sums of dZ_{l} from layer l+1's dX GEMM
 };
 
@@ -292,14 +293,22 @@ bool net_uses_tc(const spo_mlp_desc& d, int engine) {
 }
 
 // Upper bound of the row splits of a tensor-core dW launch for `rows` rows.
+// At least kDwMinKBlocks k-blocks (32 rows each) per unit of a split dW product. Large
+// batches split far less than this allows (the rule below stops at the first S that fills
+// the slots); it binds for batches of a few thousand to ~100 k rows, where a longer minimum
+// left most CTA pairs idle while a few walked their rows serially (4,096 rows: 2 splits of
+// 64 k-blocks, 46 us; with 8, 16 splits).
+constexpr int64_t kDwMinKBlocks = 8;
+
 int64_t tc_dw_splits_max(int64_t rows) {
-  return std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 32) / 64, 4LL * sm_count()));
+  return std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 32) / kDwMinKBlocks, 4LL * sm_count()));
 }
 
 // Row splits S of a tensor-core dW product whose unit grid has `tiles` output tiles per
-// split and `slots` units running at once: at least 64 k-blocks (2048 rows) per unit, and
+// split and `slots` units running at once: at least kDwMinKBlocks k-blocks per unit, and
 // the smallest S whose tiles*S units fill the slots in whole waves (>= 95% of the last
-// wave busy), else the best such fill.
+// wave busy), else the best such fill. S <= min(tc_dw_splits_max(rows), slots): S = slots
+// always fills whole waves.
 int64_t tc_dw_splits(int64_t tiles, int64_t slots, int64_t rows) {
   const int64_t smax = tc_dw_splits_max(rows);
   int64_t best = 1;
@@ -349,9 +358,11 @@ void carve_net(NetPlan& n, Carve& c, int64_t rows) {
   n.head_dbx = c.take<float>((size_t)(gh * hl));
   n.head_stats = c.take<float>((size_t)(gh * kStats));
   for (int l = 0; l + 1 < L; ++l) {
-    const int64_t parts = (n.tc && l >= 1) ? tc_dw_splits_max(rows)
+    const int64_t parts = (n.tc && l >= 1) ? std::min<int64_t>(tc_dw_splits_max(rows),
+                                                               tc_gemm_slots(TC_DW, d.dims[l + 1]))
                                            : dw_parts_bound(d.dims[l], d.dims[l + 1]);
     n.dw_part[l] = c.take<float>((size_t)(parts * d.dims[l] * d.dims[l + 1]));
+    n.dw_part_cap[l] = parts;
   }
   for (int l = 0; l + 2 < L; ++l) {  // db of layer l comes from layer l+1's dX GEMM
     const int64_t parts = std::max<int64_t>(fwd_parts_bound(d.dims[l + 1]), n.tc ? sm_count() : 0);
@@ -556,7 +567,8 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, Layer
       w.M = kin;
       w.N = nout;
       w.K = rows;
-      const int64_t S = tc_dw_splits(tc_gemm_tiles(TC_DW, kin, nout), tc_gemm_slots(TC_DW, nout), rows);
+      const int64_t S = std::min(tc_dw_splits(tc_gemm_tiles(TC_DW, kin, nout), tc_gemm_slots(TC_DW, nout), rows),
+                                 n.dw_part_cap[l]);
       w.k_chunk = align_up(ceil_div(ceil_div(rows, 32), S), 1) * 32;
       w.c_part = n.dw_part[l];
       w.err = err;

@@ -348,9 +348,10 @@ int fwd_skinny_launch(LayerInput in, const float* w, const float* b, int64_t row
   const int64_t want = std::max<int64_t>(1, 3LL * sm_count() / col_blocks);
   int64_t chunk = std::max<int64_t>(kRows, ceil_div(ceil_div(rows, want), kRows) * kRows);
   // A CTA walks its rows one after another: when that leaves fewer CTAs than SMs (small
-  // batches), shorter chunks of 8-row multiples spread the rows over about one CTA per SM.
+  // batches), shorter chunks of 8-row multiples spread the rows over about three CTAs per
+  // SM (the kernel's residency).
   if (ceil_div(rows, chunk) < sm_count())
-    chunk = std::max<int64_t>(8, ceil_div(ceil_div(rows, (int64_t)sm_count()), 8) * 8);
+    chunk = std::max<int64_t>(8, ceil_div(ceil_div(rows, want), (int64_t)8) * 8);
   dim3 grid((unsigned)ceil_div(rows, chunk), (unsigned)col_blocks);
   SPO_CUDA_TRY(launch_pdl(fwd_skinny_kernel, grid, dim3(kFwdThreads), 0, s, 0u, in.x, in.cells, w, b, rows, (int)k, n,
                           chunk, y, y_lo, bits));
