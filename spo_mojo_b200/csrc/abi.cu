@@ -492,7 +492,8 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
   int rc;
   // The input layer on tensor cores costs three launches (W_0^T and input splits, GEMM) of
   // mostly fixed latency; below kTc0MinRows rows the one-launch CUDA-core kernel, which
-  // writes the same hi/lo pair and packed mask, is faster (c0's 256 rows: ~16 us -> ~4 us).
+  // writes the same hi/lo pair and packed mask, is faster (256 rows, 27 -> 128: ~16 us of
+  // launches -> ~6 us).
   if (n.tc0 && rows >= kTc0MinRows) {
     rc = split_weights_t_pad_launch(params + n.w_off[0], d.dims[0], d.dims[1], n.w0t[0], n.w0t[1], s);
     if (rc) return rc;

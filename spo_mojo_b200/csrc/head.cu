@@ -52,8 +52,8 @@ __host__ __device__ constexpr int padded_actions() { return A == 1 ? 1 : (A + 3)
 
 // Tile buffers: the copies run NB - 1 tiles ahead. With lo halves 2 (the lo buffers take
 // the room); fp32 input: the critic (one output) 4 tiles of 4096 activations, the actor 2
-// of 8192 (two rows per warp in its logits phase; measured 2.11 vs 2.78 ms at c3's H = 512
-// against 4 x 4096, while the critic measured 1.05 vs 1.13 ms the other way round).
+// of 8192 (two rows per warp in its logits phase; measured 2.11 vs 2.78 ms for
+// 1,048,576 rows at H = 512 against 4 x 4096, while the critic measured 1.05 vs 1.13 ms the other way round).
 __host__ __device__ constexpr int head_buffers(bool has_lo, int A) { return has_lo ? 2 : (A == 1 ? 4 : 2); }
 
 __device__ __forceinline__ float softplus_f(float x) {
