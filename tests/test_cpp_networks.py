@@ -60,3 +60,22 @@ def test_layout_matches_the_python_mirror(output):
         pairs = [(int(nums[i]), int(nums[i + 1])) for i in range(0, len(nums) - 2, 2)]
         offs, want_total = NetSpec(dims).offsets()
         assert pairs == [tuple(o) for o in offs] and total == want_total, (dims, pairs, offs)
+
+
+def test_golden_program_builds(tmp_path):
+    """tests/cpp/networks_golden.cpp (the reference's actor-backward goldens through the C++
+    mirror; it needs a GPU to run) compiles warning-free and links."""
+    cxx = shutil.which("g++")
+    if cxx is None:
+        pytest.skip("no C++ compiler")
+    out = str(tmp_path / "networks_golden")
+    libdir = os.path.dirname(ffi.LIB_PATH)
+    cmd = [cxx, "-std=c++17", "-O1", "-Wall", "-Wextra", "-Werror",
+           "-I", os.path.join(ROOT, "include"), "-I", os.path.join(CUDA, "include"),
+           os.path.join(ROOT, "tests", "cpp", "networks_golden.cpp"), "-o", out,
+           "-L", libdir, "-lspo_cuda", "-Wl,-rpath," + libdir,
+           "-L", os.path.join(CUDA, "lib64"), "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    usage = subprocess.run([out], capture_output=True, text=True, timeout=60)
+    assert usage.returncode == 1 and "usage" in usage.stderr
