@@ -26,3 +26,24 @@ def test_launch_count_matches_launch_lists():
     assert bench.count_launches(WORKLOADS["c0"], clip=False, engine="cuda") == 8
     # a clipped step adds the grouped sum of squares
     assert bench.count_launches(WORKLOADS["c0"], clip=True) == 10
+
+
+def test_reference_arm_prints_the_contract_line():
+    """bench.py --impl reference (the reference's algorithm on the host cores; no GPU)
+    prints one JSON line with the keys the driver reads, on the ours arm's metric."""
+    import json
+    import subprocess
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload", "c0",
+                        "--steps", "2", "--warmup", "1"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["steps"] == 2 and d["warmup"] == 1
+    assert d["metric"] == "learner samples/sec (fwd+bwd+loss+Adam)" and d["unit"] == "samples/s"
+    assert d["higher_is_better"] is True and d["value"] > 0
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": "samples/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
