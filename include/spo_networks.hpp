@@ -614,6 +614,119 @@ inline void truncated_gae(DeviceContext& ctx, Buffer& adv, Buffer& targets, cons
                           batch, t_len, lambda));
 }
 
+// ------------------------------------------------------------------ search heads (envs/)
+
+// The weight-sync shape test of the search models (envs/tictactoe_actor.mojo:108-140,
+// envs/tictactoe_critic.mojo:145-155): a network is copied only into one of the same
+// shape; here every width must match (the reference compares input, hidden and output).
+inline void check_sync_shape(const std::vector<int>& src, const std::vector<int>& want, const char* what) {
+  if (src != want) {
+    std::string dims;
+    for (size_t i = 0; i < src.size(); ++i) dims += (i ? "x" : "") + std::to_string(src[i]);
+    throw Error(SPO_ERR_SHAPE, std::string("the ") + what + " does not have the model's shape: " + dims);
+  }
+}
+
+inline void copy_params(DeviceContext& ctx, MLPParams& dst, const MLPParams& src) {
+  check_cuda(cudaMemcpyAsync(dst.flat().unsafe_ptr(), src.flat().unsafe_ptr(), sizeof(float) * dst.size(),
+                             cudaMemcpyDeviceToDevice, ctx.stream()),
+             "cudaMemcpyAsync");
+}
+
+// The network part of the search's actor model (envs/tictactoe_actor.mojo:64-191): frozen
+// copies of the trained actor and critic, refreshed from the learner with sync_from /
+// sync_critic_from, and their batched forward over m boards (m = envs x particles in the
+// search). The environment's dynamics and the bootstrap around them are not part of this
+// library.
+class TicTacToeActorHead {
+ public:
+  TicTacToeActorHead(DeviceContext& ctx, int64_t max_batch, int hidden, int depth = 2)
+      : params(zero_actor_params(ctx, hidden, OBS_DIM, depth)),
+        cache(ctx, max_batch, params.dims()),
+        obs(zero_buffer(ctx, static_cast<size_t>(max_batch * OBS_DIM))),
+        mask(zero_buffer(ctx, static_cast<size_t>(max_batch * NUM_ACTIONS))),
+        critic(zero_critic_params(ctx, OBS_DIM, hidden, 1, depth)),
+        ccache(ctx, max_batch, critic.dims()),
+        hidden(hidden),
+        max_batch(max_batch) {}
+
+  // the trained actor's weights into the model's (:121-140)
+  void sync_from(DeviceContext& ctx, const MLPParams& src) {
+    check_sync_shape(src.dims(), params.dims(), "actor being copied");
+    copy_params(ctx, params, src);
+  }
+  // the trained critic's weights into the model's (:108-119)
+  void sync_critic_from(DeviceContext& ctx, const MLPParams& src) {
+    check_sync_shape(src.dims(), critic.dims(), "critic");
+    copy_params(ctx, critic, src);
+  }
+  // Masked logits over m boards into out_logits; the mask and the observation come from
+  // the boards (state [m x 9], +1 agent / -1 rival / 0 empty) (:148-171).
+  void _prior(DeviceContext& ctx, const Buffer& state, Buffer& out_logits, int64_t m) {
+    check_batch(max_batch, m, "model", "boards");
+    require(state, m * NUM_ACTIONS, "_prior: state");
+    require(out_logits, m * NUM_ACTIONS, "_prior: out_logits");
+    check(spo_encode_obs(ctx.handle(), obs.unsafe_ptr(), mask.unsafe_ptr(), state.unsafe_ptr(), m));
+    actor_logits(ctx, params, cache, obs, mask, m);
+    check_cuda(cudaMemcpyAsync(out_logits.unsafe_ptr(), cache.value.unsafe_ptr(), sizeof(float) * m * NUM_ACTIONS,
+                               cudaMemcpyDeviceToDevice, ctx.stream()),
+               "cudaMemcpyAsync");
+  }
+  // The prior, then V from the critic on the observation _prior encoded (eval_root,
+  // :173-191).
+  void eval_root(DeviceContext& ctx, const Buffer& state, Buffer& logits_out, Buffer& value_out, int64_t m) {
+    require(value_out, m, "eval_root: value_out");
+    _prior(ctx, state, logits_out, m);
+    critic_forward(ctx, critic, ccache, obs, m);
+    check_cuda(cudaMemcpyAsync(value_out.unsafe_ptr(), ccache.value.unsafe_ptr(), sizeof(float) * m,
+                               cudaMemcpyDeviceToDevice, ctx.stream()),
+               "cudaMemcpyAsync");
+  }
+
+  ActorParams params;
+  ActorCache cache;
+  Buffer obs;   // [max_batch x 27] encoding of the last boards
+  Buffer mask;  // [max_batch x 9] their legal cells
+  CriticParams critic;
+  CriticCache ccache;
+  int hidden;
+  int64_t max_batch;
+};
+
+// The network part of the search's critic model (envs/tictactoe_critic.mojo:98-192).
+class TicTacToeCriticHead {
+ public:
+  TicTacToeCriticHead(DeviceContext& ctx, int64_t max_batch, int hidden, int depth = 2)
+      : params(zero_critic_params(ctx, OBS_DIM, hidden, 1, depth)),
+        cache(ctx, max_batch, params.dims()),
+        obs(zero_buffer(ctx, static_cast<size_t>(max_batch * OBS_DIM))),
+        hidden(hidden),
+        max_batch(max_batch) {}
+
+  // :145-162
+  void sync_from(DeviceContext& ctx, const MLPParams& src) {
+    check_sync_shape(src.dims(), params.dims(), "critic being copied");
+    copy_params(ctx, params, src);
+  }
+  // V over m boards (the network half of eval_root, :170-192)
+  void value(DeviceContext& ctx, const Buffer& state, Buffer& value_out, int64_t m) {
+    check_batch(max_batch, m, "model", "boards");
+    require(state, m * NUM_ACTIONS, "value: state");
+    require(value_out, m, "value: value_out");
+    check(spo_encode_obs(ctx.handle(), obs.unsafe_ptr(), nullptr, state.unsafe_ptr(), m));
+    critic_forward(ctx, params, cache, obs, m);
+    check_cuda(cudaMemcpyAsync(value_out.unsafe_ptr(), cache.value.unsafe_ptr(), sizeof(float) * m,
+                               cudaMemcpyDeviceToDevice, ctx.stream()),
+               "cudaMemcpyAsync");
+  }
+
+  CriticParams params;
+  CriticCache cache;
+  Buffer obs;
+  int hidden;
+  int64_t max_batch;
+};
+
 }  // namespace networks
 }  // namespace spo
 

@@ -344,3 +344,92 @@ def truncated_gae(ctx, adv, targets, reward, discount, v_tm1, v_t, truncation, b
     """rl_utils/multistep.mojo:72-82."""
     ffi.call("spo_truncated_gae", ctx.handle, _p(adv), _p(targets), _p(reward), _p(discount),
              _p(v_tm1), _p(v_t), _p(truncation), batch, t_len, lambda_)
+
+
+# ---------------------------------------------------------------- search heads (envs/)
+
+def check_sync_shape(src_dims, want_dims, what):
+    """The weight-sync shape test of the search models (envs/tictactoe_actor.mojo:108-140,
+    envs/tictactoe_critic.mojo:145-155): a network is copied only into one of the same
+    shape; here every width must match (the reference compares input, hidden and output)."""
+    src_dims, want_dims = tuple(int(d) for d in src_dims), tuple(int(d) for d in want_dims)
+    if src_dims != want_dims:
+        raise ValueError(f"the {what} does not have the model's shape: " + "x".join(map(str, src_dims)))
+
+
+class TicTacToeActorHead:
+    """The network part of the search's actor model (envs/tictactoe_actor.mojo:64-191):
+    frozen copies of the trained actor and critic, refreshed from the learner with
+    sync_from / sync_critic_from, and their batched forward over m boards (m = envs x
+    particles in the search). The environment's dynamics and the bootstrap around them
+    are not part of this library."""
+
+    def __init__(self, ctx, max_batch, hidden, depth=2):
+        self.params = zero_actor_params(ctx, hidden, OBS_DIM, depth)
+        self.cache = ActorCache(ctx, max_batch, self.params.dims)
+        self.obs = zero_buffer(ctx, max_batch * OBS_DIM)
+        self.mask = zero_buffer(ctx, max_batch * NUM_ACTIONS)
+        self.critic = zero_critic_params(ctx, OBS_DIM, hidden, 1, depth)
+        self.ccache = CriticCache(ctx, max_batch, self.critic.dims)
+        self.hidden = hidden
+        self.max_batch = max_batch
+
+    def sync_from(self, ctx, src):
+        """The trained actor's weights into the model's (:121-140)."""
+        check_sync_shape(src.dims, self.params.dims, "actor being copied")
+        with torch.cuda.stream(ctx.stream):
+            self.params.flat.copy_(src.flat)
+
+    def sync_critic_from(self, ctx, src):
+        """The trained critic's weights into the model's (:108-119)."""
+        check_sync_shape(src.dims, self.critic.dims, "critic")
+        with torch.cuda.stream(ctx.stream):
+            self.critic.flat.copy_(src.flat)
+
+    def _check(self, m):
+        if m > self.max_batch:
+            raise ValueError(f"the model was reserved for {self.max_batch} boards and is being "
+                             f"asked for {m}")
+
+    def _prior(self, ctx, state, out_logits, m):
+        """Masked logits over m boards into out_logits; mask and observation come from the
+        boards (state [m x 9], +1 agent / -1 rival / 0 empty) (:148-171)."""
+        self._check(m)
+        ffi.call("spo_encode_obs", ctx.handle, _p(self.obs), _p(self.mask), _p(state), m)
+        actor_logits(ctx, self.params, self.cache, self.obs, self.mask, m)
+        with torch.cuda.stream(ctx.stream):
+            out_logits.view(-1)[:m * NUM_ACTIONS].copy_(self.cache.value[:m * NUM_ACTIONS])
+
+    def eval_root(self, ctx, state, logits_out, value_out, m):
+        """The prior, then V from the critic on the observation _prior encoded (:173-191)."""
+        self._prior(ctx, state, logits_out, m)
+        critic_forward(ctx, self.critic, self.ccache, self.obs, m)
+        with torch.cuda.stream(ctx.stream):
+            value_out.view(-1)[:m].copy_(self.ccache.value[:m])
+
+
+class TicTacToeCriticHead:
+    """The network part of the search's critic model (envs/tictactoe_critic.mojo:98-192)."""
+
+    def __init__(self, ctx, max_batch, hidden, depth=2):
+        self.params = zero_critic_params(ctx, OBS_DIM, hidden, 1, depth)
+        self.cache = CriticCache(ctx, max_batch, self.params.dims)
+        self.obs = zero_buffer(ctx, max_batch * OBS_DIM)
+        self.hidden = hidden
+        self.max_batch = max_batch
+
+    def sync_from(self, ctx, src):
+        """:145-162"""
+        check_sync_shape(src.dims, self.params.dims, "critic being copied")
+        with torch.cuda.stream(ctx.stream):
+            self.params.flat.copy_(src.flat)
+
+    def value(self, ctx, state, value_out, m):
+        """V over m boards (the network half of eval_root, :170-192)."""
+        if m > self.max_batch:
+            raise ValueError(f"the model was reserved for {self.max_batch} boards and is being "
+                             f"asked for {m}")
+        ffi.call("spo_encode_obs", ctx.handle, _p(self.obs), None, _p(state), m)
+        critic_forward(ctx, self.params, self.cache, self.obs, m)
+        with torch.cuda.stream(ctx.stream):
+            value_out.view(-1)[:m].copy_(self.cache.value[:m])

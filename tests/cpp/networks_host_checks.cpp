@@ -112,5 +112,15 @@ int main() {
     expect(a.unsafe_ptr() == nullptr && a.size() == 0 && b2.size() == 7, "borrowed_move");
   }
 
+  // the search models' weight-sync shape test (envs/tictactoe_actor.mojo:121-140)
+  {
+    const Error e = thrown_by([] { check_sync_shape({27, 64, 64, 9}, {27, 128, 128, 9}, "actor being copied"); });
+    expect(e.code() == SPO_ERR_SHAPE &&
+               std::string(e.what()) == "the actor being copied does not have the model's shape: 27x64x64x9",
+           "sync_shape_message", e.what());
+    expect(thrown_by([] { check_sync_shape({27, 128, 128, 1}, {27, 128, 128, 1}, "critic"); }).code() == 0,
+           "sync_shape_equal");
+  }
+
   return failures ? 1 : 0;
 }

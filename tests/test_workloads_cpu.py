@@ -108,3 +108,14 @@ def test_per_sample_work():
     assert WORKLOADS["c3"].input_bytes_per_sample() == 108 + 3 * 36 + 4
     assert WORKLOADS["c0"].param_count() == 21257 + 1   # + log_alpha
     assert WORKLOADS["c3"].param_count() == 1084426 + 1
+
+
+def test_search_head_sync_shape_check():
+    """The search models copy a network only into one of the same shape, and say which
+    shape they were given (envs/tictactoe_actor.mojo:121-140)."""
+    from spo_mojo_b200.networks import check_sync_shape
+    check_sync_shape((27, 128, 128, 9), [27, 128, 128, 9], "actor being copied")
+    with pytest.raises(ValueError, match=r"the actor being copied does not have the model's shape: 27x64x64x9"):
+        check_sync_shape((27, 64, 64, 9), (27, 128, 128, 9), "actor being copied")
+    with pytest.raises(ValueError, match="critic"):
+        check_sync_shape((27, 128, 128, 128, 1), (27, 128, 128, 1), "critic")
