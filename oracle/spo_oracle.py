@@ -21,7 +21,10 @@ family, Adam with global-norm clip, EMA and truncated GAE.
 Parity unpinned (no reference code or golden covers these; they rest on this
 restatement and on the algebra written beside each): the alpha*KL(pi_old||pi) term,
 the log_alpha dual gradient, the 27-wide three-plane input, more than two hidden
-layers, and Adam eps = 1e-8 (the reference hard-codes 1e-5).
+layers, and Adam eps = 1e-8 (the reference hard-codes 1e-5). Their algebra is
+cross-checked (tests/test_oracle_autograd.py) against float64 automatic
+differentiation of the loss written from its definition and against torch.optim.Adam,
+the role JAX autodiff and optax play for the reference's own goldens.
 """
 
 import numpy as np
