@@ -549,7 +549,8 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
 // Backward of the hidden layers L-2..1 on the tensor cores (dW split over rows; dX with
 // the ReLU mask and the bias-gradient column sums fused), then layer 0's dW on the CUDA
 // cores from the fp32 dz0.
-int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* params, LayerInput in,
+int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* /*params: the hidden weights
+                    come from their TF32 splits, made by the forward*/, LayerInput in,
                     int64_t rows, float* grads, ReduceParams& red, int* err) {
   const spo_mlp_desc& d = n.d;
   const int L = d.num_layers;
@@ -814,7 +815,8 @@ int spo_linear_fwd(spo_stream_t stream, float* y, const float* x, const float* w
   return gemm_fwd(S(stream), y, x, w, b, m, k, n, act == SPO_ACT_RELU);
 }
 
-size_t spo_linear_bwd_workspace_size(int64_t m, int64_t k, int64_t n) {
+size_t spo_linear_bwd_workspace_size(int64_t /*m: the bound holds for any row count*/, int64_t k,
+                                      int64_t n) {
   Carve c(nullptr);
   c.take<float>((size_t)(dw_parts_bound(k, n) * k * n));
   c.take<float>((size_t)(kColsumChunks * n));
