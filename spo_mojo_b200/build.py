@@ -24,6 +24,7 @@ ROOT = os.path.dirname(HERE)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+          "-Xcompiler", "-Wall,-Wextra",
           "--expt-relaxed-constexpr"]
 
 
