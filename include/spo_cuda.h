@@ -112,7 +112,10 @@ SPO_API int spo_linear_bwd(spo_stream_t stream, float* dw, float* db, float* dx,
  * every GPU loading this library keeps until the process exits. Limits: k*n + 256*n must
  * not exceed 2,097,152 floats (larger shapes return SPO_ERR_WORKSPACE; use
  * spo_linear_bwd). The first call on a device looks the array's address up (once, with
- * that device current); make that first call before any stream capture. All calls share
+ * that device current); make that first call before any stream capture. The address is
+ * kept for the life of the process: after cudaDeviceReset (or any teardown of the
+ * device's primary context) it is stale, so do not call this function again in a process
+ * that has reset the device. All calls share
  * the array, so calls whose work overlaps on the GPU (other streams, other threads)
  * race: serialise them. Nothing in the array needs clearing between calls. */
 SPO_API int spo_linear_bwd_noalloc(spo_stream_t stream, float* dw, float* db, float* dx,
@@ -198,6 +201,34 @@ SPO_API int spo_critic_head_fwd_bwd(spo_stream_t stream, const float* act, const
                             float scale, float* v_out, float* dv_out, float* dact, float* dw,
                             float* db, float* dbact, float* stats, void* workspace,
                             size_t workspace_bytes);
+
+/* Loss on caller-held outputs, for a caller that runs its own forward (the reference's
+ * actor_backward networks/actor_loss.mojo:194-214 starts from the logits; critic_backward
+ * networks/mlp.mojo:212-233 from V). Deterministic: per-CTA partial sums in the workspace
+ * (spo_loss_workspace_size bytes) are added in a fixed order.
+ *
+ * spo_actor_loss_fwd_bwd: mask_logits_kernel (networks/actor.mojo:50-71), log_softmax_rows
+ * (ops/softmax.mojo:101-135), cross_entropy/entropy/kl rows (networks/actor_loss.mojo:40-148)
+ * and logits_grad_kernel (:168-191) in one pass over logits [rows x a] (a <= 32), plus the
+ * alpha*KL(pi_old || pi) term when logits_old != NULL (alpha = softplus(*log_alpha)):
+ *   dz [rows x a] = ((pi - q) + alpha (pi - pi_old)) * scale, 0 where mask == 0
+ *   loss_stats[SPO_STAT_ACTOR_LOSS .. SPO_STAT_KL_OLD] = scale * sums over rows
+ *   *dlog_alpha (optional, device) = sigmoid(log_alpha) * (eps_kl - loss_stats[SPO_STAT_KL_OLD])
+ * mask may be NULL (every action legal); log_alpha is a device scalar (NULL: 0 when
+ * logits_old is NULL). Only the listed stats slots are written. scale is normally 1 / rows
+ * (the reference's 1/m).
+ * spo_value_loss_fwd_bwd: value_loss_grad_kernel networks/mlp.mojo:141-152 and the loss of
+ * demos/train_critic.mojo:317-327 over n values: dv = (v - target) * scale,
+ * loss_stats[SPO_STAT_CRITIC_LOSS] = scale * sum 0.5 (v - target)^2 (the only slot written). */
+SPO_API size_t spo_loss_workspace_size(void);
+SPO_API int spo_actor_loss_fwd_bwd(spo_stream_t stream, const float* logits, const float* mask,
+                                   const float* q, const float* logits_old, const float* log_alpha,
+                                   float eps_kl, int64_t rows, int32_t a, float scale, float* dz,
+                                   float* loss_stats, float* dlog_alpha, void* workspace,
+                                   size_t workspace_bytes);
+SPO_API int spo_value_loss_fwd_bwd(spo_stream_t stream, const float* v, const float* target, int64_t n,
+                                   float scale, float* dv, float* loss_stats, void* workspace,
+                                   size_t workspace_bytes);
 
 /* ------------------------------------------------------------------ optimiser
  * sum_squares networks/optim.mojo:115-130 without the host round trip: *out (device)

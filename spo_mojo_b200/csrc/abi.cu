@@ -1095,6 +1095,32 @@ int spo_critic_head_fwd_bwd(spo_stream_t stream, const float* act, const float* 
   return head_common(S(stream), hp, dw, db, dbact, stats, workspace, workspace_bytes);
 }
 
+size_t spo_loss_workspace_size(void) { return sizeof(float) * (size_t)(loss_parts_max() * kStats) + 256; }
+
+int spo_actor_loss_fwd_bwd(spo_stream_t stream, const float* logits, const float* mask, const float* q,
+                           const float* logits_old, const float* log_alpha, float eps_kl, int64_t rows,
+                           int32_t a, float scale, float* dz, float* loss_stats, float* dlog_alpha,
+                           void* workspace, size_t workspace_bytes) {
+  SPO_CHECK_ARG(rows >= 0 && a >= 1 && a <= 32, kErrShape, "rows >= 0 and 1 <= a <= 32 required");
+  SPO_CHECK_ARG(loss_stats != nullptr, kErrArg, "loss_stats is required");
+  SPO_CHECK_ARG(rows == 0 || (logits && q && dz), kErrArg, "logits, q and dz are required");
+  SPO_CHECK_ARG(!logits_old || log_alpha, kErrArg, "logits_old needs log_alpha");
+  SPO_CHECK_ARG(workspace && workspace_bytes >= spo_loss_workspace_size(), kErrWorkspace,
+                "workspace too small");
+  return actor_loss_launch(logits, mask, q, logits_old, log_alpha, eps_kl, rows, a, scale, dz, loss_stats,
+                           dlog_alpha, static_cast<float*>(workspace), S(stream));
+}
+
+int spo_value_loss_fwd_bwd(spo_stream_t stream, const float* v, const float* target, int64_t n, float scale,
+                           float* dv, float* loss_stats, void* workspace, size_t workspace_bytes) {
+  SPO_CHECK_ARG(n >= 0, kErrShape, "n >= 0 required");
+  SPO_CHECK_ARG(loss_stats != nullptr, kErrArg, "loss_stats is required");
+  SPO_CHECK_ARG(n == 0 || (v && target && dv), kErrArg, "v, target and dv are required");
+  SPO_CHECK_ARG(workspace && workspace_bytes >= spo_loss_workspace_size(), kErrWorkspace,
+                "workspace too small");
+  return value_loss_launch(v, target, n, scale, dv, loss_stats, static_cast<float*>(workspace), S(stream));
+}
+
 // ---------------------------------------------------------------- optimiser
 size_t spo_sum_squares_workspace_size(void) { return sizeof(float) * kSumsqParts + 256; }
 
@@ -1444,11 +1470,14 @@ extern "C" int spo_linear_bwd_noalloc(spo_stream_t stream, float* dw, float* db,
                                       const float* relu_src, int64_t m, int64_t k, int64_t n) {
   SPO_CHECK_ARG(m >= 0 && k >= 1 && n >= 1, kErrShape, "bad shape");
   SPO_CHECK_ARG(dw && db && (m == 0 || (x && dy)) && (!dx || w), kErrArg, "null pointer");
+  // bound n, then k, before forming k*n, so that no product of caller sizes can wrap
+  const bool fits = n <= kStaticScratchFloats / (kColsumChunks + 1) &&
+                    k <= (kStaticScratchFloats - kColsumChunks * n) / n;
+  SPO_CHECK_ARG(fits, kErrWorkspace,
+                "spo_linear_bwd_noalloc: k*n + 256*n exceeds its static scratch of " +
+                    std::to_string(kStaticScratchFloats) + " floats (k = " + std::to_string(k) +
+                    ", n = " + std::to_string(n) + "); use spo_linear_bwd with a workspace");
   const int64_t cs_floats = kColsumChunks * n;
-  SPO_CHECK_ARG(k * n + cs_floats <= kStaticScratchFloats, kErrWorkspace,
-                "spo_linear_bwd_noalloc: k*n + 256*n = " + std::to_string(k * n + cs_floats) +
-                    " floats exceeds its static scratch of " + std::to_string(kStaticScratchFloats) +
-                    " floats; use spo_linear_bwd with a workspace");
   float* scratch = nullptr;
   int rc = static_scratch(&scratch);
   if (rc) return rc;

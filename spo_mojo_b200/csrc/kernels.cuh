@@ -53,6 +53,15 @@ size_t head_smem_bytes(int H, int A, bool has_lo);
 int head_grid(const HeadParams& p);  // CTAs of the launch = partial-sum slots written
 int head_launch(HeadParams p, int grid, cudaStream_t s);
 
+// ---------------------------------------------------------------- losses on caller-held outputs
+// (loss.cu). part: [loss_parts_max()][kStats] floats of scratch.
+int64_t loss_parts_max();
+int actor_loss_launch(const float* z, const float* mask, const float* q, const float* z_old,
+                      const float* log_alpha, float eps_kl, int64_t rows, int A, float scale, float* dz,
+                      float* stats, float* dlog_alpha, float* part, cudaStream_t s);
+int value_loss_launch(const float* v, const float* target, int64_t n, float scale, float* dv, float* stats,
+                      float* part, cudaStream_t s);
+
 // ---------------------------------------------------------------- partial-sum reduction
 constexpr int kMaxSegs = 80;
 

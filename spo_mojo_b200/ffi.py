@@ -130,6 +130,9 @@ SIGNATURES = {
     "spo_actor_head_fwd_bwd": (INT, [P, P, P, P, I64, I32, I32, P, P, P, P, F, P, P, P, P, P, P, P,
                                      P, P, SZ]),
     "spo_critic_head_fwd_bwd": (INT, [P, P, P, P, I64, I32, P, F, P, P, P, P, P, P, P, P, SZ]),
+    "spo_loss_workspace_size": (SZ, []),
+    "spo_actor_loss_fwd_bwd": (INT, [P, P, P, P, P, P, F, I64, I32, F, P, P, P, P, SZ]),
+    "spo_value_loss_fwd_bwd": (INT, [P, P, P, I64, F, P, P, P, SZ]),
     "spo_sum_squares_workspace_size": (SZ, []),
     "spo_sum_squares": (INT, [P, P, I64, P, P, SZ]),
     "spo_global_clip_scale": (F, [F, F]),

@@ -304,6 +304,26 @@ def actor_backward(ctx, params, cache, grads, scratch, x, pi, q, mask, m):
     backward_from_dvalue(ctx, params, cache, grads, scratch, x, m)
 
 
+def actor_loss_fwd_bwd(ctx, dz, stats, logits, mask, q, m, num_actions=NUM_ACTIONS, logits_old=None,
+                       log_alpha=None, eps_kl=0.01, scale=None, dlog_alpha=None):
+    """The eq-11 loss on logits the caller computed, with the alpha*KL(pi_old || pi) term
+    when logits_old is given: dz = dL/dz (the reference's logits_grad_kernel, scaled by
+    1/m unless scale is given), the batch statistics into stats[0:5] (ffi.STAT) and the
+    dual gradient into dlog_alpha[0] (optional). log_alpha: a one-element device tensor."""
+    ws = ctx.workspace(ffi.lib().spo_loss_workspace_size())
+    ffi.call("spo_actor_loss_fwd_bwd", ctx.handle, _p(logits), _p(mask), _p(q), _p(logits_old),
+             _p(log_alpha), eps_kl, m, num_actions, 1.0 / m if scale is None else scale, _p(dz),
+             _p(stats), _p(dlog_alpha), ws.data_ptr(), ws.numel())
+
+
+def value_loss_fwd_bwd(ctx, dv, stats, value, target, n, scale=None):
+    """0.5 * MSE on values the caller computed (networks/mlp.mojo:141-152): dv and
+    stats[ffi.STAT['critic_loss']]."""
+    ws = ctx.workspace(ffi.lib().spo_loss_workspace_size())
+    ffi.call("spo_value_loss_fwd_bwd", ctx.handle, _p(value), _p(target), n,
+             1.0 / n if scale is None else scale, _p(dv), _p(stats), ws.data_ptr(), ws.numel())
+
+
 # ---------------------------------------------------------------- optimiser (networks/optim.mojo)
 
 class AdamState:

@@ -22,7 +22,7 @@ Families copied (reference generator in brackets):
   gae*      Stoix truncated GAE                 [gen_gae.py]
 
 Usage (needs the reference checkout; not run by the tests):
-    python tests/golden/import_reference_goldens.py /root/reference
+    python tests/golden/import_reference_goldens.py <reference checkout>
 """
 
 import hashlib
@@ -54,4 +54,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: import_reference_goldens.py <root of the reference checkout>")
+    main(sys.argv[1])

@@ -34,13 +34,13 @@ def _ffi():
     return ffi
 
 
-def _run(entry, x, w, dy, relu_src, m, k, n):
+def _run(entry, x, w, dy, relu_src, m, k, n, with_dx=True):
     f = _ffi()
     dw = torch.full((k, n), float("nan"), device="cuda")
     db = torch.full((n,), float("nan"), device="cuda")
     dx = torch.full((m, k), float("nan"), device="cuda")
-    args = [None, dw.data_ptr(), db.data_ptr(), dx.data_ptr(), x.data_ptr(), w.data_ptr(),
-            dy.data_ptr(), relu_src.data_ptr(), m, k, n]
+    args = [None, dw.data_ptr(), db.data_ptr(), dx.data_ptr() if with_dx else None, x.data_ptr(),
+            w.data_ptr(), dy.data_ptr(), None if relu_src is None else relu_src.data_ptr(), m, k, n]
     if entry == "spo_linear_bwd":
         nbytes = f.lib().spo_linear_bwd_workspace_size(m, k, n)
         ws = torch.empty(int(nbytes), dtype=torch.uint8, device="cuda")
@@ -51,24 +51,32 @@ def _run(entry, x, w, dy, relu_src, m, k, n):
     return dw, db, dx
 
 
-@pytest.mark.parametrize("m,k,n", [(4096, 512, 512), (777, 128, 256), (65536, 27, 512)])
-def test_noalloc_matches_workspace_entry_on_consecutive_calls(m, k, n):
+@pytest.mark.parametrize("m,k,n,with_dx", [(4096, 512, 512, True), (777, 128, 256, True),
+                                           (65536, 27, 512, True), (0, 128, 256, True),
+                                           (3000, 64, 128, False)])
+def test_noalloc_matches_workspace_entry_on_consecutive_calls(m, k, n, with_dx):
     g = torch.Generator(device="cuda").manual_seed(m + k + n)
     for call in range(2):
         x = torch.randn(m, k, device="cuda", generator=g).relu_()
         w = torch.randn(k, n, device="cuda", generator=g) / k ** 0.5
         dy = torch.randn(m, n, device="cuda", generator=g) * 1e-2
-        relu_src = x
-        want = _run("spo_linear_bwd", x, w, dy, relu_src, m, k, n)
-        got = _run("spo_linear_bwd_noalloc", x, w, dy, relu_src, m, k, n)
-        for name, a, b, tol in zip(("dW", "db", "dx"), got, want, (_tol(m), _tol(m), _tol(n))):
+        relu_src = x if with_dx else None   # without dx: neither dx nor its ReLU mask
+        want = _run("spo_linear_bwd", x, w, dy, relu_src, m, k, n, with_dx)
+        got = _run("spo_linear_bwd_noalloc", x, w, dy, relu_src, m, k, n, with_dx)
+        outs = zip(("dW", "db", "dx"), got, want, (_tol(m), _tol(m), _tol(n)))
+        for name, a, b, tol in list(outs)[:3 if with_dx else 2]:
             assert torch.isfinite(a).all(), f"call {call}: {name} not fully written"
             assert float((a - b).abs().max()) <= tol, f"call {call}: {name}"
+        if m == 0:  # no rows: the gradients of the weights are zero
+            assert float(got[0].abs().max()) == 0.0 and float(got[1].abs().max()) == 0.0
 
 
-def test_noalloc_refuses_shapes_beyond_its_scratch():
+@pytest.mark.parametrize("k,n", [(2048, 2048),          # k*n alone is 4,194,304 floats > 2,097,152
+                                 (2**40, 2**30),        # k*n wraps int64: refused, not wrapped
+                                 (2**40, 64),           # k alone too large
+                                 (1, 8192)])            # 256*n alone fills the scratch
+def test_noalloc_refuses_shapes_beyond_its_scratch(k, n):
     f = _ffi()
-    k = n = 2048  # k*n alone is 4,194,304 floats > 2,097,152
     with pytest.raises(f.SpoError) as e:
         f.call("spo_linear_bwd_noalloc", None, 1, 1, None, 1, 1, 1, None, 16, k, n)
     assert e.value.code == -4 and "static scratch" in str(e.value)
