@@ -141,7 +141,8 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "learner samples/sec (fwd+bwd+loss+Adam)", "value": sps,
         "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per_step * 1e3 * wl.batch / rows, "higher_is_better": True,
+        # the time of the step that was timed: one sample of rows_timed rows of the workload
+        "ms_per_step": per_step * 1e3, "rows_timed": rows, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl.describe(), "global_batch": wl.batch,
                    "sample_rows_per_step": rows},
@@ -160,14 +161,14 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
+    def __init__(self, gpu_indices):
+        self.gpus = ",".join(str(g) for g in gpu_indices)
         self.proc = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
@@ -239,12 +240,19 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
     kms = k0.elapsed_time(k1) / reps
     flops = 2.0 * rows * H * H
     achieved = flops / (kms / 1e3) / 1e12
-    peak = pk.get("bf16_tflops_sustained") or pk.get("bf16_tflops")
+    # the kernel is timed alone (back-to-back launches of it): the burst peak applies
+    peak = pk.get("bf16_tflops") or pk.get("bf16_tflops_sustained")
+    traffic = TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("bytes") if rows == 1048576 else None
+    fp32_bytes = 4.0 * (2 * rows * H + H * H + H)   # fp32 A read once, C written once, W, bias
     roof = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak,
             "unit": "TFLOP/s", "frac": achieved / peak,
-            "peak_kind": f"{kind} bf16 dense, sustained", "ms_per_launch": kms,
-            "traffic": TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("bytes") if rows == 1048576 else None,
-            "traffic_source": TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("source")}
+            "peak_kind": f"{kind} bf16 dense, burst (the kernel is timed alone)",
+            "frac_of_sustained_peak": achieved / (pk.get("bf16_tflops_sustained") or peak),
+            "ms_per_launch": kms,
+            "traffic": traffic,
+            "traffic_source": TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("source"),
+            "fp32_algorithmic_bytes": fp32_bytes,
+            "traffic_vs_fp32_bytes": traffic / fp32_bytes if traffic else None}
     if engine == "tensor":
         # 3xTF32 issues three TF32 MMAs per fp32 product; TF32 runs at half the bf16 rate
         roof["tf32_mma_tflops"] = 3 * achieved
@@ -349,6 +357,15 @@ def run_ours(args):
         with torch.cuda.stream(stream):
             graphs[key][0].replay()
 
+    # Clocks: rank 0 samples every GPU of the job with one nvidia-smi process, started
+    # before the warm-up so that its start-up is not inside the timed region.
+    def phys(i):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        return vis.split(",")[i] if vis else str(i)
+
+    clocks = ClockSampler([phys(i) for i in range(world)]) if rank == 0 else None
+    if clocks is not None:
+        clocks.start()
     torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -359,13 +376,6 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
 
-    gpu_index = local
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-    if vis:
-        try:
-            gpu_index = int(vis.split(",")[local])
-        except ValueError:
-            gpu_index = vis.split(",")[local]
     # A step whose inputs and activations fit in L2 is timed one step at a time, with a
     # write of twice the L2 size between steps (outside the timed events), so no step
     # reads what the previous one left in L2.
@@ -388,8 +398,6 @@ def run_ours(args):
         evs[-1][1].synchronize()
         return sum(a.elapsed_time(b) for a, b in evs) / args.steps
 
-    clocks = ClockSampler(gpu_index)
-    clocks.start()
     if flush:
         ms = flushed_ms(lambda i: step(batch))
     else:
@@ -401,12 +409,14 @@ def run_ours(args):
         t1.record(stream)
         t1.synchronize()
         ms = t0.elapsed_time(t1) / args.steps
-    clk = clocks.stop()
-    ms_max = ms
+    clk = clocks.stop() if clocks is not None else None
+    ms_max, ms_ranks = ms, [ms]
     if world > 1:
         tm = torch.tensor([ms], device=dev)
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        ms_max = float(tm.item())
+        every = [torch.zeros_like(tm) for _ in range(world)]
+        dist.all_gather(every, tm)
+        ms_ranks = [float(t.item()) for t in every]
+        ms_max = max(ms_ranks)
     value = B / (ms_max / 1e3)
     stats = L.stats()
 
@@ -461,6 +471,23 @@ def run_ours(args):
                "d2h_bytes_per_step": d2h, "ms_per_step": ems, "wall_ms_per_step": wall,
                "loss_read": float(stats_host[0])}
 
+    # ---- the step's one collective alone: the all-reduce of the flat gradient buffer,
+    # CUDA events on the learner's stream, averaged over 10 calls, max over ranks
+    allreduce_ms = None
+    if comm is not None:
+        dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            comm.allreduce_(L.grads, stream=stream)
+            a0.record(stream)
+            for _ in range(10):
+                comm.allreduce_(L.grads, stream=stream)
+            a1.record(stream)
+        a1.synchronize()
+        tm = torch.tensor([a0.elapsed_time(a1) / 10], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        allreduce_ms = float(tm.item())
+
     # ---- roofline of the dominant kernel: the hidden x hidden GEMM (forward shape)
     roof = None
     net = wl.actor or wl.critic
@@ -493,6 +520,12 @@ def run_ours(args):
                              ("working set per step > L2 (inputs %.0f MB, activations %.1f GB); no flush"
                               % (in_bytes / 1e6, act_bytes / 1e9))},
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+            "ms_per_rank": ms_ranks,
+            "allreduce_ms": allreduce_ms,
+            "allreduce_bytes": int(L.grads.numel() * 4) if world > 1 else 0,
+            # the whole step's arithmetic (forward, dW, dX: 2 flop per multiply-add, fp32
+            # products) over its measured time
+            "step_tflops_fp32": wl.flops_per_sample() * B / (ms_max / 1e3) / 1e12,
             "gpu_launches": count_launches(wl, clip, args.engine, rows) * args.steps,
             "engine": args.engine,
             "stats": stats,
@@ -513,7 +546,7 @@ def run_peaks():
     torch.cuda.set_device(0)
     tf32, fp32 = ctypes.c_double(), ctypes.c_double()
     rows = []
-    clocks = ClockSampler(0)
+    clocks = ClockSampler([0])
     clocks.start()
     for _ in range(3):
         ffi.call("spo_measure_peaks", torch.cuda.current_stream().cuda_stream, ctypes.byref(tf32), ctypes.byref(fp32))

@@ -322,6 +322,13 @@ typedef struct spo_tc_gemm_desc {
 } spo_tc_gemm_desc;
 SPO_API int spo_tc_gemm_shape(const spo_tc_gemm_desc* desc, int32_t* grid, int32_t* splits);
 SPO_API int spo_tc_gemm(spo_stream_t stream, const spo_tc_gemm_desc* desc);
+/* No reference counterpart: a test of the kernel's failure path. Runs spo_tc_gemm with the
+ * operands of each CTA's first k-block never loaded and every bounded wait limited to
+ * wait_us microseconds (1 .. 2,000,000; spo_tc_gemm waits up to 2 s). The MMA issuer's wait
+ * for the missing stage runs out: the kernel stops its roles, waits (bounded) for the copies
+ * and MMAs it issued, frees its tensor memory, writes a nonzero code to *desc->err (required)
+ * and returns. The output is undefined; the device stays usable. */
+SPO_API int spo_tc_gemm_withheld(spo_stream_t stream, const spo_tc_gemm_desc* desc, int64_t wait_us);
 /* hi/lo split of n floats; keep_positive: positive x never get hi == 0 (ReLU outputs). */
 SPO_API int spo_split_tf32(spo_stream_t stream, float* hi, float* lo, const float* x, int64_t n,
                            int32_t keep_positive);

@@ -1423,6 +1423,17 @@ int spo_tc_gemm(spo_stream_t stream, const spo_tc_gemm_desc* desc) {
   return tc_gemm_launch(a, S(stream));
 }
 
+int spo_tc_gemm_withheld(spo_stream_t stream, const spo_tc_gemm_desc* desc, int64_t wait_us) {
+  TcGemmArgs a;
+  int rc = tc_args_of(desc, &a);
+  if (rc) return rc;
+  SPO_CHECK_ARG(a.err != nullptr, kErrArg, "the failure test needs desc->err");
+  SPO_CHECK_ARG(wait_us >= 1 && wait_us <= 2000000, kErrArg, "wait_us must be in [1, 2000000]");
+  a.wait_ns = (uint64_t)wait_us * 1000u;
+  a.withhold = 1;  // the first k-block of every CTA is never loaded
+  return tc_gemm_launch(a, S(stream));
+}
+
 int spo_split_tf32(spo_stream_t stream, float* hi, float* lo, const float* x, int64_t n,
                    int32_t keep_positive) {
   SPO_CHECK_ARG(n >= 0 && (n == 0 || (hi && lo && x)), kErrArg, "bad argument");

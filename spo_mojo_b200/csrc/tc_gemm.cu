@@ -91,8 +91,8 @@ __host__ __device__ constexpr int seg_of() {
 // for an activation that no tensor-core product reads), without the mask bits.
 constexpr int kFwdF32 = 4;
 
-constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s
-constexpr uint64_t kDrainNs = 500000000ull;              // 0.5 s
+constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s: the limit of every wait
+// (the drains on the exit path wait a quarter of it)
 constexpr int kMaxColsumN = 1024;
 
 enum WaitCode : int { kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, kErrWaitTFull = 4 };
@@ -122,6 +122,9 @@ struct KParams {
   int* err;
   const uint32_t* mask_bits;
   uint32_t* c_bits;
+  uint64_t wait_ns;   // limit of every bounded wait
+  uint32_t withhold;  // 1 + the k-block (in the producer's count) whose operands are never
+                      // loaded, so that the MMA issuer's wait for them runs out (0: none)
 };
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -173,17 +176,17 @@ __device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) 
 }
 
 // Bounded wait. Returns false when this CTA aborted (another role gave up) or after
-// kWaitNs, in which case it raises the abort flag and records `code` in *err.
+// limit ns, in which case it raises the abort flag and records `code` in *err.
 template <bool CLUSTER = false>
 __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
-                          int code) {
+                          int code, uint64_t limit) {
   auto poll = [&]() { return CLUSTER ? mbar_try_cluster(bar, parity) : mbar_try(bar, parity); };
   if (poll()) return true;
   const uint64_t t0 = now_ns();
   while (true) {
     if (poll()) return true;
     if (*abort_flag) return false;
-    if (now_ns() - t0 > kWaitNs) {
+    if (now_ns() - t0 > limit) {
       *abort_flag = 1;
       if (err) atomicCAS(err, 0, code);
       return false;
@@ -192,9 +195,9 @@ __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_fla
 }
 
 // Bounded wait used on the exit path only (ignores the abort flag).
-__device__ void mbar_drain(uint32_t bar, uint32_t parity) {
+__device__ void mbar_drain(uint32_t bar, uint32_t parity, uint64_t limit) {
   const uint64_t t0 = now_ns();
-  while (!mbar_try(bar, parity) && now_ns() - t0 < kDrainNs) {
+  while (!mbar_try(bar, parity) && now_ns() - t0 < limit) {
   }
 }
 
@@ -427,10 +430,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       const int nkb = (int)((kend - kbeg + BK - 1) / BK);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-        if (!mbar_wait(smem_u32(&ctl->empty[s]), ph ^ 1, abort_flag, P.err, kErrWaitEmpty)) {
+        if (!mbar_wait(smem_u32(&ctl->empty[s]), ph ^ 1, abort_flag, P.err, kErrWaitEmpty, P.wait_ns)) {
           ok = false;
           break;
         }
+        // a test of the timeout path withholds one stage: its full barrier never completes
+        if (it + 1 == P.withhold) continue;
         const uint32_t bar = smem_u32(&ctl->full[s]);
         // the pair's transfers (both CTAs) complete on the first CTA's barrier
         if (leader) mbar_expect_tx(bar, PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
@@ -471,7 +476,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       if (leader) {
         const uint32_t first = it >= (uint32_t)STAGES ? it - STAGES : 0;
         for (uint32_t i = first; i < it; ++i)
-          mbar_drain(smem_u32(&ctl->full[i % STAGES]), (i / STAGES) & 1);
+          mbar_drain(smem_u32(&ctl->full[i % STAGES]), (i / STAGES) & 1, P.wait_ns / 4);
       } else {
         // the second CTA's copies complete on the first CTA's barriers: give them time
         const uint64_t t0 = now_ns();
@@ -510,7 +515,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
         for (int kb0 = 0; kb0 < nkb && ok; kb0 += SEG, ++seg_i) {
           const uint32_t acc = seg_i % NACC;
           if (!mbar_wait<PAIR>(smem_u32(&ctl->tempty[acc]), ((seg_i / NACC) & 1) ^ 1, abort_flag,
-                               P.err, kErrWaitTEmpty)) {
+                               P.err, kErrWaitTEmpty, P.wait_ns)) {
             ok = false;
             break;
           }
@@ -519,7 +524,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           const int kb1 = min(nkb, kb0 + SEG);
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-            if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull)) {
+            if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull, P.wait_ns)) {
               ok = false;
               break;
             }
@@ -559,7 +564,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
         mma_commit_pair(smem_u32(&ctl->drain));
       else
         mma_commit(smem_u32(&ctl->drain));
-      mbar_drain(smem_u32(&ctl->drain), 0);
+      mbar_drain(smem_u32(&ctl->drain), 0, P.wait_ns / 4);
     }
   } else if (warp >= 2) {
     // ------------------------------------------------ epilogue
@@ -611,7 +616,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       for (int sg = 0; sg < nseg; ++sg, ++seg_i) {
         const uint32_t acc = seg_i % NACC;
         if (!mbar_wait(smem_u32(&ctl->tfull[acc]), (seg_i / NACC) & 1, abort_flag, P.err,
-                       kErrWaitTFull)) {
+                       kErrWaitTFull, P.wait_ns)) {
           ok = false;
           break;
         }
@@ -1125,6 +1130,8 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.err = a.err;
   P.mask_bits = a.kind == TC_DX || a.kind == TC_DX_F32 ? a.mask_bits : nullptr;
   P.c_bits = a.kind == TC_FWD && a.c_lo ? a.c_bits : nullptr;
+  P.wait_ns = a.wait_ns > 0 ? a.wait_ns : kWaitNs;
+  P.withhold = a.withhold;
   const int grid = tc_gemm_grid(a);
   const size_t smem = tc_smem_bytes(a.kind, a.N, pair, bn);
   const int threads = threads_of(pair, bn);

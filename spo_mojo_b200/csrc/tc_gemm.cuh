@@ -46,6 +46,10 @@ struct TcGemmArgs {
   // word w of a row = column 32 w + j.
   const uint32_t* mask_bits;  // TC_DX*: used instead of mask when set (bit = keep)
   uint32_t* c_bits;           // TC_FWD: optional output, bit = (output > 0)
+  // Tests of the timeout path only: the limit of every bounded wait (0: 2 s) and
+  // 1 + the k-block whose operands the producer never loads (0: none).
+  uint64_t wait_ns;
+  uint32_t withhold;
 };
 
 // Launch configuration queries (host).

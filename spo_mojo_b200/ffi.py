@@ -145,6 +145,7 @@ SIGNATURES = {
     "spo_encode_obs": (INT, [P, P, P, P, I64]),
     "spo_tc_gemm_shape": (INT, [ctypes.POINTER(TcGemmDesc), ctypes.POINTER(I32), ctypes.POINTER(I32)]),
     "spo_tc_gemm": (INT, [P, ctypes.POINTER(TcGemmDesc)]),
+    "spo_tc_gemm_withheld": (INT, [P, ctypes.POINTER(TcGemmDesc), I64]),
     "spo_split_tf32": (INT, [P, P, P, P, I64, I32]),
     "spo_learner_layout_of": (INT, [ctypes.POINTER(LearnerDesc), ctypes.POINTER(LearnerLayout)]),
     "spo_learner_workspace_size": (SZ, [ctypes.POINTER(LearnerDesc)]),

@@ -6,7 +6,9 @@ max |want| per tensor (the reference's gradient metric,
 tests/test_actor_backward.mojo:59-71); post-Adam parameters rel 1e-4 / abs 1e-6.
 """
 
+import json
 import math
+import os
 
 import numpy as np
 import pytest
@@ -129,22 +131,54 @@ def check_against_oracle(wl, L, grads0, stats0, rep0, ora, nets, la, params, bat
                  O.adam_step(b, gb_, np.zeros_like(gb_), np.zeros_like(gb_), 1, wl.lr, wl.beta1,
                              wl.beta2, wl.adam_eps, clip_o)[0])
                 for (w, b), (gw_, gb_) in zip(params[which], og)]
-        check_adam(wl, L, which, grads0, og, want, params[which], rep0[f"clip_{which}"])
+        excluded = {}
+        check_adam(wl, L, which, grads0, og, want, params[which], rep0[f"clip_{which}"], excluded)
+        n_out = sum(e for e, _ in excluded.values())
+        n_all = sum(t for _, t in excluded.values())
+        _record_excluded(wl, rows, which, excluded)
+        # the undetermined updates are the gradients within the fp32 error of zero: few
+        assert n_out <= 0.03 * n_all, (which, excluded)
     if wl.actor is not None and wl.dual:
         want = ora["log_alpha"]["grad"]
         assert abs(rep0["dlog_alpha"] - want) <= 1e-4 * abs(want) + 1e-7
         assert abs(float(L.log_alpha) - la) <= PARAM_RTOL * abs(la) + PARAM_ATOL
 
 
-def check_adam(wl, L, which, grads_gpu, grads_ora, params_ora, p0, clip):
-    """Post-Adam parameters, rel 1e-4 / abs 1e-6, checked two ways.
+def _record_excluded(wl, rows, which, excluded):
+    """Appends the per-tensor counts of post-Adam elements checked only against the 2 lr
+    bound to the JSON-lines file named by SPO_PARITY_REPORT (when set)."""
+    path = os.environ.get("SPO_PARITY_REPORT")
+    if not path:
+        return
+    with open(path, "a") as f:
+        f.write(json.dumps({"workload": wl.name, "rows": rows, "net": which,
+                            "excluded": {k: list(v) for k, v in excluded.items()}}) + "\n")
 
-    Adam's first step moves a parameter by lr * g / (|g| + eps): for a gradient within
-    the gradient tolerance of zero its sign, hence the update, is not determined by the
-    fp32 inputs at all. So (1) the update is checked exactly as the optimiser defines it,
-    by applying the oracle's Adam (float64) to this library's own gradients, on every
-    element; (2) against the full oracle on every element whose gradient is clear of the
-    gradient tolerance (|g| > 10 * GRAD_RTOL * max|g| of its tensor).
+
+def adam_determined(g_or, g_gpu, lr, eps):
+    """Elements whose first Adam step lr * g / (|g| + eps) the fp32 gradient determines to
+    within PARAM_ATOL / 2: a gradient that is exactly zero in both (a unit no row
+    activates: the parameter does not move), or one whose magnitude is at least ten times
+    the tensor's largest gradient error d (so the sign is right) and large enough that the
+    step's sensitivity lr * eps * d / (|g| - d)^2 stays below PARAM_ATOL / 2."""
+    d = float(np.max(np.abs(g_gpu - g_or))) if g_or.size else 0.0
+    a = np.abs(g_or)
+    both_zero = (g_or == 0) & (g_gpu == 0)
+    big = (a >= 10 * d) & ((a - d) ** 2 * (0.5 * PARAM_ATOL) >= lr * eps * d)
+    return both_zero | big
+
+
+def check_adam(wl, L, which, grads_gpu, grads_ora, params_ora, p0, clip, report=None):
+    """Post-Adam parameters, rel 1e-4 / abs 1e-6, on every element, checked two ways.
+
+    Adam's first step moves a parameter by lr * g / (|g| + eps): for a gradient within the
+    gradient error of zero its sign, hence the update, is not determined by the fp32 inputs
+    at all. So (1) the update is checked exactly as the optimiser defines it, by applying
+    the oracle's Adam (float64) to this library's own gradients, on every element; (2)
+    against the full oracle on every element whose update the gradient determines
+    (adam_determined), and on the others (reported in `report`: a few tenths of a percent
+    of the elements, the gradients within the fp32 error of zero) to within the largest
+    step Adam can take, 2 lr.
     """
     for i, ((pw, pb), (gw, gb), (ogw, ogb), (ow, ob), (w0, b0)) in enumerate(
             zip(L.tensors(which), L.tensors(which, grads_gpu), grads_ora, params_ora, p0)):
@@ -155,9 +189,12 @@ def check_adam(wl, L, which, grads_gpu, grads_ora, params_ora, p0, clip):
                                      wl.lr, wl.beta1, wl.beta2, wl.adam_eps, clip)
             np.testing.assert_allclose(got, mine, rtol=PARAM_RTOL, atol=PARAM_ATOL,
                                        err_msg=f"{which} {nm}{i + 1}: Adam on our gradients")
-            clear = np.abs(g_or) > 10 * GRAD_RTOL * max(np.max(np.abs(g_or)), 1e-30)
+            clear = adam_determined(np.asarray(g_or, np.float64) * clip, g_gpu * clip, wl.lr, wl.adam_eps)
             np.testing.assert_allclose(got[clear], want[clear], rtol=PARAM_RTOL, atol=PARAM_ATOL,
                                        err_msg=f"{which} {nm}{i + 1}: oracle Adam")
+            assert np.all(np.abs(got[~clear] - want[~clear]) <= 2 * wl.lr * (1 + 1e-3) + PARAM_ATOL)
+            if report is not None:
+                report[f"{which} {nm}{i + 1}"] = (int((~clear).sum()), int(clear.size))
 
 
 @pytest.mark.parametrize("engine", ["tensor", "cuda"])
@@ -314,9 +351,11 @@ def test_deterministic(engine):
     assert torch.equal(g1, g2)
 
 
-@pytest.mark.parametrize("engine", ["tensor", "cuda"])
-def test_c3_full_batch_vs_float64(engine):
-    """c3 at its full 1,048,576 rows against a float64 restatement run on the GPU.
+@pytest.mark.parametrize("name,engine", [("c3", "tensor"), ("c3", "cuda"), ("c4", "tensor"), ("c4", "cuda")])
+def test_full_batch_vs_float64(name, engine):
+    """c3 at its full 1,048,576 rows (actor + critic 27-512x3-{9,1}) and c4 at its full
+    262,144 rows (actor 27-1024x4-9, the deepest products: 32 k-blocks each) against a
+    float64 restatement run on the GPU.
 
     Forward: every hidden activation within 1e-5 of max, losses within 1e-5 relative.
     ReLU decisions of activations within fp32 noise of zero can differ from float64
@@ -325,18 +364,18 @@ def test_c3_full_batch_vs_float64(engine):
     """
     import fp64_reference as R
     from spo_mojo_b200.learner import Learner
-    wl = WORKLOADS["c3"]
+    wl = WORKLOADS[name]
     B = wl.batch
     params = init_params(wl, seed=0)
     batch = to_dev(make_batch(wl, B, seed=13))
     L = Learner.for_workload(wl, max_rows=B, engine=engine)
-    L.load(actor=params["actor"], critic=params["critic"])
+    L.load(actor=params.get("actor"), critic=params.get("critic"), log_alpha=wl.log_alpha)
     L.backward(batch)
     torch.cuda.synchronize()
     assert L.device_status() == 0
     st = L.stats()
     x = batch["obs"].double()
-    for which in ("actor", "critic"):
+    for which in [w for w in ("actor", "critic") if w in params]:
         p64 = [(torch.from_numpy(w).cuda().double(), torch.from_numpy(b).cuda().double())
                for w, b in params[which]]
         acts, out = R.mlp_forward(p64, x)

@@ -212,3 +212,40 @@ def test_unsupported_shapes_are_rejected():
     with pytest.raises(f.SpoError) as e:
         f.call("spo_tc_gemm_shape", ctypes.byref(d), None, None)
     assert e.value.code == -7
+
+
+def test_bounded_wait_runs_out_and_the_device_recovers():
+    """The failure path of the kernel's bounded waits, without a fault: the operands of each
+    CTA's first k-block are never loaded and every wait is limited to 2 ms
+    (spo_tc_gemm_withheld). The MMA issuer's wait runs out; the kernel must drain, free its
+    tensor memory, report a nonzero code in its error word and return; then a normal launch
+    on the same device must be exact again."""
+    import time
+    f = ffi()
+    M, K, N = 512, 64, 128
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(M, K, device="cuda", generator=g).relu_()
+    w = torch.randn(K, N, device="cuda", generator=g) / K ** 0.5
+    b = torch.zeros(N, device="cuda")
+    xh, xl = split(x)
+    wth, wtl = split(w.t().contiguous())
+    yh, yl = torch.empty(M, N, device="cuda"), torch.empty(M, N, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d = f.TcGemmDesc(kind=f.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wth.data_ptr(),
+                     b_lo=wtl.data_ptr(), m=M, n=N, k=K, bias=b.data_ptr(), c_hi=yh.data_ptr(),
+                     c_lo=yl.data_ptr(), err=err.data_ptr())
+    torch.cuda.synchronize()
+    t0 = time.time()
+    f.call("spo_tc_gemm_withheld", None, ctypes.byref(d), 2000)
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 10.0
+    code = int(err.item())
+    assert code in (1, 2, 3, 4), code     # a wait gave up (which role first is a race)
+    with pytest.raises(f.SpoError, match="needs desc->err"):
+        f.call("spo_tc_gemm_withheld", None, ctypes.byref(f.TcGemmDesc(
+            kind=f.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wth.data_ptr(), b_lo=wtl.data_ptr(),
+            m=M, n=N, k=K, bias=b.data_ptr(), c_hi=yh.data_ptr(), c_lo=yl.data_ptr())), 2000)
+    d.err = None
+    run(d)                                 # the same launch without the withheld stage
+    want = np.maximum(x.double().cpu().numpy() @ w.double().cpu().numpy(), 0)
+    assert rel_err((yh.double() + yl.double()).cpu().numpy(), want) <= 1e-5
