@@ -216,15 +216,16 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
     bb = torch.zeros(H, device=dev)
     y = torch.empty(rows, H, device=dev)
     if engine == "tensor":
-        xh, xl, wh, wl, yl = (torch.empty_like(t) for t in (x, x, w, w, y))
-        for src, hi, lo in ((x, xh, xl), (w, wh, wl)):
-            ffi.call("spo_split_tf32", stream.cuda_stream, hi.data_ptr(), lo.data_ptr(), src.data_ptr(),
-                     src.numel(), 1)
-        d = ffi.TcGemmDesc(kind=ffi.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wh.data_ptr(),
+        # as the learner runs it: the activations plain fp32 (split into TF32 halves in shared
+        # memory by the kernel), W^T as a hi/lo pair, fp32 output with its packed ReLU mask
+        wh, wl = torch.empty_like(w), torch.empty_like(w)
+        ffi.call("spo_split_tf32", stream.cuda_stream, wh.data_ptr(), wl.data_ptr(), w.data_ptr(), w.numel(), 0)
+        bits = torch.empty(rows, H // 32, dtype=torch.int32, device=dev)
+        d = ffi.TcGemmDesc(kind=ffi.TC_FWD, a_hi=x.data_ptr(), a_lo=None, b_hi=wh.data_ptr(),
                            b_lo=wl.data_ptr(), m=rows, n=H, k=H, bias=bb.data_ptr(), c_hi=y.data_ptr(),
-                           c_lo=yl.data_ptr())
+                           c_bits=bits.data_ptr())
         launch = lambda: ffi.call("spo_tc_gemm", stream.cuda_stream, ctypes.byref(d))  # noqa: E731
-        name = "tc_gemm_kernel (tcgen05 3xTF32), hidden forward %dx%dx%d" % (rows, H, H)
+        name = "tc_gemm_kernel (tcgen05 3xTF32, fp32 operand split on chip), hidden forward %dx%dx%d" % (rows, H, H)
     else:
         launch = lambda: ffi.call("spo_linear_fwd", stream.cuda_stream, y.data_ptr(), x.data_ptr(),  # noqa: E731
                                   w.data_ptr(), bb.data_ptr(), rows, H, H, 1)
@@ -243,7 +244,8 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
     # the kernel is timed alone (back-to-back launches of it): the burst peak applies
     peak = pk.get("bf16_tflops") or pk.get("bf16_tflops_sustained")
     traffic = TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("bytes") if rows == 1048576 else None
-    fp32_bytes = 4.0 * (2 * rows * H + H * H + H)   # fp32 A read once, C written once, W, bias
+    # fp32 A read once, C written once, its packed mask, W^T as a hi/lo pair, bias
+    fp32_bytes = 4.0 * (2 * rows * H + 2 * H * H + H) + rows * H / 8
     roof = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak,
             "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_kind": f"{kind} bf16 dense, burst (the kernel is timed alone)",
@@ -266,12 +268,10 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
 
 
 # DRAM bytes (read + write) of one launch of the roofline kernel at 1,048,576 rows, from an
-# ncu capture of the same kernel at 262,144 rows (1.076 GB read + 1.045 GB write) scaled by
-# the 4x rows: the kernel streams its activations once, so traffic grows with the rows.
-TRAFFIC_PER_LAUNCH = {
-    ("tensor", 512): {"bytes": 4 * (1.075955e9 + 1.044996e9),
-                      "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum at 262144 rows x4"},
-}
+# ncu capture of the same kernel at 262,144 rows scaled by the 4x rows (the kernel streams
+# its activations once, so traffic grows with the rows). Filled in from the capture of the
+# current kernel (profiles/); absent until then.
+TRAFFIC_PER_LAUNCH = {}
 
 
 TC0_MIN_ROWS = 16384  # the library runs the input layer on tensor cores from this many rows

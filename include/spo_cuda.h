@@ -293,6 +293,10 @@ SPO_API int spo_encode_obs(spo_stream_t stream, float* obs, float* mask, const f
  *   SPO_TC_DW      C = A^T B from A [k x m], B [k x n], rows of k split in chunks of
  *                  k_chunk, one fp32 partial per chunk -> c_part [splits][m x n]
  * Shapes: n % 128 == 0; FWD/DX: k % 32 == 0, n <= 1024 for DX; DW: m % 128 == 0.
+ * Plain fp32 operands: with a_lo == NULL, A is plain fp32 in a_hi and the kernel splits it
+ * into its TF32 halves in shared memory (forward, dX: B must be a pair; dW: b_lo == NULL
+ * too, both operands plain fp32). With c_lo == NULL, SPO_TC_FWD writes plain fp32 (and
+ * c_bits when set).
  * colsum receives [grid][n] partials (grid from spo_tc_gemm_shape). All pointers
  * 16-byte aligned. err (optional) receives a nonzero code if a bounded wait of the
  * kernel gave up (the kernel then returns without hanging).
@@ -405,11 +409,10 @@ SPO_API int spo_learner_backward(spo_learner_t learner, spo_stream_t stream, con
 SPO_API int spo_learner_apply(spo_learner_t learner, spo_stream_t stream, const spo_train_state* state);
 /* The activation cache of the last forward (CriticCache a1, a2, ...,
  * networks/mlp.mojo:84-102): device pointers to the post-ReLU activations of hidden layer
- * `layer` (0-based, [rows x d_{layer+1}]) of network `which` (0 actor, 1 critic). With the
- * tensor-core engine the activations that feed tensor-core products are stored as TF32
- * hi/lo pairs (value = hi + lo) and *lo is set; otherwise (the CUDA-core engine, and the
- * last hidden layer, which only the fused head reads) *lo is NULL and *hi is the plain
- * fp32 value. Valid until the next call on the learner. */
+ * `layer` (0-based, [rows x d_{layer+1}]) of network `which` (0 actor, 1 critic), plain fp32
+ * in *hi with either engine (the tensor-core kernels split their operands on chip); *lo is
+ * always set to NULL (kept for callers of the earlier hi/lo form). Valid until the next
+ * call on the learner. */
 SPO_API int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer,
                               const float** hi, const float** lo);
 /* Reads (synchronously) and clears the learner's device error word: 0 when every

@@ -270,8 +270,9 @@ fwd_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, 
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-// Tensor-core operands of the first layer: the input rows padded to kPadK columns as TF32
-// hi/lo pairs (zeros past k), and W^T [n x kPadK] likewise. One thread per element.
+// Tensor-core operands of the first layer: the input rows padded to kPadK columns (zeros
+// past k), as plain fp32 (lo null) or TF32 hi/lo pairs, and W^T [n x kPadK] as hi/lo
+// pairs. One thread per element.
 __global__ void pad_split_input_kernel(const float* __restrict__ x, const float* __restrict__ cells, int k,
                                        int64_t rows, float* __restrict__ hi, float* __restrict__ lo) {
   pdl_wait();
@@ -290,10 +291,14 @@ __global__ void pad_split_input_kernel(const float* __restrict__ x, const float*
         v = __ldg(x + r * k + c);
       }
     }
-    float h, l;
-    tf32_split(v, h, l);
-    hi[e] = h;
-    lo[e] = l;
+    if (lo) {
+      float h, l;
+      tf32_split(v, h, l);
+      hi[e] = h;
+      lo[e] = l;
+    } else {
+      hi[e] = v;   // plain fp32: the tensor-core kernel splits it
+    }
   }
 }
 

@@ -152,7 +152,8 @@ int fwd_skinny_launch(LayerInput in, const float* w, const float* b, int64_t row
                       float* y, float* y_lo, uint32_t* bits, cudaStream_t s);
 
 // The first layer on tensor cores: input rows [rows x k] (k <= 32) padded to 32 columns as
-// TF32 hi/lo pairs, and W [k x n] as W^T [n x 32] hi/lo pairs (zeros past k).
+// plain fp32 (lo null) or TF32 hi/lo pairs, and W [k x n] as W^T [n x 32] hi/lo pairs
+// (zeros past k).
 int pad_split_input_launch(LayerInput in, int64_t k, int64_t rows, float* hi, float* lo, cudaStream_t s);
 int split_weights_t_pad_launch(const float* w, int64_t k, int64_t n, float* wt_hi, float* wt_lo, cudaStream_t s);
 

@@ -40,6 +40,12 @@ constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
 constexpr int STAGES_MAX = 4;
 constexpr int NACC_MAX = 4;
 constexpr uint32_t TMEM_COLS = 512;                      // the whole TMEM of the SM
+constexpr int kConvWarps = 2;                            // operand-split warps (fp32 operands)
+
+// Operands held in global memory as plain fp32 ("raw") instead of TF32 hi/lo pairs: the
+// producer loads them into the hi slot of a stage and the split warps write hi (in place)
+// and lo before the MMAs read the stage. RAW bit 0: A, bit 1: B.
+constexpr int kRawA = 1, kRawB = 2;
 
 // Geometry of one instantiation: PAIR = CTA pair (cta_group::2), TBN = output columns per
 // tile (128, or 256 when N allows: one 128 x 256 MMA per k-step reads A once for twice the
@@ -49,7 +55,7 @@ constexpr uint32_t TMEM_COLS = 512;                      // the whole TMEM of th
 // the MMA issued by the pair's first CTA reads both CTAs' shared memory. The ring takes as
 // many stages as fit in ~200 KB; TMEM holds 512 / TBN accumulators; the epilogue has one
 // warp per (TMEM lane quadrant, 64-column group).
-template <bool PAIR, int TBN>
+template <bool PAIR, int TBN, int RAW = 0>
 struct Geo {
   static constexpr int BN = TBN;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
@@ -62,7 +68,9 @@ struct Geo {
   static constexpr int NACC = (int)(TMEM_COLS / BN);
   static constexpr int EPI_WARPS = 4 * (BN / EPI_COLS);
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-  static constexpr int THREADS = 64 + EPI_THREADS;
+  // fp32 operands are split into their hi/lo halves in shared memory by these warps
+  static constexpr int CONV_WARPS = RAW != 0 ? kConvWarps : 0;
+  static constexpr int THREADS = 64 + EPI_THREADS + 32 * CONV_WARPS;
 };
 // The tensor core's accumulation into TMEM is not exact fp32: its error grows with the
 // number of MMAs summed into one accumulator. The epilogue therefore folds each
@@ -95,11 +103,14 @@ constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s: the limit of ev
 // (the drains on the exit path wait a quarter of it)
 constexpr int kMaxColsumN = 1024;
 
-enum WaitCode : int { kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, kErrWaitTFull = 4 };
+enum WaitCode : int {
+  kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, kErrWaitTFull = 4, kErrWaitLoaded = 5
+};
 
 struct __align__(64) Ctl {
-  uint64_t full[STAGES_MAX];
-  uint64_t empty[STAGES_MAX];
+  uint64_t full[STAGES_MAX];     // operands ready for the MMAs
+  uint64_t empty[STAGES_MAX];    // stage consumed by the MMAs
+  uint64_t loaded[STAGES_MAX];   // raw operands: the stage's copies have landed
   uint64_t tfull[NACC_MAX];
   uint64_t tempty[NACC_MAX];
   uint64_t drain;
@@ -343,16 +354,49 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// TF32 hi/lo split of n4 float4 of a stage tile in place (hi) and into lo, threads t of nt.
+__device__ __forceinline__ void split_tile(float4* hi, float4* lo, int n4, int t, int nt) {
+#pragma unroll 4
+  for (int i = t; i < n4; i += nt) {
+    float4 v = hi[i], l;
+    tf32_split(v.x, v.x, l.x);
+    tf32_split(v.y, v.y, l.y);
+    tf32_split(v.z, v.z, l.z);
+    tf32_split(v.w, v.w, l.w);
+    hi[i] = v;
+    lo[i] = l;
+  }
+}
+
+// Stores the packed ReLU bits of a warp's 64 columns (c0 = first column) for its 32 rows:
+// the 4 threads of a row hold disjoint bits, OR them, one thread stores the two words.
+__device__ __forceinline__ void store_bits(uint32_t (&bw)[2][4], const KParams& P, int64_t wrow0, int tr,
+                                           int lane, int64_t c0) {
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1)
+#pragma unroll
+      for (int w = 0; w < 4; ++w) bw[hh][w] |= __shfl_xor_sync(0xffffffffu, bw[hh][w], o);
+    const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
+    if ((lane & 3) == 0) {
+      const int64_t wpr = P.N / 32, w0 = c0 / 32;
+      if (ra < P.M) *reinterpret_cast<uint2*>(P.c_bits + ra * wpr + w0) = make_uint2(bw[hh][0], bw[hh][1]);
+      if (rb < P.M) *reinterpret_cast<uint2*>(P.c_bits + rb * wpr + w0) = make_uint2(bw[hh][2], bw[hh][3]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- the kernel
 // One instantiation per epilogue (KIND) and dX mask format (BITS: packed bits instead of
 // fp32). 10 warps share the SM's four 16K-register files 3/3/2/2: at most 168 registers a
 // thread.
-template <int KIND, bool BITS, bool PAIR, int TBN>
-__global__ void __launch_bounds__(Geo<PAIR, TBN>::THREADS, 1)
+template <int KIND, bool BITS, bool PAIR, int TBN, int RAW>
+__global__ void __launch_bounds__(Geo<PAIR, TBN, RAW>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
                const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
                const KParams P) {
-  using G = Geo<PAIR, TBN>;
+  using G = Geo<PAIR, TBN, RAW>;
   constexpr int BN = G::BN;
   constexpr int NACC = G::NACC;
   constexpr int kEpiWarps = G::EPI_WARPS;
@@ -379,8 +423,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&ctl->full[s]), 1);
+      // raw operands: the split warps of both CTAs of a pair arrive on the first CTA's barrier
+      mbar_init(smem_u32(&ctl->full[s]), RAW ? (PAIR ? 2 : 1) * G::CONV_WARPS : 1);
       mbar_init(smem_u32(&ctl->empty[s]), 1);
+      mbar_init(smem_u32(&ctl->loaded[s]), 1);
     }
     for (int a = 0; a < NACC; ++a) {
       mbar_init(smem_u32(&ctl->tfull[a]), 1);
@@ -434,14 +480,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           ok = false;
           break;
         }
-        // a test of the timeout path withholds one stage: its full barrier never completes
+        // a test of the timeout path withholds one stage: its barriers never complete
         if (it + 1 == P.withhold) continue;
-        const uint32_t bar = smem_u32(&ctl->full[s]);
-        // the pair's transfers (both CTAs) complete on the first CTA's barrier
-        if (leader) mbar_expect_tx(bar, PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
-        const uint32_t cbar = PAIR ? map_to_rank(bar, 0) : bar;
+        // Raw operands: every CTA's copies complete on its own `loaded` barrier (its split
+        // warps wait there). Otherwise on `full`, a pair's (both CTAs') on the first CTA's.
+        const uint32_t bar = smem_u32(RAW ? &ctl->loaded[s] : &ctl->full[s]);
+        constexpr uint32_t kMyBytes = ((RAW & kRawA) ? A_TILE : 2 * A_TILE) + ((RAW & kRawB) ? B_TILE : 2 * B_TILE);
+        if (RAW)
+          mbar_expect_tx(bar, kMyBytes);
+        else if (leader)
+          mbar_expect_tx(bar, PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
+        const uint32_t cbar = PAIR && !RAW ? map_to_rank(bar, 0) : bar;
         auto load = [&](uint32_t dst, const CUtensorMap* m, int32_t x, int32_t y) {
-          if constexpr (PAIR)
+          if constexpr (PAIR && !RAW)
             tma_load_2d_pair(dst, m, cbar, x, y);
           else
             tma_load_2d(dst, m, bar, x, y);
@@ -449,34 +500,36 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
         const int32_t k0 = (int32_t)(kbeg + (int64_t)kb * BK);
         const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
         const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
+        constexpr bool ra = (RAW & kRawA) != 0, rb = (RAW & kRawB) != 0;
         if (P.a_mn) {
 #pragma unroll
           for (int j = 0; j < BM / 32; ++j) {
             load(a_hi + j * 4096, &tm_ah, m0 + 32 * j, k0);
-            load(a_lo + j * 4096, &tm_al, m0 + 32 * j, k0);
+            if (!ra) load(a_lo + j * 4096, &tm_al, m0 + 32 * j, k0);
           }
         } else {
           load(a_hi, &tm_ah, k0, m0);
-          load(a_lo, &tm_al, k0, m0);
+          if (!ra) load(a_lo, &tm_al, k0, m0);
         }
         if (P.b_mn) {
 #pragma unroll
           for (int j = 0; j < G::B_ROWS / 32; ++j) {
             load(b_hi + j * 4096, &tm_bh, n0 + 32 * j, k0);
-            load(b_lo + j * 4096, &tm_bl, n0 + 32 * j, k0);
+            if (!rb) load(b_lo + j * 4096, &tm_bl, n0 + 32 * j, k0);
           }
         } else {
           load(b_hi, &tm_bh, k0, n0);
-          load(b_lo, &tm_bl, k0, n0);
+          if (!rb) load(b_lo, &tm_bl, k0, n0);
         }
       }
     }
     if (!ok) {
       // let the copies already issued land before the CTA's shared memory goes away
-      if (leader) {
+      if (RAW || leader) {
         const uint32_t first = it >= (uint32_t)STAGES ? it - STAGES : 0;
         for (uint32_t i = first; i < it; ++i)
-          mbar_drain(smem_u32(&ctl->full[i % STAGES]), (i / STAGES) & 1, P.wait_ns / 4);
+          mbar_drain(smem_u32(RAW ? &ctl->loaded[i % STAGES] : &ctl->full[i % STAGES]), (i / STAGES) & 1,
+                     P.wait_ns / 4);
       } else {
         // the second CTA's copies complete on the first CTA's barriers: give them time
         const uint64_t t0 = now_ns();
@@ -524,7 +577,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           const int kb1 = min(nkb, kb0 + SEG);
           for (int kb = kb0; kb < kb1; ++kb, ++it) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
-            if (!mbar_wait(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull, P.wait_ns)) {
+            if (!mbar_wait<(PAIR && RAW != 0)>(smem_u32(&ctl->full[s]), ph, abort_flag, P.err, kErrWaitFull,
+                                              P.wait_ns)) {
               ok = false;
               break;
             }
@@ -565,6 +619,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       else
         mma_commit(smem_u32(&ctl->drain));
       mbar_drain(smem_u32(&ctl->drain), 0, P.wait_ns / 4);
+    }
+  } else if (RAW && warp >= 2 + kEpiWarps) {
+    // ------------------------------------------------ operand split
+    // The raw (fp32) operand tiles of each stage become TF32 hi/lo pairs in place: hi
+    // overwrites the fp32 value, lo goes to the stage's lo slot at the same offset (the
+    // split is elementwise, so the TMA swizzle of the tile carries over to both halves).
+    // Then the writes are made visible to the tensor core (async proxy) and the stage is
+    // handed to the MMA issuer, in the first CTA of a pair.
+    const int ct = (warp - 2 - kEpiWarps) * 32 + lane;
+    constexpr int kCT = 32 * G::CONV_WARPS;
+    const uint32_t full0 = smem_u32(&ctl->full[0]);
+    const uint32_t full_at = PAIR ? map_to_rank(full0, 0) : full0;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int64_t u = first_unit; u < P.units && ok; u += unit_step) {
+      const int64_t split = u / per_split;
+      const int64_t kbeg = split * P.k_chunk;
+      const int64_t kend = min(P.K, kbeg + P.k_chunk);
+      const int nkb = (int)((kend - kbeg + BK - 1) / BK);
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+        if (!mbar_wait(smem_u32(&ctl->loaded[s]), ph, abort_flag, P.err, kErrWaitLoaded, P.wait_ns)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        if constexpr ((RAW & kRawA) != 0)
+          split_tile(reinterpret_cast<float4*>(st), reinterpret_cast<float4*>(st + A_TILE), A_TILE / 16, ct, kCT);
+        if constexpr ((RAW & kRawB) != 0)
+          split_tile(reinterpret_cast<float4*>(st + 2 * A_TILE), reinterpret_cast<float4*>(st + 2 * A_TILE + B_TILE),
+                     B_TILE / 16, ct, kCT);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR && !leader)
+            mbar_arrive_cluster(full_at + s * 8);
+          else
+            mbar_arrive(full0 + s * 8);
+        }
+      }
     }
   } else if (warp >= 2) {
     // ------------------------------------------------ epilogue
@@ -670,10 +764,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
         // only a few values besides the running sums are live at once.
         const int64_t cbase = n0 + cb + tc;
         if constexpr (KIND == kFwdF32) {
+          uint32_t bw[2][4] = {};  // [hh]: bits of rows ra, rb, columns 0-31 / 32-63
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
             const int64_t col = cbase + 8 * g;
             const float2 b2 = __ldg(reinterpret_cast<const float2*>(P.bias + col));
+            const uint32_t sh = (8 * g + tc) & 31;
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
               const float* v = rs + 32 * hh;
@@ -682,8 +778,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
               const float x2 = v[4 * g + 2] + b2.x, x3 = v[4 * g + 3] + b2.y;
               if (ra < P.M) store2(P.c_hi + ra * P.N + col, x0 > 0.f ? x0 : 0.f, x1 > 0.f ? x1 : 0.f);
               if (rb < P.M) store2(P.c_hi + rb * P.N + col, x2 > 0.f ? x2 : 0.f, x3 > 0.f ? x3 : 0.f);
+              if (BITS) {
+                const uint32_t pa = (x0 > 0.f ? 1u : 0u) | (x1 > 0.f ? 2u : 0u);
+                const uint32_t pb = (x2 > 0.f ? 1u : 0u) | (x3 > 0.f ? 2u : 0u);
+                bw[hh][(g < 4 ? 0 : 1)] |= pa << sh;
+                bw[hh][(g < 4 ? 2 : 3)] |= pb << sh;
+              }
             }
           }
+          if (BITS) store_bits(bw, P, wrow0, tr, lane, n0 + cb);
         } else if constexpr (KIND == TC_FWD) {
           uint32_t bw[2][4] = {};  // [hh]: bits of rows ra, rb, columns 0-31 / 32-63
 #pragma unroll
@@ -714,22 +817,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
               bw[hh][(g < 4 ? 2 : 3)] |= pb << sh;
             }
           }
-          if (P.c_bits) {
-            // the 4 threads of a row hold disjoint bits: OR them, one thread stores
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-              for (int o = 1; o <= 2; o <<= 1)
-#pragma unroll
-                for (int w = 0; w < 4; ++w) bw[hh][w] |= __shfl_xor_sync(0xffffffffu, bw[hh][w], o);
-              const int64_t ra = wrow0 + 16 * hh + tr, rb = ra + 8;
-              if ((lane & 3) == 0) {
-                const int64_t wpr = P.N / 32, w0 = (n0 + cb) / 32;
-                if (ra < P.M) *reinterpret_cast<uint2*>(P.c_bits + ra * wpr + w0) = make_uint2(bw[hh][0], bw[hh][1]);
-                if (rb < P.M) *reinterpret_cast<uint2*>(P.c_bits + rb * wpr + w0) = make_uint2(bw[hh][2], bw[hh][3]);
-              }
-            }
-          }
+          if (P.c_bits) store_bits(bw, P, wrow0, tr, lane, n0 + cb);
         } else if constexpr (dx) {
 #pragma unroll
           for (int g = 0; g < 8; ++g) {
@@ -938,7 +1026,10 @@ int tile_n(int kind, bool fp32_fwd, int64_t N) {
 }
 int tile_of(const TcGemmArgs& a) { return tile_n(a.kind, a.c_lo == nullptr, a.N); }
 
-int threads_of(bool pair, int bn) {
+int threads_of(bool pair, int bn, int raw) {
+  if (raw)
+    return bn == 256 ? (pair ? Geo<true, 256, 3>::THREADS : Geo<false, 256, 3>::THREADS)
+                     : (pair ? Geo<true, 128, 3>::THREADS : Geo<false, 128, 3>::THREADS);
   return bn == 256 ? (pair ? Geo<true, 256>::THREADS : Geo<false, 256>::THREADS)
                    : (pair ? Geo<true, 128>::THREADS : Geo<false, 128>::THREADS);
 }
@@ -959,25 +1050,33 @@ size_t tc_smem_bytes(int kind, int64_t N, bool pair, int bn) {
 
 using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const KParams);
 
-template <int TBN>
-Kern pick_kernel(int kind, bool pair, bool bits, bool has_lo) {
-  if (pair) return tc_gemm_kernel<TC_DW, false, true, TBN>;  // use_pair: dW only
+// The instantiations. raw: kRawA / kRawB bits (fp32 operands split in the kernel); bits: the
+// packed ReLU mask (read by dX, written by the fp32 forward); has_lo: the output is a hi/lo
+// pair. 256-column tiles exist for the light epilogues only (tile_n): dW and the fp32
+// forward.
+template <int RAW>
+Kern pick_fwd_dx(int kind, bool bits, bool has_lo, int bn) {
+  if (bn == 256)
+    return bits ? tc_gemm_kernel<kFwdF32, true, false, 256, RAW> : tc_gemm_kernel<kFwdF32, false, false, 256, RAW>;
   switch (kind) {
-    case TC_FWD: return has_lo ? tc_gemm_kernel<TC_FWD, false, false, TBN> : tc_gemm_kernel<kFwdF32, false, false, TBN>;
-    case TC_DX: return bits ? tc_gemm_kernel<TC_DX, true, false, TBN> : tc_gemm_kernel<TC_DX, false, false, TBN>;
-    case TC_DX_F32:
-      return bits ? tc_gemm_kernel<TC_DX_F32, true, false, TBN> : tc_gemm_kernel<TC_DX_F32, false, false, TBN>;
-    default: return tc_gemm_kernel<TC_DW, false, false, TBN>;
+    case TC_FWD:
+      if (has_lo) return tc_gemm_kernel<TC_FWD, false, false, 128, RAW>;
+      return bits ? tc_gemm_kernel<kFwdF32, true, false, 128, RAW> : tc_gemm_kernel<kFwdF32, false, false, 128, RAW>;
+    case TC_DX: return bits ? tc_gemm_kernel<TC_DX, true, false, 128, RAW> : tc_gemm_kernel<TC_DX, false, false, 128, RAW>;
+    default:
+      return bits ? tc_gemm_kernel<TC_DX_F32, true, false, 128, RAW> : tc_gemm_kernel<TC_DX_F32, false, false, 128, RAW>;
   }
 }
 
-// 256-column tiles exist for the light epilogues only (tile_n).
-Kern pick(int kind, bool pair, bool bits, bool has_lo, int bn) {
-  if (bn == 256) {
-    if (pair) return tc_gemm_kernel<TC_DW, false, true, 256>;
-    return kind == TC_DW ? tc_gemm_kernel<TC_DW, false, false, 256> : tc_gemm_kernel<kFwdF32, false, false, 256>;
-  }
-  return pick_kernel<128>(kind, pair, bits, has_lo);
+template <int RAW>
+Kern pick_dw(bool pair, int bn) {
+  if (bn == 256) return pair ? tc_gemm_kernel<TC_DW, false, true, 256, RAW> : tc_gemm_kernel<TC_DW, false, false, 256, RAW>;
+  return tc_gemm_kernel<TC_DW, false, false, 128, RAW>;
+}
+
+Kern pick(int kind, bool pair, bool bits, bool has_lo, int bn, int raw) {
+  if (kind == TC_DW) return raw ? pick_dw<kRawA | kRawB>(pair, bn) : pick_dw<0>(pair, bn);
+  return raw ? pick_fwd_dx<kRawA>(kind, bits, has_lo, bn) : pick_fwd_dx<0>(kind, bits, has_lo, bn);
 }
 
 // Opt an instantiation in to its shared memory once per device (never while a stream is
@@ -1001,7 +1100,7 @@ int opt_in(Kern kern, bool pair, int bn) {
 int pair_slots_query(int bn) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2);
-  cfg.blockDim = dim3(threads_of(true, bn));
+  cfg.blockDim = dim3(threads_of(true, bn, kRawA | kRawB));
   cfg.dynamicSmemBytes = tc_smem_bytes(TC_DX, kMaxColsumN, true, bn);  // the opt-in size of every launch
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1010,7 +1109,7 @@ int pair_slots_query(int bn) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  Kern kern = pick(TC_DW, true, false, true, bn);
+  Kern kern = pick(TC_DW, true, false, true, bn, kRawA | kRawB);  // the learner's dW
   int n = 0;
   if (opt_in(kern, true, bn) != kOk || cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
     (void)cudaGetLastError();
@@ -1076,7 +1175,11 @@ int tc_gemm_grid(const TcGemmArgs& a) {
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   SPO_CHECK_ARG(tc_gemm_supported(a.kind, a.M, a.N, a.K), kErrUnsupported,
                 "tc_gemm: unsupported shape (N % 128, K % 32, dW M % 128)");
-  SPO_CHECK_ARG(a.a_hi && a.a_lo && a.b_hi && a.b_lo, kErrArg, "tc_gemm: null operand");
+  // Operands: a_lo / b_lo null = the operand is plain fp32, split in the kernel. The forward
+  // and dX products take B (the weights) as a pair; dW takes both pairs or both fp32.
+  SPO_CHECK_ARG(a.a_hi && a.b_hi && (a.kind == TC_DW ? (a.a_lo == nullptr) == (a.b_lo == nullptr) : a.b_lo != nullptr),
+                kErrArg, "tc_gemm: null operand (dW: both operands fp32 or both hi/lo pairs; forward and dX: B as a pair)");
+  const int raw = a.a_lo == nullptr ? (a.kind == TC_DW ? kRawA | kRawB : kRawA) : 0;
   if (a.kind == TC_DW)
     SPO_CHECK_ARG(a.k_chunk >= BK && a.k_chunk % BK == 0 && a.c_part, kErrArg,
                   "tc_gemm: dW needs c_part and k_chunk a multiple of 32");
@@ -1100,13 +1203,13 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   if (mn) {  // A [K x M], B [K x N] row-major; boxes 32 wide (MN) x 32 deep (K)
     const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     if ((rc = make_map(&m_ah, a.a_hi, a.M, a.K, 32, BK, sw))) return rc;
-    if ((rc = make_map(&m_al, a.a_lo, a.M, a.K, 32, BK, sw))) return rc;
+    if ((rc = make_map(&m_al, a.a_lo ? a.a_lo : a.a_hi, a.M, a.K, 32, BK, sw))) return rc;
     if ((rc = make_map(&m_bh, a.b_hi, a.N, a.K, 32, BK, sw))) return rc;
-    if ((rc = make_map(&m_bl, a.b_lo, a.N, a.K, 32, BK, sw))) return rc;
+    if ((rc = make_map(&m_bl, a.b_lo ? a.b_lo : a.b_hi, a.N, a.K, 32, BK, sw))) return rc;
   } else {   // A [M x K], B [N x K] row-major; boxes 32 deep (K) x 128 (A) / b_rows (B) rows
     const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
     if ((rc = make_map(&m_ah, a.a_hi, a.K, a.M, BK, BM, sw))) return rc;
-    if ((rc = make_map(&m_al, a.a_lo, a.K, a.M, BK, BM, sw))) return rc;
+    if ((rc = make_map(&m_al, a.a_lo ? a.a_lo : a.a_hi, a.K, a.M, BK, BM, sw))) return rc;
     if ((rc = make_map(&m_bh, a.b_hi, a.K, a.N, BK, b_rows, sw))) return rc;
     if ((rc = make_map(&m_bl, a.b_lo, a.K, a.N, BK, b_rows, sw))) return rc;
   }
@@ -1129,13 +1232,14 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.colsum = a.colsum;
   P.err = a.err;
   P.mask_bits = a.kind == TC_DX || a.kind == TC_DX_F32 ? a.mask_bits : nullptr;
-  P.c_bits = a.kind == TC_FWD && a.c_lo ? a.c_bits : nullptr;
+  P.c_bits = a.kind == TC_FWD ? a.c_bits : nullptr;
   P.wait_ns = a.wait_ns > 0 ? a.wait_ns : kWaitNs;
   P.withhold = a.withhold;
   const int grid = tc_gemm_grid(a);
   const size_t smem = tc_smem_bytes(a.kind, a.N, pair, bn);
-  const int threads = threads_of(pair, bn);
-  const Kern kern = pick(a.kind, pair, P.mask_bits != nullptr, a.c_lo != nullptr, bn);
+  const int threads = threads_of(pair, bn, raw);
+  const bool bits = a.kind == TC_FWD ? P.c_bits != nullptr : P.mask_bits != nullptr;
+  const Kern kern = pick(a.kind, pair, bits, a.c_lo != nullptr, bn, raw);
   if ((rc = opt_in(kern, pair, bn))) return rc;
   SPO_CUDA_TRY(launch_pdl(kern, dim3((unsigned)grid), dim3(threads), smem, s, pair ? 2u : 0u, m_ah, m_al, m_bh,
                           m_bl, P));

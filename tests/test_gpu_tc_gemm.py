@@ -206,6 +206,87 @@ def test_dw_split_partials(rows, Kin, N, chunk):
     assert rel_err(got, want) <= 1e-5
 
 
+@pytest.mark.parametrize("M,K,N", [(1000, 256, 256), (4096, 512, 512), (300, 1024, 1024), (777, 32, 128)])
+def test_forward_plain_fp32_operand_equals_presplit(M, K, N):
+    """A given as plain fp32 (a_lo NULL: split in shared memory by the kernel) and the
+    output written as plain fp32 with its packed ReLU mask: bit-identical to the same
+    product from A split beforehand by spo_split_tf32, and within 1e-5 of float64."""
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(11 * M + K)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    if K > 32:
+        x = x.relu_()
+    w = torch.randn(K, N, device="cuda", generator=g) / K ** 0.5
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+    xh, xl = split(x)
+    wth, wtl = split(w.t().contiguous())
+    outs = []
+    for raw in (True, False):
+        y = torch.full((M, N), float("nan"), device="cuda")
+        bits = torch.full((M + 1, N // 32), -1, dtype=torch.int32, device="cuda")  # + a guard row
+        d = f.TcGemmDesc(kind=f.TC_FWD, a_hi=(x if raw else xh).data_ptr(), a_lo=None if raw else xl.data_ptr(),
+                         b_hi=wth.data_ptr(), b_lo=wtl.data_ptr(), m=M, n=N, k=K, bias=b.data_ptr(),
+                         c_hi=y.data_ptr(), c_bits=bits.data_ptr())
+        run(d)
+        outs.append((y.cpu(), bits.cpu().numpy().view(np.uint32)))
+    (y1, b1), (y0, b0) = outs
+    assert torch.equal(y1, y0) and np.array_equal(b1, b0)
+    want = np.maximum(x.double().cpu().numpy() @ w.double().cpu().numpy() + b.double().cpu().numpy(), 0)
+    assert rel_err(y1.numpy(), want) <= 1e-5
+    assert np.array_equal(b1[:M], pack_mask(y1.numpy() > 0)) and np.all(b1[M] == 0xFFFFFFFF)
+
+
+@pytest.mark.parametrize("M,Kout,Nin", [(1000, 512, 512), (2048, 1024, 512), (129, 128, 256)])
+def test_dx_plain_fp32_operand_equals_presplit(M, Kout, Nin):
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(M + 5 * Kout + Nin)
+    dy = torch.randn(M, Kout, device="cuda", generator=g) * 1e-3
+    w = torch.randn(Nin, Kout, device="cuda", generator=g) / Kout ** 0.5
+    act = torch.randn(M, Nin, device="cuda", generator=g).relu_()
+    bits = torch.from_numpy(pack_mask(act.cpu().numpy() > 0).view(np.int32)).cuda()
+    dyh, dyl = split(dy)
+    wh, wl = split(w)
+    outs = []
+    for raw in (True, False):
+        out = torch.full((M, Nin), float("nan"), device="cuda")
+        desc = f.TcGemmDesc(kind=f.TC_DX_F32, a_hi=(dy if raw else dyh).data_ptr(),
+                            a_lo=None if raw else dyl.data_ptr(), b_hi=wh.data_ptr(), b_lo=wl.data_ptr(),
+                            m=M, n=Nin, k=Kout, mask_bits=bits.data_ptr(), c_hi=out.data_ptr())
+        grid = ctypes.c_int32()
+        f.call("spo_tc_gemm_shape", ctypes.byref(desc), ctypes.byref(grid), None)
+        cs = torch.full((grid.value, Nin), float("nan"), device="cuda")
+        desc.colsum = cs.data_ptr()
+        run(desc)
+        outs.append((out.cpu(), cs.cpu()))
+    (o1, c1), (o0, c0) = outs
+    assert torch.equal(o1, o0) and torch.equal(c1, c0)
+    want = (dy.double() @ w.double().t()).cpu().numpy() * (act.cpu().numpy() > 0)
+    assert rel_err(o1.numpy(), want) <= 1e-5
+
+
+@pytest.mark.parametrize("rows,Kin,N,chunk", [(4096, 512, 512, 1024), (1000, 128, 128, 256),
+                                               (65536, 256, 256, 4096), (777, 1024, 1024, 224)])
+def test_dw_plain_fp32_operands_equal_presplit(rows, Kin, N, chunk):
+    f = ffi()
+    g = torch.Generator(device="cuda").manual_seed(3 * rows + Kin)
+    act = torch.randn(rows, Kin, device="cuda", generator=g).relu_()
+    dz = torch.randn(rows, N, device="cuda", generator=g) * 1e-4
+    ah, al = split(act)
+    zh, zl = split(dz)
+    splits = -(-rows // chunk)
+    parts = []
+    for raw in (True, False):
+        part = torch.full((splits, Kin, N), float("nan"), device="cuda")
+        d = f.TcGemmDesc(kind=f.TC_DW, a_hi=(act if raw else ah).data_ptr(), a_lo=None if raw else al.data_ptr(),
+                         b_hi=(dz if raw else zh).data_ptr(), b_lo=None if raw else zl.data_ptr(),
+                         m=Kin, n=N, k=rows, k_chunk=chunk, c_part=part.data_ptr())
+        run(d)
+        parts.append(part.cpu())
+    assert torch.equal(parts[0], parts[1])
+    want = act.double().t().cpu().numpy() @ dz.double().cpu().numpy()
+    assert rel_err(parts[0].double().sum(0).numpy(), want) <= 1e-5
+
+
 def test_unsupported_shapes_are_rejected():
     f = ffi()
     d = f.TcGemmDesc(kind=f.TC_FWD, m=128, n=96, k=128)  # n not a multiple of 128
@@ -240,7 +321,7 @@ def test_bounded_wait_runs_out_and_the_device_recovers():
     torch.cuda.synchronize()
     assert time.time() - t0 < 10.0
     code = int(err.item())
-    assert code in (1, 2, 3, 4), code     # a wait gave up (which role first is a race)
+    assert code in (1, 2, 3, 4, 5), code  # a wait gave up (which role first is a race)
     with pytest.raises(f.SpoError, match="needs desc->err"):
         f.call("spo_tc_gemm_withheld", None, ctypes.byref(f.TcGemmDesc(
             kind=f.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wth.data_ptr(), b_lo=wtl.data_ptr(),
