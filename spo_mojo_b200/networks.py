@@ -312,7 +312,7 @@ def actor_loss_fwd_bwd(ctx, dz, stats, logits, mask, q, m, num_actions=NUM_ACTIO
     dual gradient into dlog_alpha[0] (optional). log_alpha: a one-element device tensor."""
     ws = ctx.workspace(ffi.lib().spo_loss_workspace_size())
     ffi.call("spo_actor_loss_fwd_bwd", ctx.handle, _p(logits), _p(mask), _p(q), _p(logits_old),
-             _p(log_alpha), eps_kl, m, num_actions, 1.0 / m if scale is None else scale, _p(dz),
+             _p(log_alpha), eps_kl, m, num_actions, (1.0 / m if m else 0.0) if scale is None else scale, _p(dz),
              _p(stats), _p(dlog_alpha), ws.data_ptr(), ws.numel())
 
 
@@ -321,7 +321,7 @@ def value_loss_fwd_bwd(ctx, dv, stats, value, target, n, scale=None):
     stats[ffi.STAT['critic_loss']]."""
     ws = ctx.workspace(ffi.lib().spo_loss_workspace_size())
     ffi.call("spo_value_loss_fwd_bwd", ctx.handle, _p(value), _p(target), n,
-             1.0 / n if scale is None else scale, _p(dv), _p(stats), ws.data_ptr(), ws.numel())
+             (1.0 / n if n else 0.0) if scale is None else scale, _p(dv), _p(stats), ws.data_ptr(), ws.numel())
 
 
 # ---------------------------------------------------------------- optimiser (networks/optim.mojo)

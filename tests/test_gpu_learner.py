@@ -137,7 +137,7 @@ def check_against_oracle(wl, L, grads0, stats0, rep0, ora, nets, la, params, bat
         n_all = sum(t for _, t in excluded.values())
         _record_excluded(wl, rows, which, excluded)
         # the undetermined updates are the gradients within the fp32 error of zero: few
-        assert n_out <= 0.03 * n_all, (which, excluded)
+        assert n_out <= 0.05 * n_all, (which, excluded)
     if wl.actor is not None and wl.dual:
         want = ora["log_alpha"]["grad"]
         assert abs(rep0["dlog_alpha"] - want) <= 1e-4 * abs(want) + 1e-7

@@ -65,6 +65,8 @@ def test_noalloc_matches_workspace_entry_on_consecutive_calls(m, k, n, with_dx):
         got = _run("spo_linear_bwd_noalloc", x, w, dy, relu_src, m, k, n, with_dx)
         outs = zip(("dW", "db", "dx"), got, want, (_tol(m), _tol(m), _tol(n)))
         for name, a, b, tol in list(outs)[:3 if with_dx else 2]:
+            if a.numel() == 0:     # dx of zero rows
+                continue
             assert torch.isfinite(a).all(), f"call {call}: {name} not fully written"
             assert float((a - b).abs().max()) <= tol, f"call {call}: {name}"
         if m == 0:  # no rows: the gradients of the weights are zero
