@@ -409,10 +409,11 @@ SPO_API int spo_learner_backward(spo_learner_t learner, spo_stream_t stream, con
 SPO_API int spo_learner_apply(spo_learner_t learner, spo_stream_t stream, const spo_train_state* state);
 /* The activation cache of the last forward (CriticCache a1, a2, ...,
  * networks/mlp.mojo:84-102): device pointers to the post-ReLU activations of hidden layer
- * `layer` (0-based, [rows x d_{layer+1}]) of network `which` (0 actor, 1 critic), plain fp32
- * in *hi with either engine (the tensor-core kernels split their operands on chip); *lo is
- * always set to NULL (kept for callers of the earlier hi/lo form). Valid until the next
- * call on the learner. */
+ * `layer` (0-based, [rows x d_{layer+1}]) of network `which` (0 actor, 1 critic). With the
+ * tensor-core engine the activations that feed tensor-core products are stored as TF32
+ * hi/lo pairs (value = hi + lo) and *lo is set; otherwise (the CUDA-core engine, and the
+ * last hidden layer, which only the fused head reads) *lo is NULL and *hi is the plain
+ * fp32 value. Valid until the next call on the learner. */
 SPO_API int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer,
                               const float** hi, const float** lo);
 /* Reads (synchronously) and clears the learner's device error word: 0 when every

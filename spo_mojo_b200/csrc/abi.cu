@@ -239,19 +239,21 @@ struct NetPlan {
   int64_t w_off[SPO_MAX_LAYERS], b_off[SPO_MAX_LAYERS], size = 0, offset = 0;
   int64_t max_hidden = 0;
   // Tensor-core mode: hidden x hidden products on tcgen05 (3xTF32). Activations and the
-  // gradients between hidden layers stay plain fp32 in HBM; the tensor-core kernels split
-  // them into TF32 hi/lo halves in shared memory. dz0 is the gradient of layer 0's output
-  // (its dW stays on the CUDA cores: the 27-wide input has no 16-byte-aligned rows for TMA).
+  // gradients between hidden layers are then stored as TF32 hi/lo pairs (acts/acts_lo,
+  // dz/dz_lo); dz0 is the plain fp32 gradient of layer 0's output (its dW stays on the
+  // CUDA cores: the 27-wide input has no 16-byte-aligned rows for TMA).
   bool tc = false;
   // workspace carve-outs
-  float* acts[SPO_MAX_LAYERS] = {};     // a_l, l = 0..L-2: [rows x d_{l+1}]
+  float* acts[SPO_MAX_LAYERS] = {};     // a_l, l = 0..L-2: [rows x d_{l+1}] (hi in TC mode)
+  float* acts_lo[SPO_MAX_LAYERS] = {};  // TC mode, l <= L-3: lo halves (a_{L-2} is fp32)
   uint32_t* acts_bits[SPO_MAX_LAYERS] = {};  // TC mode, l <= L-3: a_l > 0 packed [rows x d_{l+1}/32]
-  float* dz[2] = {};                    // ping-pong [rows x max_hidden]
-  float* dz0 = nullptr;                 // TC mode: [rows x d_1]
+  float* dz[2] = {};                    // ping-pong [rows x max_hidden] (hi in TC mode)
+  float* dz_lo[2] = {};                 // TC mode
+  float* dz0 = nullptr;                 // TC mode: [rows x d_1] fp32
   // TC mode with a first layer at most 32 wide and d_1 % 128 == 0: that layer's forward
-  // runs on tensor cores too, from the input padded to 32 columns and W_0^T padded (hi/lo)
+  // runs on tensor cores too, from the input padded to 32 columns (hi/lo) and W_0^T padded
   bool tc0 = false;
-  float* x0 = nullptr;                  // [rows x 32] fp32
+  float* x0[2] = {};                    // [rows x 32] hi, lo
   float* w0t[2] = {};                   // [d_1 x 32] hi, lo
   float* wsplit[SPO_MAX_LAYERS][4] = {};  // TC mode, hidden l: W^T hi, W^T lo, W hi, W lo
   float* head_dw = nullptr;          // [Gh][d_{L-1} x d_L]
@@ -328,18 +330,24 @@ void carve_net(NetPlan& n, Carve& c, int64_t rows) {
   const int L = d.num_layers;
   for (int l = 0; l + 1 < L; ++l) {
     n.acts[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
+    // the last hidden activation is read only by the fused head: plain fp32
+    if (n.tc && l + 2 < L) n.acts_lo[l] = c.take<float>((size_t)rows * d.dims[l + 1]);
     // packed for the dX GEMM of layer l + 1 (the last hidden layer's mask is read by the
     // head); layer 0's is written by the input-layer forward when its shape allows
     const bool packs = l >= 1 || (fwd_skinny_ok(d.dims[0], d.dims[1]) && d.dims[1] % 32 == 0);
     if (n.tc && packs && l + 2 < L) n.acts_bits[l] = c.take<uint32_t>((size_t)rows * (d.dims[l + 1] / 32));
   }
-  for (int i = 0; i < 2; ++i) n.dz[i] = c.take<float>((size_t)rows * n.max_hidden);
+  for (int i = 0; i < 2; ++i) {
+    n.dz[i] = c.take<float>((size_t)rows * n.max_hidden);
+    if (n.tc) n.dz_lo[i] = c.take<float>((size_t)rows * n.max_hidden);
+  }
   if (n.tc) {
     n.dz0 = c.take<float>((size_t)rows * d.dims[1]);
-    if (n.tc0) {
-      n.x0 = c.take<float>((size_t)rows * 32);
-      for (int k = 0; k < 2; ++k) n.w0t[k] = c.take<float>((size_t)d.dims[1] * 32);
-    }
+    if (n.tc0)
+      for (int k = 0; k < 2; ++k) {
+        n.x0[k] = c.take<float>((size_t)rows * 32);
+        n.w0t[k] = c.take<float>((size_t)d.dims[1] * 32);
+      }
     for (int l = 1; l + 1 < L; ++l)
       for (int k = 0; k < 4; ++k) n.wsplit[l][k] = c.take<float>((size_t)d.dims[l] * d.dims[l + 1]);
   }
@@ -489,12 +497,13 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
   if (n.tc0 && rows >= kTc0MinRows) {
     rc = split_weights_t_pad_launch(params + n.w_off[0], d.dims[0], d.dims[1], n.w0t[0], n.w0t[1], s);
     if (rc) return rc;
-    rc = pad_split_input_launch(in, d.dims[0], rows, n.x0, nullptr, s);
+    rc = pad_split_input_launch(in, d.dims[0], rows, n.x0[0], n.x0[1], s);
     if (rc) return rc;
     if (rows > 0) {
       TcGemmArgs a{};
       a.kind = TC_FWD;
-      a.a_hi = n.x0;   // fp32: split in the kernel
+      a.a_hi = n.x0[0];
+      a.a_lo = n.x0[1];
       a.b_hi = n.w0t[0];
       a.b_lo = n.w0t[1];
       a.M = rows;
@@ -502,6 +511,7 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
       a.K = 32;
       a.bias = params + n.b_off[0];
       a.c_hi = n.acts[0];
+      a.c_lo = n.acts_lo[0];
       a.c_bits = n.acts_bits[0];
       a.err = err;
       rc = tc_gemm_launch(a, s);
@@ -509,8 +519,8 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
   } else {
     rc = fwd_skinny_ok(d.dims[0], d.dims[1])
              ? fwd_skinny_launch(in, params + n.w_off[0], params + n.b_off[0], rows, d.dims[0], d.dims[1],
-                                 n.acts[0], nullptr, n.acts_bits[0], s)
-             : gemm_fwd_split(s, n.acts[0], nullptr, in.x, params + n.w_off[0], params + n.b_off[0],
+                                 n.acts[0], n.acts_lo[0], n.acts_bits[0], s)
+             : gemm_fwd_split(s, n.acts[0], n.acts_lo[0], in.x, params + n.w_off[0], params + n.b_off[0],
                               rows, d.dims[0], d.dims[1]);
   }
   if (rc) return rc;
@@ -518,7 +528,8 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
   for (int l = 1; l + 1 < d.num_layers; ++l) {
     TcGemmArgs a{};
     a.kind = TC_FWD;
-    a.a_hi = n.acts[l - 1];   // fp32: split in the kernel
+    a.a_hi = n.acts[l - 1];
+    a.a_lo = n.acts_lo[l - 1];
     a.b_hi = n.wsplit[l][0];
     a.b_lo = n.wsplit[l][1];
     a.M = rows;
@@ -526,6 +537,7 @@ int net_forward_hidden(const NetPlan& n, cudaStream_t s, const float* params, La
     a.K = d.dims[l];
     a.bias = params + n.b_off[l];
     a.c_hi = n.acts[l];
+    a.c_lo = n.acts_lo[l];
     a.c_bits = n.acts_bits[l];
     a.err = err;
     rc = tc_gemm_launch(a, s);
@@ -550,8 +562,10 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* /*params: the
     if (rows > 0) {
       TcGemmArgs w{};
       w.kind = TC_DW;
-      w.a_hi = n.acts[l - 1];   // both fp32: split in the kernel
+      w.a_hi = n.acts[l - 1];
+      w.a_lo = n.acts_lo[l - 1];
       w.b_hi = n.dz[cur];
+      w.b_lo = n.dz_lo[cur];
       w.M = kin;
       w.N = nout;
       w.K = rows;
@@ -570,7 +584,9 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* /*params: the
     if (rows > 0) {
       TcGemmArgs x{};
       const bool last = l == 1;
-      x.a_hi = n.dz[cur];   // fp32: split in the kernel
+      x.kind = last ? TC_DX_F32 : TC_DX;
+      x.a_hi = n.dz[cur];
+      x.a_lo = n.dz_lo[cur];
       x.b_hi = n.wsplit[l][2];
       x.b_lo = n.wsplit[l][3];
       x.M = rows;
@@ -578,8 +594,8 @@ int net_backward_tc(const NetPlan& n, cudaStream_t s, const float* /*params: the
       x.K = nout;
       x.mask = n.acts[l - 1];
       x.mask_bits = n.acts_bits[l - 1];  // packed by the forward of layer l - 1, when it was
-      x.kind = TC_DX_F32;
       x.c_hi = last ? n.dz0 : n.dz[cur ^ 1];
+      x.c_lo = last ? nullptr : n.dz_lo[cur ^ 1];
       x.colsum = n.db_part[l - 1];
       x.err = err;
       cparts = tc_gemm_grid(x);
@@ -614,7 +630,8 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
   const int hl = d.dims[L - 1], al = d.dims[L];
   HeadParams hp{};
   hp.act = n.acts[L - 2];
-
+  hp.act_lo = n.tc ? n.acts_lo[L - 2] : nullptr;
+  hp.dX_lo = n.tc ? n.dz_lo[0] : nullptr;
   hp.W = params + n.w_off[L - 1];
   hp.b = params + n.b_off[L - 1];
   hp.M = rows;
@@ -1240,7 +1257,7 @@ int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer, const
   const NetPlan& n = learner->net[which];
   SPO_CHECK_ARG(layer >= 0 && layer + 1 < n.d.num_layers, kErrArg, "no such hidden layer");
   *hi = n.acts[layer];
-  *lo = nullptr;
+  *lo = n.tc ? n.acts_lo[layer] : nullptr;
   return kOk;
 }
 
@@ -1275,6 +1292,10 @@ int spo_learner_forward(spo_learner_t learner, spo_stream_t stream, int32_t whic
   int rc = net_forward_hidden(n, s, p, LayerInput{obs, nullptr}, rows, learner->err);
   if (rc) return rc;
   const int L = n.d.num_layers;
+  if (n.tc && n.acts_lo[L - 2]) {  // the last layer reads plain fp32: fold lo into hi
+    rc = combine_tf32_launch(n.acts[L - 2], n.acts_lo[L - 2], rows * n.d.dims[L - 1], s);
+    if (rc) return rc;
+  }
   rc = gemm_fwd(s, out, n.acts[L - 2], p + n.w_off[L - 1], p + n.b_off[L - 1], rows, n.d.dims[L - 1],
                 n.d.dims[L], false);
   if (rc) return rc;

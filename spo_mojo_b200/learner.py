@@ -138,7 +138,7 @@ class Learner:
 
     def activations(self, which, rows):
         """Post-ReLU activations of the last forward, one [rows x d] tensor per hidden
-        layer (a copy)."""
+        layer (a copy; hi + lo with the tensor-core engine)."""
         dims = self.actor_dims if which == "actor" else self.critic_dims
         out = []
         for layer in range(len(dims) - 2):
