@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -40,12 +41,15 @@ constexpr uint32_t A_TILE = BM * BK * 4;                 // 16 KB
 constexpr int STAGES_MAX = 4;
 constexpr int NACC_MAX = 4;
 constexpr uint32_t TMEM_COLS = 512;                      // the whole TMEM of the SM
-constexpr int kConvWarps = 2;                            // operand-split warps (fp32 operands)
+constexpr int ASTG_MAX = 4;
 
-// Operands held in global memory as plain fp32 ("raw") instead of TF32 hi/lo pairs: the
-// producer loads them into the hi slot of a stage and the split warps write hi (in place)
-// and lo before the MMAs read the stage. RAW bit 0: A, bit 1: B.
+// Operands held in global memory as plain fp32 ("raw") instead of TF32 hi/lo pairs, split
+// on chip by four split warps (one per TMEM lane quadrant). RAW bit 0: A, whose hi and lo
+// halves the split warps write to tensor memory (tcgen05.st), from where the MMAs read A
+// (no shared-memory traffic for A beyond the one read of the fp32 tile); bit 1: B (dW),
+// split in shared memory (hi in place, lo in the stage's lo slot).
 constexpr int kRawA = 1, kRawB = 2;
+constexpr int kSplitWarps = 4;
 
 // Geometry of one instantiation: PAIR = CTA pair (cta_group::2), TBN = output columns per
 // tile (128, or 256 when N allows: one 128 x 256 MMA per k-step reads A once for twice the
@@ -60,16 +64,23 @@ struct Geo {
   static constexpr int BN = TBN;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
   static constexpr uint32_t B_TILE = B_ROWS * BK * 4;
-  static constexpr uint32_t STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
+  // A from tensor memory: a stage holds the fp32 A tile only (no lo slot)
+  static constexpr bool TA = (RAW & kRawA) != 0;
+  static constexpr uint32_t A_BYTES = TA ? A_TILE : 2 * A_TILE;   // A slots of a stage
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + 2 * B_TILE;
   static constexpr int STAGES = (200u * 1024u) / STAGE_BYTES < (uint32_t)STAGES_MAX
                                     ? (int)((200u * 1024u) / STAGE_BYTES)
                                     : STAGES_MAX;
   static constexpr int UNIT_M = PAIR ? 2 * BM : BM;                // output rows per unit
-  static constexpr int NACC = (int)(TMEM_COLS / BN);
+  // TMEM columns: accumulators first, then (A in TMEM) ASTG stages of A, 64 columns each
+  // (32 hi, 32 lo): 2 x 128 + 4 x 64, or 1 x 256 + 4 x 64. Four A stages let the split
+  // warps run up to three k-blocks ahead of the MMAs.
+  static constexpr int NACC = TA ? (BN == 128 ? 2 : 1) : (int)(TMEM_COLS / BN);
+  static constexpr int ASTG = TA ? (int)((TMEM_COLS - NACC * BN) / 64) : 0;
+  static constexpr uint32_t ACOL0 = (uint32_t)(NACC * BN);
   static constexpr int EPI_WARPS = 4 * (BN / EPI_COLS);
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-  // fp32 operands are split into their hi/lo halves in shared memory by these warps
-  static constexpr int CONV_WARPS = RAW != 0 ? kConvWarps : 0;
+  static constexpr int CONV_WARPS = RAW != 0 ? kSplitWarps : 0;
   static constexpr int THREADS = 64 + EPI_THREADS + 32 * CONV_WARPS;
 };
 // The tensor core's accumulation into TMEM is not exact fp32: its error grows with the
@@ -104,13 +115,15 @@ constexpr uint64_t kWaitNs = 2000000000ull;              // 2 s: the limit of ev
 constexpr int kMaxColsumN = 1024;
 
 enum WaitCode : int {
-  kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, kErrWaitTFull = 4, kErrWaitLoaded = 5
+  kErrWaitEmpty = 1, kErrWaitFull = 2, kErrWaitTEmpty = 3, kErrWaitTFull = 4, kErrWaitLoaded = 5,
+  kErrWaitAEmpty = 6
 };
 
 struct __align__(64) Ctl {
   uint64_t full[STAGES_MAX];     // operands ready for the MMAs
   uint64_t empty[STAGES_MAX];    // stage consumed by the MMAs
   uint64_t loaded[STAGES_MAX];   // raw operands: the stage's copies have landed
+  uint64_t aempty[ASTG_MAX];     // A in TMEM: the stage's MMAs are done with it
   uint64_t tfull[NACC_MAX];
   uint64_t tempty[NACC_MAX];
   uint64_t drain;
@@ -236,6 +249,43 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64
       "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+
+// The same MMA with A read from tensor memory (a_tmem: lane 0, first column of the 8 K
+// columns of this k-step; row i of A in lane i).
+__device__ __forceinline__ void mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_tf32_ta_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// tcgen05.st.32x32b.x16: thread t of the warp writes 16 consecutive 32-bit columns of TMEM
+// lane (quadrant base + t), starting at the column of taddr.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -405,6 +455,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
   constexpr int STAGES = G::STAGES;
   constexpr uint32_t STAGE_BYTES = G::STAGE_BYTES;
   constexpr uint32_t B_TILE = G::B_TILE;
+  constexpr bool TA = G::TA;                   // A from tensor memory
+  constexpr int ASTG = G::ASTG;
+  constexpr uint32_t B_OFF = G::A_BYTES;       // B's offset in a stage
+  constexpr bool AMN = KIND == TC_DW;          // A (and B) MN-major: dW
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -432,6 +486,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       mbar_init(smem_u32(&ctl->tfull[a]), 1);
       mbar_init(smem_u32(&ctl->tempty[a]), PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
+    for (int j = 0; j < ASTG; ++j) mbar_init(smem_u32(&ctl->aempty[j]), 1);
     mbar_init(smem_u32(&ctl->drain), 1);
     ctl->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -499,9 +554,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
         };
         const int32_t k0 = (int32_t)(kbeg + (int64_t)kb * BK);
         const uint32_t a_hi = smem0 + s * STAGE_BYTES, a_lo = a_hi + A_TILE;
-        const uint32_t b_hi = a_hi + 2 * A_TILE, b_lo = b_hi + B_TILE;
+        const uint32_t b_hi = a_hi + B_OFF, b_lo = b_hi + B_TILE;
         constexpr bool ra = (RAW & kRawA) != 0, rb = (RAW & kRawB) != 0;
-        if (P.a_mn) {
+        if (TA && AMN) {
+          load(a_hi, &tm_ah, m0, k0);   // one unswizzled [32 k][128 m] box
+        } else if (P.a_mn) {
 #pragma unroll
           for (int j = 0; j < BM / 32; ++j) {
             load(a_hi + j * 4096, &tm_ah, m0 + 32 * j, k0);
@@ -552,7 +609,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
       // descriptor of another stage, half or k-step is the same high word and a low word
       // plus ((byte offset) >> 4): one add per descriptor in the loop.
       const uint64_t da0 = make_desc(smem0, lbo, sbo, lay);
-      const uint64_t db0 = make_desc(smem0 + 2 * A_TILE, lbo, sbo, lay);
+      const uint64_t db0 = make_desc(smem0 + B_OFF, lbo, sbo, lay);
+      // A from tensor memory is read in rows (lane = row of A): K-major whatever its layout in
+      // global memory
+      constexpr uint32_t idesc_ta = idesc & ~(1u << 15);
       const uint32_t da_lo = (uint32_t)da0, db_lo = (uint32_t)db0;
       const uint64_t d_hi = da0 & 0xFFFFFFFF00000000ull;  // equal for A and B
       // Each unit's k-range is cut into segments of at most SEG k-blocks; every segment
@@ -590,7 +650,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
               const uint64_t adh = d_hi | ah, adl = d_hi | (ah + (A_TILE >> 4));
               const uint64_t bdh = d_hi | bh, bdl = d_hi | (bh + (B_TILE >> 4));
               const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
-              if constexpr (PAIR) {
+              if constexpr (TA) {
+                const uint32_t th = tmem_base + G::ACOL0 + (it % ASTG) * 64 + 8 * ks, tl = th + 32;
+                if constexpr (PAIR) {
+                  mma_tf32_ta_pair(d, tl, bdh, idesc_ta, accum);
+                  mma_tf32_ta_pair(d, th, bdl, idesc_ta, 1u);
+                  mma_tf32_ta_pair(d, th, bdh, idesc_ta, 1u);
+                } else {
+                  mma_tf32_ta(d, tl, bdh, idesc_ta, accum);
+                  mma_tf32_ta(d, th, bdl, idesc_ta, 1u);
+                  mma_tf32_ta(d, th, bdh, idesc_ta, 1u);
+                }
+              } else if constexpr (PAIR) {
                 mma_tf32_pair(d, adl, bdh, idesc, accum);
                 mma_tf32_pair(d, adh, bdl, idesc, 1u);
                 mma_tf32_pair(d, adh, bdh, idesc, 1u);
@@ -604,6 +675,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
               mma_commit_pair(smem_u32(&ctl->empty[s]));
             else
               mma_commit(smem_u32(&ctl->empty[s]));
+            if constexpr (TA) {   // the A stage in TMEM is free once these MMAs complete
+              if constexpr (PAIR)
+                mma_commit_pair(smem_u32(&ctl->aempty[it % ASTG]));
+              else
+                mma_commit(smem_u32(&ctl->aempty[it % ASTG]));
+            }
           }
           if (!ok) break;
           if constexpr (PAIR)
@@ -622,11 +699,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
     }
   } else if (RAW && warp >= 2 + kEpiWarps) {
     // ------------------------------------------------ operand split
-    // The raw (fp32) operand tiles of each stage become TF32 hi/lo pairs in place: hi
-    // overwrites the fp32 value, lo goes to the stage's lo slot at the same offset (the
-    // split is elementwise, so the TMA swizzle of the tile carries over to both halves).
-    // Then the writes are made visible to the tensor core (async proxy) and the stage is
-    // handed to the MMA issuer, in the first CTA of a pair.
+    // Four warps, one per TMEM lane quadrant; thread t of the warp for quadrant q owns row
+    // r = 32 q + t of A. Per k-block: the fp32 A row (32 k values) is read from the stage,
+    // split into TF32 hi/lo and written to TMEM lane r, columns [hi 0..31 | lo 32..63] of
+    // A stage it % ASTG (after the MMAs of that stage's previous use completed). A raw B
+    // (dW) is split in shared memory by all four warps (hi in place, lo in the lo slot).
+    // Then the stage is handed to the MMA issuer (in the first CTA of a pair).
+    const int q = warp & 3;
+    const int row = 32 * q + lane;
+    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
     const int ct = (warp - 2 - kEpiWarps) * 32 + lane;
     constexpr int kCT = 32 * G::CONV_WARPS;
     const uint32_t full0 = smem_u32(&ctl->full[0]);
@@ -645,12 +726,47 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant_
           break;
         }
         uint8_t* st = smem + s * STAGE_BYTES;
-        if constexpr ((RAW & kRawA) != 0)
-          split_tile(reinterpret_cast<float4*>(st), reinterpret_cast<float4*>(st + A_TILE), A_TILE / 16, ct, kCT);
+        if constexpr (TA) {
+          const uint32_t j = it % ASTG;
+          if (!mbar_wait(smem_u32(&ctl->aempty[j]), ((it / ASTG) & 1) ^ 1, abort_flag, P.err, kErrWaitAEmpty,
+                         P.wait_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ta = tmem_base + lane_addr + G::ACOL0 + j * 64;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float v[16], lo[16];
+            if constexpr (!AMN) {
+              // K-major 128-byte-swizzled rows: 16-byte chunk c of row r sits at c ^ (r % 8)
+              const float4* rp = reinterpret_cast<const float4*>(st + row * 128);
+#pragma unroll
+              for (int c4 = 0; c4 < 4; ++c4) {
+                const float4 x = rp[(4 * h + c4) ^ (row & 7)];
+                v[4 * c4] = x.x;
+                v[4 * c4 + 1] = x.y;
+                v[4 * c4 + 2] = x.z;
+                v[4 * c4 + 3] = x.w;
+              }
+            } else {
+              // MN-major, unswizzled [32 k][128 m]
+              const float* cp = reinterpret_cast<const float*>(st) + row;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = cp[(16 * h + i) * 128];
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) tf32_split(v[i], v[i], lo[i]);
+            tmem_st16(ta + 16 * h, v);
+            tmem_st16(ta + 32 + 16 * h, lo);
+          }
+        }
         if constexpr ((RAW & kRawB) != 0)
-          split_tile(reinterpret_cast<float4*>(st + 2 * A_TILE), reinterpret_cast<float4*>(st + 2 * A_TILE + B_TILE),
+          split_tile(reinterpret_cast<float4*>(st + B_OFF), reinterpret_cast<float4*>(st + B_OFF + B_TILE),
                      B_TILE / 16, ct, kCT);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if constexpr (TA) tmem_wait_st();
+        if constexpr ((RAW & kRawB) != 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           if (PAIR && !leader)
@@ -1024,7 +1140,12 @@ int tile_n(int kind, bool fp32_fwd, int64_t N) {
   const bool light = kind == TC_DW || (kind == TC_FWD && fp32_fwd);
   return (SPO_TC_BN256 != 0 && light && N % 256 == 0) ? 256 : 128;
 }
-int tile_of(const TcGemmArgs& a) { return tile_n(a.kind, a.c_lo == nullptr, a.N); }
+// A plain fp32 A (split into tensor memory) takes 128-column tiles in the forward and dX:
+// two 128-column accumulators and four A stages fill the 512 TMEM columns.
+int tile_of(const TcGemmArgs& a) {
+  if (a.a_lo == nullptr && a.kind != TC_DW) return 128;
+  return tile_n(a.kind, a.c_lo == nullptr, a.N);
+}
 
 int threads_of(bool pair, int bn, int raw) {
   if (raw)
@@ -1034,16 +1155,22 @@ int threads_of(bool pair, int bn, int raw) {
                    : (pair ? Geo<true, 128>::THREADS : Geo<false, 128>::THREADS);
 }
 
-size_t ring_bytes(bool pair, int bn) {
-  if (bn == 256)
-    return pair ? (size_t)Geo<true, 256>::STAGES * Geo<true, 256>::STAGE_BYTES
-                : (size_t)Geo<false, 256>::STAGES * Geo<false, 256>::STAGE_BYTES;
-  return pair ? (size_t)Geo<true, 128>::STAGES * Geo<true, 128>::STAGE_BYTES
-              : (size_t)Geo<false, 128>::STAGES * Geo<false, 128>::STAGE_BYTES;
+template <bool PAIR, int BN, int RAW>
+constexpr size_t ring_of() { return (size_t)Geo<PAIR, BN, RAW>::STAGES * Geo<PAIR, BN, RAW>::STAGE_BYTES; }
+
+size_t ring_bytes(bool pair, int bn, int raw) {
+  if (raw)
+    return bn == 256 ? (pair ? ring_of<true, 256, 3>() : ring_of<false, 256, 3>())
+                     : (pair ? ring_of<true, 128, 3>() : ring_of<false, 128, 3>());
+  return bn == 256 ? (pair ? ring_of<true, 256, 0>() : ring_of<false, 256, 0>())
+                   : (pair ? ring_of<true, 128, 0>() : ring_of<false, 128, 0>());
 }
 
-size_t tc_smem_bytes(int kind, int64_t N, bool pair, int bn) {
-  size_t b = 1024 + ring_bytes(pair, bn) + sizeof(Ctl);
+// Dynamic shared memory of a launch; raw = -1: the most any variant of this geometry takes
+// (the size every instantiation is opted in to).
+size_t tc_smem_bytes(int kind, int64_t N, bool pair, int bn, int raw = -1) {
+  const size_t ring = raw < 0 ? std::max(ring_bytes(pair, bn, 0), ring_bytes(pair, bn, 3)) : ring_bytes(pair, bn, raw);
+  size_t b = 1024 + ring + sizeof(Ctl);
   if (kind == TC_DX || kind == TC_DX_F32) b += (size_t)4 * N * sizeof(float);
   return b;
 }
@@ -1071,7 +1198,7 @@ Kern pick_fwd_dx(int kind, bool bits, bool has_lo, int bn) {
 template <int RAW>
 Kern pick_dw(bool pair, int bn) {
   if (bn == 256) return pair ? tc_gemm_kernel<TC_DW, false, true, 256, RAW> : tc_gemm_kernel<TC_DW, false, false, 256, RAW>;
-  return tc_gemm_kernel<TC_DW, false, false, 128, RAW>;
+  return pair ? tc_gemm_kernel<TC_DW, false, true, 128, RAW> : tc_gemm_kernel<TC_DW, false, false, 128, RAW>;
 }
 
 Kern pick(int kind, bool pair, bool bits, bool has_lo, int bn, int raw) {
@@ -1202,8 +1329,13 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   int rc;
   if (mn) {  // A [K x M], B [K x N] row-major; boxes 32 wide (MN) x 32 deep (K)
     const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    if ((rc = make_map(&m_ah, a.a_hi, a.M, a.K, 32, BK, sw))) return rc;
-    if ((rc = make_map(&m_al, a.a_lo ? a.a_lo : a.a_hi, a.M, a.K, 32, BK, sw))) return rc;
+    if (raw & kRawA) {   // fp32 A for tensor memory: one unswizzled [32 k][128 m] box
+      if ((rc = make_map(&m_ah, a.a_hi, a.M, a.K, BM, BK, CU_TENSOR_MAP_SWIZZLE_NONE))) return rc;
+      m_al = m_ah;
+    } else {
+      if ((rc = make_map(&m_ah, a.a_hi, a.M, a.K, 32, BK, sw))) return rc;
+      if ((rc = make_map(&m_al, a.a_lo, a.M, a.K, 32, BK, sw))) return rc;
+    }
     if ((rc = make_map(&m_bh, a.b_hi, a.N, a.K, 32, BK, sw))) return rc;
     if ((rc = make_map(&m_bl, a.b_lo ? a.b_lo : a.b_hi, a.N, a.K, 32, BK, sw))) return rc;
   } else {   // A [M x K], B [N x K] row-major; boxes 32 deep (K) x 128 (A) / b_rows (B) rows
@@ -1236,7 +1368,7 @@ int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s) {
   P.wait_ns = a.wait_ns > 0 ? a.wait_ns : kWaitNs;
   P.withhold = a.withhold;
   const int grid = tc_gemm_grid(a);
-  const size_t smem = tc_smem_bytes(a.kind, a.N, pair, bn);
+  const size_t smem = tc_smem_bytes(a.kind, a.N, pair, bn, raw);
   const int threads = threads_of(pair, bn, raw);
   const bool bits = a.kind == TC_FWD ? P.c_bits != nullptr : P.mask_bits != nullptr;
   const Kern kern = pick(a.kind, pair, bits, a.c_lo != nullptr, bn, raw);
