@@ -277,9 +277,29 @@ TRAFFIC_PER_LAUNCH = {}
 TC0_MIN_ROWS = 16384  # the library runs the input layer on tensor cores from this many rows
 
 
-def count_launches(wl, clip, engine="tensor", rows=None):
+SMALL_MAX_ROWS = 8192  # batches up to this many rows run as one launch when the shapes fit
+
+
+def small_step_fits(wl, rows):
+    """Whether the library runs this step as its one-launch small-batch step."""
+    if rows < 1 or rows > SMALL_MAX_ROWS:
+        return False
+    for net in (wl.actor, wl.critic):
+        if net is None:
+            continue
+        d = net.dims
+        if not (2 <= net.num_layers <= 4 and d[0] <= 32 and d[-1] in (1, 9)):
+            return False
+        if any(h % 32 or h > 256 for h in d[1:-1]):
+            return False
+    return True
+
+
+def count_launches(wl, clip, engine="tensor", rows=None, world=1):
     """libspo_cuda kernel launches of one learner step on `rows` rows (per rank)."""
     rows = wl.batch if rows is None else rows
+    if small_step_fits(wl, rows):
+        return 1 if world == 1 else 2    # the step; or backward, then Adam after the all-reduce
     n = 0
     for net in (wl.actor, wl.critic):
         if net is None:
@@ -526,7 +546,7 @@ def run_ours(args):
             # the whole step's arithmetic (forward, dW, dX: 2 flop per multiply-add, fp32
             # products) over its measured time
             "step_tflops_fp32": wl.flops_per_sample() * B / (ms_max / 1e3) / 1e12,
-            "gpu_launches": count_launches(wl, clip, args.engine, rows) * args.steps,
+            "gpu_launches": count_launches(wl, clip, args.engine, rows, world) * args.steps,
             "engine": args.engine,
             "stats": stats,
         }

@@ -419,6 +419,16 @@ SPO_API int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t laye
 /* Reads (synchronously) and clears the learner's device error word: 0 when every
  * bounded wait of its tensor-core kernels completed since the last call. */
 SPO_API int spo_learner_status(spo_learner_t learner, int32_t* device_error);
+/* Batches of at most max_rows rows run the whole step (or the backward of
+ * spo_learner_backward) as ONE cooperative launch whose phases are separated by grid-wide
+ * barriers, instead of ~10 dependent launches; 0 turns that off. The default is
+ * min(8192, desc.max_rows) when every network has 2-4 layers, an input at most 32 wide and
+ * hidden widths that are multiples of 32 up to 256 (else 0, and nonzero values are
+ * refused). Results agree with the multi-launch path within the fp32 tolerances; the
+ * reduction order of the partial sums differs, so the two are not bit-identical.
+ * No reference counterpart (the reference's update() is ~35 launches,
+ * demos/train_spo.mojo:417-554). */
+SPO_API int spo_learner_set_small_rows(spo_learner_t learner, int64_t max_rows);
 /* backward (grad_scale = 1 / rows) + apply. */
 SPO_API int spo_learner_step(spo_learner_t learner, spo_stream_t stream, const spo_batch* batch,
                      const spo_train_state* state);

@@ -26,6 +26,7 @@
 #include "gemm_simt.cuh"
 #include "kernels.cuh"
 #include "tc_gemm.cuh"
+#include "small_step.cuh"
 
 namespace spo {
 
@@ -263,6 +264,12 @@ struct NetPlan {
   float* dw_part[SPO_MAX_LAYERS] = {};
   int64_t dw_part_cap[SPO_MAX_LAYERS] = {};  // partials dw_part[l] holds
   float* db_part[SPO_MAX_LAYERS] = {};  // column sums of dZ_{l} from layer l+1's dX GEMM
+  // the one-launch small-batch step (small_step.cu): its partial sums
+  bool small = false;                   // the network's shape fits the small step
+  float* sm_pw[SPO_MAX_LAYERS] = {};
+  float* sm_pb[SPO_MAX_LAYERS] = {};
+  int sm_S[SPO_MAX_LAYERS] = {};
+  float* sm_pstats = nullptr;
 };
 
 }  // namespace spo
@@ -275,6 +282,12 @@ struct spo_learner {
   unsigned* ticket = nullptr;
   int* err = nullptr;  // device error word of the tensor-core kernels' bounded waits
   size_t ws_bytes = 0;
+  // one-launch step for batches of at most small_rows rows (0: never)
+  int64_t small_rows = 0;
+  int sm_grid = 0;
+  float* sm_sumsq = nullptr;            // [kMaxGroups][sm_grid]
+  unsigned* sm_sync = nullptr;          // barrier words, zero between launches
+  bool last_small = false;              // the last forward ran in the small step
 };
 
 namespace spo {
@@ -389,6 +402,16 @@ int check_net_desc(const spo_mlp_desc& d, int out_dim, const char* which) {
   return kOk;
 }
 
+// Shapes of the one-launch small-batch step: 2 to 4 Linear layers, input at most 32 wide,
+// hidden widths multiples of 32 up to 256, output 9 (actor) or 1 (critic).
+bool small_net_ok(const spo_mlp_desc& d) {
+  if (d.num_layers < 2 || d.num_layers > kSmallMaxLayers || d.dims[0] > kSmallMaxIn) return false;
+  for (int l = 1; l < d.num_layers; ++l)
+    if (d.dims[l] % 32 != 0 || d.dims[l] > kSmallMaxHidden) return false;
+  const int a = d.dims[d.num_layers];
+  return a == 1 || a == kSmallMaxA;
+}
+
 int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* bytes) {
   SPO_CHECK_ARG(desc != nullptr, kErrArg, "null descriptor");
   SPO_CHECK_ARG(desc->actor.num_layers > 0 || desc->critic.num_layers > 0, kErrArg,
@@ -444,6 +467,28 @@ int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* b
   L->sumsq_part = c.take<float>(kMaxGroups * kSumsqParts);
   L->ticket = c.take<unsigned>(4);
   L->err = c.take<int>(4);
+  L->sm_sync = c.take<unsigned>(4);
+  // The one-launch small-batch step: every present network must fit it.
+  bool small = true;
+  for (int i = 0; i < 2; ++i)
+    if (L->net[i].present) small = small && (L->net[i].small = small_net_ok(L->net[i].d));
+  L->small_rows = small ? std::min<int64_t>(kSmallDefaultRows, desc->max_rows) : 0;
+  if (small) {
+    const int G = sm_count();   // one CTA per SM
+    L->sm_grid = G;
+    for (int i = 0; i < 2; ++i) {
+      NetPlan& n = L->net[i];
+      if (!n.present) continue;
+      for (int l = 0; l < n.d.num_layers; ++l) {
+        const int64_t blocks = ceil_div(n.d.dims[l], 32) * ceil_div(n.d.dims[l + 1], 32);
+        n.sm_S[l] = (int)std::max<int64_t>(1, std::min<int64_t>(kSmallMaxS, ceil_div(G, blocks)));
+        n.sm_pw[l] = c.take<float>((size_t)n.sm_S[l] * n.d.dims[l] * n.d.dims[l + 1]);
+        n.sm_pb[l] = c.take<float>((size_t)n.sm_S[l] * n.d.dims[l + 1]);
+      }
+      n.sm_pstats = c.take<float>((size_t)G * kStats);
+    }
+    L->sm_sumsq = c.take<float>((size_t)kMaxGroups * G);
+  }
   *bytes = c.off + 256;
   return kOk;
 }
@@ -695,8 +740,148 @@ int net_backward(const spo_learner* Lr, int which, cudaStream_t s, const float* 
   return kOk;
 }
 
+// The loss statistics' segments of the reduction: the actor's slots and the critic's loss
+// slot from their per-CTA partials, the dual-gradient slot zeroed (Adam sets it).
+void add_stats_segs(ReduceParams& red, const spo_learner* Lr, float* grads, const float* const* src,
+                    const int* parts) {
+  const spo_learner_layout& lay = Lr->layout;
+  float* stats = grads + lay.stats_offset;
+  if (Lr->net[0].present && Lr->net[1].present) {
+    add_seg(red, src[0], stats, kStatCriticLoss, kStats, parts[0]);
+    add_seg(red, src[1] + kStatCriticLoss, stats + kStatCriticLoss, 1, kStats, parts[1]);
+    add_seg(red, src[0] + kStatCriticLoss + 1, stats + kStatCriticLoss + 1,
+            kStats - kStatCriticLoss - 1, kStats, parts[0]);
+  } else {
+    const int i = Lr->net[0].present ? 0 : 1;
+    add_seg(red, src[i], stats, kStats, kStats, parts[i]);
+  }
+  add_seg(red, nullptr, grads + lay.alpha_index, kAlignFloats, 0, 0);  // dual gradient: set by Adam
+}
+
+// Adam over the learner's flat buffers: one group per network (its lr and clip) and, with
+// the dual, the log_alpha slot. *clip: whether a global-norm clip applies.
+int build_adam(const spo_learner* Lr, const spo_train_state* st, AdamParams& ap, bool* clip) {
+  SPO_CHECK_ARG(st && st->params && st->grads && st->adam_m && st->adam_v && st->step, kErrArg,
+                "null train state");
+  const spo_learner_layout& lay = Lr->layout;
+  const spo_learner_desc& d = Lr->desc;
+  ap = AdamParams{};
+  ap.p = st->params;
+  ap.g = st->grads;
+  ap.m = st->adam_m;
+  ap.v = st->adam_v;
+  ap.b1 = d.beta1;
+  ap.b2 = d.beta2;
+  ap.eps = d.adam_eps;
+  ap.grad_scale = 1.f;
+  ap.step = st->step;
+  ap.ticket = Lr->ticket;
+  ap.alpha_index = -1;
+  ap.report = st->report;
+  *clip = d.max_grad_norm > 0.f && std::isfinite(d.max_grad_norm);
+  if (Lr->net[0].present)
+    ap.grp[ap.ngrp++] = AdamGroup{lay.actor_offset, lay.actor_offset + lay.actor_size, d.lr_actor,
+                                  *clip ? d.max_grad_norm : 0.f};
+  else
+    ap.grp[ap.ngrp++] = AdamGroup{0, 0, 0.f, 0.f};
+  if (Lr->net[1].present)
+    ap.grp[ap.ngrp++] = AdamGroup{lay.critic_offset, lay.critic_offset + lay.critic_size,
+                                  d.lr_critic, *clip ? d.max_grad_norm : 0.f};
+  else
+    ap.grp[ap.ngrp++] = AdamGroup{0, 0, 0.f, 0.f};
+  if (Lr->net[0].present && d.dual && d.use_kl) {
+    ap.grp[ap.ngrp++] = AdamGroup{lay.alpha_index, lay.alpha_index + 4, d.lr_actor, 0.f};
+    ap.alpha_index = lay.alpha_index;
+    ap.kl_stat = st->grads + lay.stats_offset + kStatKLold;
+    ap.kl_eps = d.kl_eps;
+  }
+  return kOk;
+}
+
+int learner_apply(spo_learner* Lr, cudaStream_t s, const spo_train_state* st) {
+  AdamParams ap{};
+  bool clip = false;
+  int rc = build_adam(Lr, st, ap, &clip);
+  if (rc) return rc;
+  if (clip) {
+    rc = sumsq_groups_launch(st->grads, ap.grp, 2, Lr->sumsq_part, s);
+    if (rc) return rc;
+    ap.sumsq_part = Lr->sumsq_part;
+  }
+  return adam_launch(ap, Lr->layout.total, s);
+}
+
+// The whole step of a small batch in one launch (small_step.cu); with apply, the clip and
+// Adam too.
+int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale, const spo_train_state* st,
+               bool apply) {
+  SmallStepParams p{};
+  const spo_learner_layout& lay = Lr->layout;
+  const int G = Lr->sm_grid;
+  SPO_CHECK_ARG(G >= 1 && G <= small_step_grid(), kErrUnsupported, "small step: grid is not co-resident");
+  const float* stats_src[2] = {nullptr, nullptr};
+  int stats_parts[2] = {0, 0};
+  for (int i = 0; i < 2; ++i) {
+    const NetPlan& n = Lr->net[i];
+    SmallNet& sn = p.net[i];
+    if (!n.present) continue;
+    const spo_mlp_desc& d = n.d;
+    const float* prm = st->params + n.offset;
+    float* grads = st->grads + n.offset;
+    sn.L = d.num_layers;
+    sn.mode = i;
+    for (int l = 0; l <= d.num_layers; ++l) sn.dims[l] = d.dims[l];
+    for (int l = 0; l < d.num_layers; ++l) {
+      sn.W[l] = prm + n.w_off[l];
+      sn.b[l] = prm + n.b_off[l];
+      sn.pw[l] = n.sm_pw[l];
+      sn.pb[l] = n.sm_pb[l];
+      sn.S[l] = n.sm_S[l];
+      add_seg(p.red, n.sm_pw[l], grads + n.w_off[l], (int64_t)d.dims[l] * d.dims[l + 1],
+              (int64_t)d.dims[l] * d.dims[l + 1], n.sm_S[l]);
+      add_seg(p.red, n.sm_pb[l], grads + n.b_off[l], d.dims[l + 1], d.dims[l + 1], n.sm_S[l]);
+    }
+    for (int l = 0; l + 1 < d.num_layers; ++l) sn.act[l] = n.acts[l];
+    sn.dz[0] = n.dz[0];
+    sn.dz[1] = n.dz[1];
+    sn.pstats = n.sm_pstats;
+    add_gap_segs(p.red, d, n.w_off, n.b_off, n.size, grads);
+    stats_src[i] = n.sm_pstats;
+    stats_parts[i] = G;
+  }
+  add_stats_segs(p.red, Lr, st->grads, stats_src, stats_parts);
+  SPO_CHECK_ARG(p.red.nseg <= kMaxSegs, kErrUnsupported, "too many reduction segments");
+  p.obs = b->obs;
+  p.cells = b->obs ? nullptr : b->cells;
+  p.mask = b->mask;
+  p.q = b->q;
+  p.z_old = Lr->desc.use_kl ? b->logits_old : nullptr;
+  p.target = b->target;
+  p.log_alpha = st->params + lay.alpha_index;
+  p.rows = b->rows;
+  p.scale = scale;
+  p.apply = apply ? 1 : 0;
+  if (apply) {
+    bool clip = false;
+    int rc = build_adam(Lr, st, p.adam, &clip);
+    if (rc) return rc;
+    p.clip = clip ? 1 : 0;
+  }
+  p.total = lay.total;
+  p.sumsq = Lr->sm_sumsq;
+  p.sync = Lr->sm_sync;
+  p.err = Lr->err;
+  p.wait_ns = 2000000000ull;
+  Lr->last_small = true;
+  return small_step_launch(p, G, s);
+}
+
+// Forward, loss and backward (gradients and statistics into st->grads). When `applied` is
+// given and the batch takes the one-launch small step, that launch also applies the
+// optimiser and *applied is set.
 int learner_backward(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
-                     const spo_train_state* st) {
+                     const spo_train_state* st, bool* applied = nullptr) {
+  if (applied) *applied = false;
   SPO_CHECK_ARG(b != nullptr && st != nullptr && st->params && st->grads, kErrArg, "null argument");
   SPO_CHECK_ARG(b->rows >= 0 && b->rows <= Lr->desc.max_rows, kErrShape,
                 "batch rows " + std::to_string(b->rows) + " exceed the learner's max_rows " +
@@ -713,10 +898,16 @@ int learner_backward(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float 
     SPO_CHECK_ARG(b->rows == 0 || b->target, kErrArg, "critic needs batch.target");
   SPO_CHECK_ARG(aligned16(st->params) && aligned16(st->grads), kErrAlign,
                 "params/grads must be 16-byte aligned");
-  const spo_learner_layout& lay = Lr->layout;
+  if (b->rows >= 1 && b->rows <= Lr->small_rows && (b->obs || (b->cells && (Lr->net[0].present ? Lr->net[0].d.dims[0] : Lr->net[1].d.dims[0]) == 27))) {
+    int rc = small_step(Lr, s, b, scale, st, applied != nullptr);
+    if (rc == kOk && applied) *applied = true;
+    return rc;
+  }
+  Lr->last_small = false;
   ReduceParams red{};
   const float* stats_src[2] = {nullptr, nullptr};
   int stats_parts[2] = {0, 0};
+  const spo_learner_layout& lay = Lr->layout;
   for (int i = 0; i < 2; ++i) {
     if (!Lr->net[i].present) continue;
     const int64_t off = Lr->net[i].offset;
@@ -724,62 +915,9 @@ int learner_backward(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float 
                           st->grads + off, red, &stats_src[i], &stats_parts[i]);
     if (rc) return rc;
   }
-  float* stats = st->grads + lay.stats_offset;
-  if (Lr->net[0].present && Lr->net[1].present) {
-    add_seg(red, stats_src[0], stats, kStatCriticLoss, kStats, stats_parts[0]);
-    add_seg(red, stats_src[1] + kStatCriticLoss, stats + kStatCriticLoss, 1, kStats, stats_parts[1]);
-    add_seg(red, stats_src[0] + kStatCriticLoss + 1, stats + kStatCriticLoss + 1,
-            kStats - kStatCriticLoss - 1, kStats, stats_parts[0]);
-  } else {
-    const int i = Lr->net[0].present ? 0 : 1;
-    add_seg(red, stats_src[i], stats, kStats, kStats, stats_parts[i]);
-  }
-  add_seg(red, nullptr, st->grads + lay.alpha_index, kAlignFloats, 0, 0);  // dual gradient: set by Adam
+  add_stats_segs(red, Lr, st->grads, stats_src, stats_parts);
   if (red.nseg > kMaxSegs) return set_error(kErrUnsupported, "too many reduction segments");
   return reduce_launch(red, s);
-}
-
-int learner_apply(spo_learner* Lr, cudaStream_t s, const spo_train_state* st) {
-  SPO_CHECK_ARG(st && st->params && st->grads && st->adam_m && st->adam_v && st->step, kErrArg,
-                "null train state");
-  const spo_learner_layout& lay = Lr->layout;
-  const spo_learner_desc& d = Lr->desc;
-  AdamParams ap{};
-  ap.p = st->params;
-  ap.g = st->grads;
-  ap.m = st->adam_m;
-  ap.v = st->adam_v;
-  ap.b1 = d.beta1;
-  ap.b2 = d.beta2;
-  ap.eps = d.adam_eps;
-  ap.grad_scale = 1.f;
-  ap.step = st->step;
-  ap.ticket = Lr->ticket;
-  ap.alpha_index = -1;
-  ap.report = st->report;
-  const bool clip = d.max_grad_norm > 0.f && std::isfinite(d.max_grad_norm);
-  if (Lr->net[0].present)
-    ap.grp[ap.ngrp++] = AdamGroup{lay.actor_offset, lay.actor_offset + lay.actor_size, d.lr_actor,
-                                  clip ? d.max_grad_norm : 0.f};
-  else
-    ap.grp[ap.ngrp++] = AdamGroup{0, 0, 0.f, 0.f};
-  if (Lr->net[1].present)
-    ap.grp[ap.ngrp++] = AdamGroup{lay.critic_offset, lay.critic_offset + lay.critic_size,
-                                  d.lr_critic, clip ? d.max_grad_norm : 0.f};
-  else
-    ap.grp[ap.ngrp++] = AdamGroup{0, 0, 0.f, 0.f};
-  if (Lr->net[0].present && d.dual && d.use_kl) {
-    ap.grp[ap.ngrp++] = AdamGroup{lay.alpha_index, lay.alpha_index + 4, d.lr_actor, 0.f};
-    ap.alpha_index = lay.alpha_index;
-    ap.kl_stat = st->grads + lay.stats_offset + kStatKLold;
-    ap.kl_eps = d.kl_eps;
-  }
-  if (clip) {
-    int rc = sumsq_groups_launch(st->grads, ap.grp, 2, Lr->sumsq_part, s);
-    if (rc) return rc;
-    ap.sumsq_part = Lr->sumsq_part;
-  }
-  return adam_launch(ap, lay.total, s);
 }
 
 }  // namespace
@@ -1222,6 +1360,7 @@ int spo_learner_create(const spo_learner_desc* desc, void* workspace, size_t wor
       L->ws_bytes = need;
       cudaError_t e = cudaMemset(L->ticket, 0, 4 * sizeof(unsigned));
       if (e == cudaSuccess) e = cudaMemset(L->err, 0, 4 * sizeof(int));
+      if (e == cudaSuccess) e = cudaMemset(L->sm_sync, 0, 4 * sizeof(unsigned));
       if (e != cudaSuccess) rc = set_error(kErrCuda, std::string("memset: ") + cudaGetErrorString(e));
     }
     if (rc != kOk) {
@@ -1257,7 +1396,7 @@ int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer, const
   const NetPlan& n = learner->net[which];
   SPO_CHECK_ARG(layer >= 0 && layer + 1 < n.d.num_layers, kErrArg, "no such hidden layer");
   *hi = n.acts[layer];
-  *lo = n.tc ? n.acts_lo[layer] : nullptr;
+  *lo = n.tc && !learner->last_small ? n.acts_lo[layer] : nullptr;
   return kOk;
 }
 
@@ -1274,9 +1413,22 @@ int spo_learner_step(spo_learner_t learner, spo_stream_t stream, const spo_batch
                      const spo_train_state* state) {
   SPO_CHECK_ARG(learner && batch, kErrArg, "null argument");
   const float scale = batch->rows > 0 ? 1.f / (float)batch->rows : 0.f;
-  int rc = learner_backward(learner, S(stream), batch, scale, state);
-  if (rc) return rc;
+  bool applied = false;
+  int rc = learner_backward(learner, S(stream), batch, scale, state, &applied);
+  if (rc || applied) return rc;
   return learner_apply(learner, S(stream), state);
+}
+
+int spo_learner_set_small_rows(spo_learner_t learner, int64_t max_rows) {
+  SPO_CHECK_ARG(learner != nullptr, kErrArg, "null learner");
+  SPO_CHECK_ARG(max_rows >= 0, kErrShape, "max_rows must be >= 0");
+  bool fits = true;
+  for (int i = 0; i < 2; ++i)
+    if (learner->net[i].present) fits = fits && learner->net[i].small;
+  SPO_CHECK_ARG(max_rows == 0 || fits, kErrUnsupported,
+                "the one-launch step needs 2-4 layers, input <= 32, hidden widths multiples of 32 up to 256");
+  learner->small_rows = std::min<int64_t>(max_rows, learner->desc.max_rows);
+  return kOk;
 }
 
 int spo_learner_forward(spo_learner_t learner, spo_stream_t stream, int32_t which,

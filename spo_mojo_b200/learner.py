@@ -152,6 +152,10 @@ class Learner:
             out.append(t.view(rows, dims[layer + 1]))
         return out
 
+    def set_small_rows(self, max_rows):
+        """Batches of at most max_rows rows run as one cooperative launch (0: never)."""
+        ffi.call("spo_learner_set_small_rows", self._h, int(max_rows))
+
     def device_status(self):
         """0 when every bounded wait of the tensor-core kernels completed (synchronises)."""
         v = ctypes.c_int32()

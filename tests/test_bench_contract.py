@@ -1,6 +1,6 @@
 """bench.py's launch count (its gpu_launches claim) against the kernels one learner step
-launches, as the ncu launch lists of c0 (256 rows: 9 kernels) and c3 (1,048,576 rows: 28
-kernels) show them."""
+launches, as the ncu launch lists show them: c0 (256 rows: one launch) and c3 (1,048,576
+rows: 28 kernels)."""
 
 import os
 import sys
@@ -14,18 +14,23 @@ from spo_mojo_b200.workloads import WORKLOADS  # noqa: E402
 
 
 def test_launch_count_matches_launch_lists():
-    # c0: W1 split, input-layer forward (CUDA cores below 16,384 rows), hidden forward,
-    # head, hidden dW, dX into the input layer, input-layer dW, reduction, Adam
-    assert bench.count_launches(WORKLOADS["c0"], clip=False) == 9
-    # c3, actor and critic: per network W1/W2 splits, W0^T and input splits, three forward
-    # GEMMs, head, two hidden dW, two dX, input-layer dW; then reduction and Adam
+    # c0 (256 rows) and c1 (4,096 rows): the one-launch small-batch step; under data
+    # parallelism its backward, then Adam after the all-reduce
+    assert bench.count_launches(WORKLOADS["c0"], clip=False) == 1
+    assert bench.count_launches(WORKLOADS["c1"], clip=True) == 1
+    assert bench.count_launches(WORKLOADS["c0"], clip=False, world=2) == 2
+    # c2 above the small-step rows: per network the W1/W2 splits, the input layer's W0^T and
+    # input splits (65,536 rows: tensor cores), three forward GEMMs, head, two hidden dW,
+    # two dX, input-layer dW; then reduction and Adam
+    assert bench.count_launches(WORKLOADS["c2"], clip=False) == 28
+    # c3, actor and critic: the same sequence
     assert bench.count_launches(WORKLOADS["c3"], clip=False) == 28
     # the same network below the input layer's tensor-core threshold: two launches fewer each
     assert bench.count_launches(WORKLOADS["c3"], clip=False, rows=bench.TC0_MIN_ROWS - 1) == 24
     # the CUDA-core engine has no splits
-    assert bench.count_launches(WORKLOADS["c0"], clip=False, engine="cuda") == 8
+    assert bench.count_launches(WORKLOADS["c3"], clip=False, engine="cuda") == 20
     # a clipped step adds the grouped sum of squares
-    assert bench.count_launches(WORKLOADS["c0"], clip=True) == 10
+    assert bench.count_launches(WORKLOADS["c3"], clip=True) == 29
 
 
 def test_reference_arm_prints_the_contract_line():
