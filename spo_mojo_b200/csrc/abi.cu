@@ -266,10 +266,9 @@ struct NetPlan {
   float* db_part[SPO_MAX_LAYERS] = {};  // column sums of dZ_{l} from layer l+1's dX GEMM
   // the one-launch small-batch step (small_step.cu): its partial sums
   bool small = false;                   // the network's shape fits the small step
-  float* sm_pw[SPO_MAX_LAYERS] = {};
-  float* sm_pb[SPO_MAX_LAYERS] = {};
-  int sm_S[SPO_MAX_LAYERS] = {};
-  float* sm_pstats = nullptr;
+  float* sm_pw[SPO_MAX_LAYERS] = {};   // [grid][d_l x d_{l+1}]
+  float* sm_pb[SPO_MAX_LAYERS] = {};   // [grid][d_{l+1}]
+  float* sm_pstats = nullptr;          // [grid][kStats]
 };
 
 }  // namespace spo
@@ -406,10 +405,12 @@ int check_net_desc(const spo_mlp_desc& d, int out_dim, const char* which) {
 // hidden widths multiples of 32 up to 256, output 9 (actor) or 1 (critic).
 bool small_net_ok(const spo_mlp_desc& d) {
   if (d.num_layers < 2 || d.num_layers > kSmallMaxLayers || d.dims[0] > kSmallMaxIn) return false;
+  int64_t params = 0;
+  for (int l = 0; l < d.num_layers; ++l) params += (int64_t)d.dims[l] * d.dims[l + 1] + d.dims[l + 1];
   for (int l = 1; l < d.num_layers; ++l)
     if (d.dims[l] % 32 != 0 || d.dims[l] > kSmallMaxHidden) return false;
   const int a = d.dims[d.num_layers];
-  return a == 1 || a == kSmallMaxA;
+  return (a == 1 || a == kSmallMaxA) && params <= kSmallMaxParams && small_step_smem(&d, 1) <= kSmallMaxSmem;
 }
 
 int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* bytes) {
@@ -480,10 +481,8 @@ int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* b
       NetPlan& n = L->net[i];
       if (!n.present) continue;
       for (int l = 0; l < n.d.num_layers; ++l) {
-        const int64_t blocks = ceil_div(n.d.dims[l], 32) * ceil_div(n.d.dims[l + 1], 32);
-        n.sm_S[l] = (int)std::max<int64_t>(1, std::min<int64_t>(kSmallMaxS, ceil_div(G, blocks)));
-        n.sm_pw[l] = c.take<float>((size_t)n.sm_S[l] * n.d.dims[l] * n.d.dims[l + 1]);
-        n.sm_pb[l] = c.take<float>((size_t)n.sm_S[l] * n.d.dims[l + 1]);
+        n.sm_pw[l] = c.take<float>((size_t)G * n.d.dims[l] * n.d.dims[l + 1]);
+        n.sm_pb[l] = c.take<float>((size_t)G * n.d.dims[l + 1]);
       }
       n.sm_pstats = c.take<float>((size_t)G * kStats);
     }
@@ -819,13 +818,20 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
   const spo_learner_layout& lay = Lr->layout;
   const int G = Lr->sm_grid;
   SPO_CHECK_ARG(G >= 1 && G <= small_step_grid(), kErrUnsupported, "small step: grid is not co-resident");
+  // rows per CTA: a multiple of 8, enough CTAs to spread the rows over the SMs
+  p.rows = b->rows;
+  p.rows_per_cta = std::max<int64_t>(8, align_up(ceil_div(b->rows, G), 8));
+  p.parts = (int)ceil_div(b->rows, p.rows_per_cta);
   const float* stats_src[2] = {nullptr, nullptr};
   int stats_parts[2] = {0, 0};
+  spo_mlp_desc descs[2];
+  int ndesc = 0;
   for (int i = 0; i < 2; ++i) {
     const NetPlan& n = Lr->net[i];
     SmallNet& sn = p.net[i];
     if (!n.present) continue;
     const spo_mlp_desc& d = n.d;
+    descs[ndesc++] = d;
     const float* prm = st->params + n.offset;
     float* grads = st->grads + n.offset;
     sn.L = d.num_layers;
@@ -836,21 +842,24 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
       sn.b[l] = prm + n.b_off[l];
       sn.pw[l] = n.sm_pw[l];
       sn.pb[l] = n.sm_pb[l];
-      sn.S[l] = n.sm_S[l];
       add_seg(p.red, n.sm_pw[l], grads + n.w_off[l], (int64_t)d.dims[l] * d.dims[l + 1],
-              (int64_t)d.dims[l] * d.dims[l + 1], n.sm_S[l]);
-      add_seg(p.red, n.sm_pb[l], grads + n.b_off[l], d.dims[l + 1], d.dims[l + 1], n.sm_S[l]);
+              (int64_t)d.dims[l] * d.dims[l + 1], p.parts);
+      add_seg(p.red, n.sm_pb[l], grads + n.b_off[l], d.dims[l + 1], d.dims[l + 1], p.parts);
     }
-    for (int l = 0; l + 1 < d.num_layers; ++l) sn.act[l] = n.acts[l];
-    sn.dz[0] = n.dz[0];
-    sn.dz[1] = n.dz[1];
     sn.pstats = n.sm_pstats;
     add_gap_segs(p.red, d, n.w_off, n.b_off, n.size, grads);
     stats_src[i] = n.sm_pstats;
-    stats_parts[i] = G;
+    stats_parts[i] = p.parts;
   }
   add_stats_segs(p.red, Lr, st->grads, stats_src, stats_parts);
   SPO_CHECK_ARG(p.red.nseg <= kMaxSegs, kErrUnsupported, "too many reduction segments");
+  int64_t e = 0;
+  for (int k = 0; k < p.red.nseg; ++k) {
+    p.seg_start[k] = e;
+    p.flat_index[k] = p.red.seg[k].dst - st->grads;
+    e += p.red.seg[k].count;
+  }
+  p.total_red = e;
   p.obs = b->obs;
   p.cells = b->obs ? nullptr : b->cells;
   p.mask = b->mask;
@@ -858,7 +867,6 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
   p.z_old = Lr->desc.use_kl ? b->logits_old : nullptr;
   p.target = b->target;
   p.log_alpha = st->params + lay.alpha_index;
-  p.rows = b->rows;
   p.scale = scale;
   p.apply = apply ? 1 : 0;
   if (apply) {
@@ -873,7 +881,7 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
   p.err = Lr->err;
   p.wait_ns = 2000000000ull;
   Lr->last_small = true;
-  return small_step_launch(p, G, s);
+  return small_step_launch(p, G, small_step_smem(descs, ndesc), s);
 }
 
 // Forward, loss and backward (gradients and statistics into st->grads). When `applied` is

@@ -1,6 +1,7 @@
 // The one-launch learner step for small batches (small_step.cu): parameters and limits.
 #pragma once
 
+#include "spo_cuda.h"
 #include "kernels.cuh"
 
 namespace spo {
@@ -9,10 +10,9 @@ constexpr int kSmallMaxLayers = 4;     // Linear layers per network
 constexpr int kSmallMaxHidden = 256;   // hidden widths: multiples of 32, at most this
 constexpr int kSmallMaxIn = 32;        // input width
 constexpr int kSmallMaxA = 9;          // output width (9 actions, or 1 value)
-constexpr int kSmallMaxS = 16;         // row chunks of a dW product
+constexpr int64_t kSmallMaxParams = 65536;   // weights + biases per network (partials per CTA)
 constexpr int64_t kSmallDefaultRows = 8192;
-
-__host__ __device__ inline int64_t ceil_div_dev(int64_t a, int64_t b) { return (a + b - 1) / b; }
+constexpr size_t kSmallMaxSmem = 200 * 1024;
 
 struct SmallNet {
   int L;                               // Linear layers (0: no such network)
@@ -20,12 +20,9 @@ struct SmallNet {
   int mode;                            // 0 actor (9 actions), 1 critic (1 value)
   const float* W[kSmallMaxLayers];     // W_l [d_l x d_{l+1}], b_l: views of the params
   const float* b[kSmallMaxLayers];
-  float* act[kSmallMaxLayers - 1];     // post-ReLU a_l [rows x d_{l+1}]
-  float* dz[2];                        // gradients flowing down, ping-pong [rows x <= max width]
-  float* pw[kSmallMaxLayers];          // dW partials [S_l][d_l x d_{l+1}]
-  float* pb[kSmallMaxLayers];          // db partials [S_l][d_{l+1}]
-  int S[kSmallMaxLayers];              // row chunks of layer l's dW
-  float* pstats;                       // loss statistics per CTA [grid][kStats]
+  float* pw[kSmallMaxLayers];          // dW partials [parts][d_l x d_{l+1}]
+  float* pb[kSmallMaxLayers];          // db partials [parts][d_{l+1}]
+  float* pstats;                       // loss statistics [parts][kStats]
 };
 
 struct SmallStepParams {
@@ -38,8 +35,13 @@ struct SmallStepParams {
   const float* target;                 // critic [rows]
   const float* log_alpha;
   int64_t rows;
+  int64_t rows_per_cta;                // CTA c owns rows [c * rows_per_cta, ...)
+  int parts;                           // CTAs with rows (= partials per sum)
   float scale;                         // gradient scale (1 / global batch)
   ReduceParams red;                    // partials -> flat gradients
+  int64_t seg_start[kMaxSegs];         // first reduced element of each segment
+  int64_t flat_index[kMaxSegs];        // its index in the flat buffers
+  int64_t total_red;                   // reduced elements
   int apply;                           // clip (optional) and Adam after the backward
   int clip;
   AdamParams adam;
@@ -50,7 +52,9 @@ struct SmallStepParams {
   uint64_t wait_ns;                    // limit of every barrier wait
 };
 
+// Dynamic shared memory of the nets' row blocks (the largest of the given networks).
+size_t small_step_smem(const spo_mlp_desc* nets, int count);
 int small_step_grid();                 // CTAs of a launch (all co-resident), 0 if unavailable
-int small_step_launch(const SmallStepParams& p, int grid, cudaStream_t s);
+int small_step_launch(const SmallStepParams& p, int grid, size_t smem, cudaStream_t s);
 
 }  // namespace spo
