@@ -824,14 +824,11 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
   p.parts = (int)ceil_div(b->rows, p.rows_per_cta);
   const float* stats_src[2] = {nullptr, nullptr};
   int stats_parts[2] = {0, 0};
-  spo_mlp_desc descs[2];
-  int ndesc = 0;
   for (int i = 0; i < 2; ++i) {
     const NetPlan& n = Lr->net[i];
     SmallNet& sn = p.net[i];
     if (!n.present) continue;
     const spo_mlp_desc& d = n.d;
-    descs[ndesc++] = d;
     const float* prm = st->params + n.offset;
     float* grads = st->grads + n.offset;
     sn.L = d.num_layers;
@@ -847,6 +844,7 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
       add_seg(p.red, n.sm_pb[l], grads + n.b_off[l], d.dims[l + 1], d.dims[l + 1], p.parts);
     }
     sn.pstats = n.sm_pstats;
+    for (int l = 0; l + 1 < d.num_layers; ++l) sn.gact[l] = n.acts[l];   // the activation cache
     add_gap_segs(p.red, d, n.w_off, n.b_off, n.size, grads);
     stats_src[i] = n.sm_pstats;
     stats_parts[i] = p.parts;
@@ -881,7 +879,7 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
   p.err = Lr->err;
   p.wait_ns = 2000000000ull;
   Lr->last_small = true;
-  return small_step_launch(p, G, small_step_smem(descs, ndesc), s);
+  return small_step_launch(p, G, kSmallMaxSmem, s);
 }
 
 // Forward, loss and backward (gradients and statistics into st->grads). When `applied` is

@@ -95,63 +95,90 @@ __device__ bool grid_barrier(unsigned& target, const SmallStepParams& P) {
 // Shared-memory rows: stride = width rounded up to 4 (float4 access).
 __device__ __forceinline__ int pad4(int n) { return (n + 3) & ~3; }
 
-// out[R x N] = relu(in[R x K] W[K x N] + b) (in: stride ks; out: stride N). N % 32 == 0.
+// out[R x N] = relu(in[R x K] W[K x N] + b) (in: stride ks; out: stride N), N % 32 == 0;
+// also to gout (the activation cache in global memory, stride N) when given. W comes into
+// shared memory (ws, wcap floats) a chunk of whole rows at a time, every thread issuing its
+// share of the 16-byte loads before any is used.
 __device__ void block_forward(const float* in, int ks, int K, const float* W, const float* b, int N, float* out,
-                              int R) {
+                              float* gout, int R, float* ws, int wcap) {
   const int cg = N / 4, rg = kT / cg, t = threadIdx.x;
   const int c = 4 * (t % cg), r0 = t / cg;
-  if (r0 >= rg) return;   // threads past the last full row group (when 256 % cg != 0)
-  constexpr int kMaxRows = kR / 4;   // rows per thread (N >= 32 gives rg >= 32 / (N / 32) ...)
+  const bool active = r0 < rg;   // threads past the last full row group (256 % cg != 0) only stage
+  constexpr int kMaxRows = kR / 4;
   float acc[kMaxRows][4] = {};
-  const int nr = (R - r0 + rg - 1) / rg;   // rows r0, r0 + rg, ... of this thread
-  for (int k = 0; k < K; ++k) {
-    const float4 w = *reinterpret_cast<const float4*>(W + (int64_t)k * N + c);
+  const int nr = active ? (R - r0 + rg - 1) / rg : 0;   // rows r0, r0 + rg, ... of this thread
+  const int rc = max(4, min(K, wcap / N) & ~3);   // W rows per chunk
+  for (int kc = 0; kc < K; kc += rc) {
+    const int kn = min(rc, K - kc);
+    __syncthreads();   // the previous chunk's readers are done
+    const float4* src = reinterpret_cast<const float4*>(W + (int64_t)kc * N);
+    float4* dst = reinterpret_cast<float4*>(ws);
+    for (int e = t; e < kn * N / 4; e += kT) dst[e] = src[e];
+    __syncthreads();
+    for (int k = 0; k < kn; ++k) {
+      const float4 w = *reinterpret_cast<const float4*>(ws + k * N + c);
 #pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) {
-      if (j >= nr) break;
-      const float a = in[(r0 + j * rg) * ks + k];
-      acc[j][0] = fmaf(a, w.x, acc[j][0]);
-      acc[j][1] = fmaf(a, w.y, acc[j][1]);
-      acc[j][2] = fmaf(a, w.z, acc[j][2]);
-      acc[j][3] = fmaf(a, w.w, acc[j][3]);
+      for (int j = 0; j < kMaxRows; ++j) {
+        if (j >= nr) break;
+        const float a = in[(r0 + j * rg) * ks + kc + k];
+        acc[j][0] = fmaf(a, w.x, acc[j][0]);
+        acc[j][1] = fmaf(a, w.y, acc[j][1]);
+        acc[j][2] = fmaf(a, w.z, acc[j][2]);
+        acc[j][3] = fmaf(a, w.w, acc[j][3]);
+      }
     }
   }
+  if (!active) return;
   const float4 bb = *reinterpret_cast<const float4*>(b + c);
 #pragma unroll
   for (int j = 0; j < kMaxRows; ++j) {
     if (j >= nr) break;
+    const int r = r0 + j * rg;
     float4 y;
     y.x = fmaxf(acc[j][0] + bb.x, 0.f);
     y.y = fmaxf(acc[j][1] + bb.y, 0.f);
     y.z = fmaxf(acc[j][2] + bb.z, 0.f);
     y.w = fmaxf(acc[j][3] + bb.w, 0.f);
-    *reinterpret_cast<float4*>(out + (r0 + j * rg) * N + c) = y;
+    *reinterpret_cast<float4*>(out + r * N + c) = y;
+    if (gout) __stcg(reinterpret_cast<float4*>(gout + (int64_t)r * N + c), y);
   }
 }
 
-// out[R x K] = (dz[R x N] W[K x N]^T) * [act > 0] (dz: stride zs; act, out: stride K).
-// K % 32 == 0 (a hidden width); N any (9 or 1 for the last layer).
+// out[R x K] = (dz[R x N] W[K x N]^T) * [act > 0] (dz: stride zs; act, out: stride K),
+// K % 32 == 0 (a hidden width), N any (9 or 1 for the last layer). W comes into shared
+// memory transposed, a chunk of its columns at a time: wt[n][k], row stride K + 4.
 __device__ void block_dx(const float* dz, int zs, int N, const float* W, int K, const float* act, float* out,
-                         int R) {
+                         int R, float* wt, int wcap) {
   const int cg = K / 4, rg = kT / cg, t = threadIdx.x;
   const int c = 4 * (t % cg), r0 = t / cg;
-  if (r0 >= rg) return;
+  const bool active = r0 < rg;
   constexpr int kMaxRows = kR / 4;
   float acc[kMaxRows][4] = {};
-  const int nr = (R - r0 + rg - 1) / rg;
-  for (int n = 0; n < N; ++n) {
-    const float w0 = W[(int64_t)c * N + n], w1 = W[(int64_t)(c + 1) * N + n];
-    const float w2 = W[(int64_t)(c + 2) * N + n], w3 = W[(int64_t)(c + 3) * N + n];
+  const int nr = active ? (R - r0 + rg - 1) / rg : 0;
+  const int ws = K + 4;
+  const int nc = max(1, min(N, wcap / ws));   // W columns per chunk
+  for (int n0 = 0; n0 < N; n0 += nc) {
+    const int nn = min(nc, N - n0);
+    __syncthreads();
+    for (int e = t; e < K * nn; e += kT) {
+      const int k = e / nn, n = e - k * nn;
+      wt[n * ws + k] = W[(int64_t)k * N + n0 + n];
+    }
+    __syncthreads();
+    for (int n = 0; n < nn; ++n) {
+      const float4 w = *reinterpret_cast<const float4*>(wt + n * ws + c);
 #pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) {
-      if (j >= nr) break;
-      const float z = dz[(r0 + j * rg) * zs + n];
-      acc[j][0] = fmaf(z, w0, acc[j][0]);
-      acc[j][1] = fmaf(z, w1, acc[j][1]);
-      acc[j][2] = fmaf(z, w2, acc[j][2]);
-      acc[j][3] = fmaf(z, w3, acc[j][3]);
+      for (int j = 0; j < kMaxRows; ++j) {
+        if (j >= nr) break;
+        const float z = dz[(r0 + j * rg) * zs + n0 + n];
+        acc[j][0] = fmaf(z, w.x, acc[j][0]);
+        acc[j][1] = fmaf(z, w.y, acc[j][1]);
+        acc[j][2] = fmaf(z, w.z, acc[j][2]);
+        acc[j][3] = fmaf(z, w.w, acc[j][3]);
+      }
     }
   }
+  if (!active) return;
 #pragma unroll
   for (int j = 0; j < kMaxRows; ++j) {
     if (j >= nr) break;
@@ -204,9 +231,8 @@ __device__ void block_dw(const float* in, int ks, int K, const float* dz, int zs
 // Logits / V of rows [0, R) of the block, the row losses and dz (into dz, stride zs); the
 // statistics accumulate in st (lane 0 of each warp).
 __device__ void block_loss(const SmallStepParams& P, const SmallNet& n, const float* act, int64_t row0, int R,
-                           float* dz, int zs, float (&st)[kStats]) {
-  const int L = n.L, H = n.dims[L - 1], A = n.dims[L];
-  const float* W = n.W[L - 1];
+                           float* dz, int zs, const float* W, float (&st)[kStats]) {
+  const int L = n.L, H = n.dims[L - 1], A = n.dims[L];   // W: the last layer's [H x A] in shared memory
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool actor = n.mode == 0;
   const float alpha = (actor && P.z_old) ? softplus_f(*P.log_alpha) : 0.f;
@@ -268,12 +294,23 @@ __device__ void block_loss(const SmallStepParams& P, const SmallNet& n, const fl
   }
 }
 
+// Shared memory of one network's row block, in floats: x [kR x 32] | a_0 .. a_{L-2}
+// [kR x d_{l+1}] | dz ping-pong 2 x [kR x dmax] | the last layer's W [H x A] | a weight
+// staging area (the rest, up to kSmallMaxSmem).
+__host__ __device__ inline int small_base_floats(const int* dims, int L) {
+  int f = kR * 32, dmax = (dims[L] + 3) & ~3;
+  for (int l = 1; l < L; ++l) {
+    f += kR * dims[l];
+    dmax = dims[l] > dmax ? dims[l] : dmax;
+  }
+  return f + 2 * kR * dmax + ((dims[L - 1] * dims[L] + 3) & ~3);
+}
+
 // One network over this CTA's rows [rb, re), 32 rows at a time.
 __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re, float* sm,
                          float* red) {
   const int L = n.L, d0 = n.dims[0];
   const int part = blockIdx.x;
-  // shared memory: x [kR x 32] | a_0 .. a_{L-2} [kR x d] | dz ping-pong 2 x [kR x dmax]
   float* xs = sm;
   float* acts[kSmallMaxLayers - 1];
   float* p = xs + kR * 32;
@@ -284,6 +321,10 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
     dmax = max(dmax, n.dims[l + 1]);
   }
   float* dzb[2] = {p, p + kR * dmax};
+  float* hw = p + 2 * kR * dmax;
+  float* ws = hw + pad4(n.dims[L - 1] * n.dims[L]);
+  const int wcap = (int)(kSmallMaxSmem / sizeof(float)) - small_base_floats(n.dims, L);
+  for (int e = threadIdx.x; e < n.dims[L - 1] * n.dims[L]; e += kT) hw[e] = n.W[L - 1][e];
   float st[kStats] = {};
   bool first = true;
   for (int64_t r0 = rb; r0 < re; r0 += kR, first = false) {
@@ -307,11 +348,11 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
     __syncthreads();
     for (int l = 0; l + 1 < L; ++l) {
       block_forward(l == 0 ? xs : acts[l - 1], l == 0 ? 32 : n.dims[l], n.dims[l], n.W[l], n.b[l], n.dims[l + 1],
-                    acts[l], R);
+                    acts[l], n.gact[l] ? n.gact[l] + r0 * n.dims[l + 1] : nullptr, R, ws, wcap);
       __syncthreads();
     }
     int zs = pad4(n.dims[L]);   // row stride of the gradient in dzb[cur]: its layer's width
-    block_loss(P, n, acts[L - 2], r0, R, dzb[0], zs, st);
+    block_loss(P, n, acts[L - 2], r0, R, dzb[0], zs, hw, st);
     __syncthreads();
     int cur = 0;
     for (int l = L - 1; l >= 0; --l) {
@@ -319,7 +360,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
       const int ks = l == 0 ? 32 : n.dims[l];
       block_dw(in, ks, n.dims[l], dzb[cur], zs, n.dims[l + 1], R, n.pw[l] + (int64_t)part * n.dims[l] * n.dims[l + 1],
                n.pb[l] + (int64_t)part * n.dims[l + 1], first);
-      if (l >= 1) block_dx(dzb[cur], zs, n.dims[l + 1], n.W[l], n.dims[l], acts[l - 1], dzb[cur ^ 1], R);
+      if (l >= 1) block_dx(dzb[cur], zs, n.dims[l + 1], n.W[l], n.dims[l], acts[l - 1], dzb[cur ^ 1], R, ws, wcap);
       __syncthreads();
       zs = n.dims[l];
       cur ^= 1;
@@ -505,18 +546,15 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
 }  // namespace
 
 size_t small_step_smem(const spo_mlp_desc* nets, int count) {
+  // the base of every network plus room to stage at least 4 rows (forward) and 1 column
+  // (dX, stride <= 260) of its weights; the launch takes all kSmallMaxSmem bytes
   size_t most = 0;
   for (int i = 0; i < count; ++i) {
     const spo_mlp_desc& d = nets[i];
     if (d.num_layers < 2) continue;
-    size_t f = (size_t)kR * 32;
-    int dmax = (d.dims[d.num_layers] + 3) & ~3;
-    for (int l = 1; l < d.num_layers; ++l) {
-      f += (size_t)kR * d.dims[l];
-      dmax = std::max(dmax, d.dims[l]);
-    }
-    f += 2 * (size_t)kR * dmax;
-    most = std::max(most, f * sizeof(float));
+    int wneed = 4 * 256;
+    for (int l = 0; l < d.num_layers; ++l) wneed = std::max(wneed, 4 * d.dims[l + 1]);
+    most = std::max(most, (size_t)(small_base_floats(d.dims, d.num_layers) + wneed) * sizeof(float));
   }
   return most;
 }

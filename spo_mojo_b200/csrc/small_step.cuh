@@ -12,7 +12,7 @@ constexpr int kSmallMaxIn = 32;        // input width
 constexpr int kSmallMaxA = 9;          // output width (9 actions, or 1 value)
 constexpr int64_t kSmallMaxParams = 65536;   // weights + biases per network (partials per CTA)
 constexpr int64_t kSmallDefaultRows = 8192;
-constexpr size_t kSmallMaxSmem = 200 * 1024;
+constexpr size_t kSmallMaxSmem = 220 * 1024;   // dynamic shared memory of every launch
 
 struct SmallNet {
   int L;                               // Linear layers (0: no such network)
@@ -23,6 +23,7 @@ struct SmallNet {
   float* pw[kSmallMaxLayers];          // dW partials [parts][d_l x d_{l+1}]
   float* pb[kSmallMaxLayers];          // db partials [parts][d_{l+1}]
   float* pstats;                       // loss statistics [parts][kStats]
+  float* gact[kSmallMaxLayers - 1];    // the activation cache a_l [rows x d_{l+1}] (or null)
 };
 
 struct SmallStepParams {
