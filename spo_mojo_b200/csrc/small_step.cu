@@ -95,6 +95,21 @@ __device__ bool grid_barrier(unsigned& target, const SmallStepParams& P) {
 // Shared-memory rows: stride = width rounded up to 4 (float4 access).
 __device__ __forceinline__ int pad4(int n) { return (n + 3) & ~3; }
 
+// Shared-memory copies of global data issued as asynchronous 16-byte copies (L2 only),
+// every thread's share in flight at once; the caller waits with copies_wait().
+__device__ __forceinline__ void cp16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void copies_wait() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+// n4 float4 from src (16-byte aligned) to dst, all threads of the CTA.
+__device__ __forceinline__ void stage16(float* dst, const float* src, int n4) {
+  for (int e = threadIdx.x; e < n4; e += kT) cp16(dst + 4 * e, src + 4 * e);
+}
+
 // out[R x N] = relu(in[R x K] W[K x N] + b) (in: stride ks; out: stride N), N % 32 == 0;
 // also to gout (the activation cache in global memory, stride N) when given. W comes into
 // shared memory (ws, wcap floats) a chunk of whole rows at a time, every thread issuing its
@@ -111,9 +126,8 @@ __device__ void block_forward(const float* in, int ks, int K, const float* W, co
   for (int kc = 0; kc < K; kc += rc) {
     const int kn = min(rc, K - kc);
     __syncthreads();   // the previous chunk's readers are done
-    const float4* src = reinterpret_cast<const float4*>(W + (int64_t)kc * N);
-    float4* dst = reinterpret_cast<float4*>(ws);
-    for (int e = t; e < kn * N / 4; e += kT) dst[e] = src[e];
+    stage16(ws, W + (int64_t)kc * N, kn * N / 4);
+    copies_wait();
     __syncthreads();
     for (int k = 0; k < kn; ++k) {
       const float4 w = *reinterpret_cast<const float4*>(ws + k * N + c);
@@ -160,9 +174,25 @@ __device__ void block_dx(const float* dz, int zs, int N, const float* W, int K, 
   for (int n0 = 0; n0 < N; n0 += nc) {
     const int nn = min(nc, N - n0);
     __syncthreads();
-    for (int e = t; e < K * nn; e += kT) {
-      const int k = e / nn, n = e - k * nn;
-      wt[n * ws + k] = W[(int64_t)k * N + n0 + n];
+    // 8 loads in flight per thread, then their transposed stores
+    for (int e0 = t; e0 < K * nn; e0 += 8 * kT) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + u * kT;
+        if (e < K * nn) {
+          const int k = e / nn, n = e - k * nn;
+          v[u] = W[(int64_t)k * N + n0 + n];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int e = e0 + u * kT;
+        if (e < K * nn) {
+          const int k = e / nn, n = e - k * nn;
+          wt[n * ws + k] = v[u];
+        }
+      }
     }
     __syncthreads();
     for (int n = 0; n < nn; ++n) {
@@ -324,26 +354,35 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
   float* hw = p + 2 * kR * dmax;
   float* ws = hw + pad4(n.dims[L - 1] * n.dims[L]);
   const int wcap = (int)(kSmallMaxSmem / sizeof(float)) - small_base_floats(n.dims, L);
-  for (int e = threadIdx.x; e < n.dims[L - 1] * n.dims[L]; e += kT) hw[e] = n.W[L - 1][e];
+  // the last layer's W: H x A floats, a multiple of 4 (H % 32 == 0), 16-byte aligned
+  stage16(hw, n.W[L - 1], n.dims[L - 1] * n.dims[L] / 4);
+  copies_wait();
   float st[kStats] = {};
   bool first = true;
   for (int64_t r0 = rb; r0 < re; r0 += kR, first = false) {
     const int R = (int)min((int64_t)kR, re - r0);
     // input rows (zero past d0); board cells expand to the plane-major planes
-    for (int e = threadIdx.x; e < kR * 32; e += kT) {
-      const int r = e >> 5, f = e & 31;
-      float v = 0.f;
-      if (r < R && f < d0) {
-        const int64_t row = r0 + r;
-        if (P.obs) {
-          v = P.obs[row * d0 + f];
-        } else {
-          const float c = P.cells[row * 9 + (f % 9)];
-          const int plane = f / 9;
-          v = (plane == 0 ? c == 0.f : (plane == 1 ? c == 1.f : c == -1.f)) ? 1.f : 0.f;
+    {
+      float v[kR * 32 / kT];   // this thread's 4 input values, loaded together
+#pragma unroll
+      for (int u = 0; u < kR * 32 / kT; ++u) {
+        const int e = threadIdx.x + u * kT, r = e >> 5, f = e & 31;
+        v[u] = 0.f;
+        if (r < R && f < d0) {
+          const int64_t row = r0 + r;
+          v[u] = P.obs ? P.obs[row * d0 + f] : P.cells[row * 9 + (f % 9)];
         }
       }
-      xs[e] = v;
+#pragma unroll
+      for (int u = 0; u < kR * 32 / kT; ++u) {
+        const int e = threadIdx.x + u * kT, r = e >> 5, f = e & 31;
+        float x = v[u];
+        if (!P.obs && r < R && f < d0) {   // cell code -> the plane's 0/1 value
+          const int plane = f / 9;
+          x = (plane == 0 ? x == 0.f : (plane == 1 ? x == 1.f : x == -1.f)) ? 1.f : 0.f;
+        }
+        xs[e] = x;
+      }
     }
     __syncthreads();
     for (int l = 0; l + 1 < L; ++l) {
@@ -388,14 +427,25 @@ __device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, 
   p = p - lr * (m * bc1) / (sqrtf(v * bc2) + eps);
 }
 
+// sum over k < parts of src[k * stride] with 8 loads in flight: part k goes to partial sum
+// k % 8 and the eight are combined in a fixed order (deterministic).
+__device__ __forceinline__ float sum_parts(const float* src, int parts, int64_t stride) {
+  float a[8] = {};
+  int k = 0;
+  for (; k + 8 <= parts; k += 8) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) a[u] += ldcg(src + (int64_t)(k + u) * stride);
+  }
+  for (int u = 0; k < parts; ++k, ++u) a[u] += ldcg(src + (int64_t)k * stride);
+  return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+}
+
 // Reduced value of flat element e (the segment it falls in, its parts in order).
 __device__ __forceinline__ float reduced(const SmallStepParams& P, int64_t e, int& si) {
   while (si + 1 < P.red.nseg && e >= P.seg_start[si + 1]) ++si;
   const ReduceSeg& sg = P.red.seg[si];
   const int64_t i = e - P.seg_start[si];
-  float v = 0.f;
-  for (int k = 0; k < sg.parts; ++k) v += ldcg(sg.src + (int64_t)k * sg.part_stride + i);
-  return v;
+  return sum_parts(sg.src + i, sg.parts, sg.part_stride);
 }
 
 __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant__ SmallStepParams P) {
@@ -446,8 +496,7 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
       if (fe == ap.alpha_index) {
         // dual gradient: sigmoid(log_alpha) * (eps - mean KL(pi_old || pi)), the KL from the
         // actor's per-CTA statistics in the same order as its own reduced slot
-        float kl = 0.f;
-        for (int k = 0; k < P.parts; ++k) kl += ldcg(P.net[0].pstats + (int64_t)k * kStats + kStatKLold);
+        const float kl = sum_parts(P.net[0].pstats + kStatKLold, P.parts, kStats);
         gv = (1.f / (1.f + expf(-ldcg(ap.p + fe)))) * (ap.kl_eps - kl);
         __stcg(ap.g + fe, gv);
         if (ap.report) ap.report[kRepDlogAlpha] = gv;
