@@ -348,9 +348,11 @@ def run_ours(args):
     scale = 1.0 / B
 
     def eager_step(b):
+        if comm is None:             # one GPU: the public step (one launch for small batches)
+            L.step(b, stream=stream)
+            return
         L.backward(b, grad_scale=scale, stream=stream)
-        if comm is not None:
-            comm.allreduce_(L.grads, stream=stream)
+        comm.allreduce_(L.grads, stream=stream)
         L.apply(stream=stream)
 
     if args.graph and world > 1:
