@@ -40,7 +40,37 @@ namespace {
 constexpr int kT = 256;      // threads per CTA
 constexpr int kW = kT / 32;  // warps per CTA
 constexpr int kR = 32;       // rows held in shared memory at a time
+constexpr int kLossIn = 28;  // per-row loss inputs in shared memory: mask | q | pi_old logits (9 each)
 constexpr int kErrGridWait = 16;
+
+// SPO_SMALL_TRACE builds record %globaltimer at the phase boundaries of every CTA (thread
+// 0) into small_trace[CTA][mark], read back with spo_small_trace_read; other builds
+// compile the marks away.
+#ifdef SPO_SMALL_TRACE
+constexpr int kTraceMarks = 16;
+__device__ unsigned long long small_trace[1024 * kTraceMarks];
+#define SS_MARK(i)                                                                          \
+  do {                                                                                      \
+    if (threadIdx.x == 0) {                                                                 \
+      unsigned long long t_;                                                                \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                \
+      small_trace[blockIdx.x * kTraceMarks + (i)] = t_;                                     \
+      if ((i) == 0 || (i) == 8) small_trace[blockIdx.x * kTraceMarks + 14 + ((i) == 8)] = clock64(); \
+    }                                                                                       \
+  } while (0)
+#define SS_SYNC_MARK(i) \
+  do {                  \
+    __syncthreads();    \
+    SS_MARK(i);         \
+  } while (0)
+#else
+#define SS_SYNC_MARK(i) \
+  do {                  \
+  } while (0)
+#define SS_MARK(i) \
+  do {             \
+  } while (0)
+#endif
 
 __device__ __forceinline__ uint64_t now_ns() {
   uint64_t t;
@@ -95,187 +125,346 @@ __device__ bool grid_barrier(unsigned& target, const SmallStepParams& P) {
 // Shared-memory rows: stride = width rounded up to 4 (float4 access).
 __device__ __forceinline__ int pad4(int n) { return (n + 3) & ~3; }
 
-// Shared-memory copies of global data issued as asynchronous 16-byte copies (L2 only),
-// every thread's share in flight at once; the caller waits with copies_wait().
-__device__ __forceinline__ void cp16(float* dst, const float* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-               "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void copies_wait() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
-// n4 float4 from src (16-byte aligned) to dst, all threads of the CTA.
-__device__ __forceinline__ void stage16(float* dst, const float* src, int n4) {
-  for (int e = threadIdx.x; e < n4; e += kT) cp16(dst + 4 * e, src + 4 * e);
+// Dynamic shared memory of the kernel. The per-block steps below address it by float
+// offsets (never through pointers held in arrays), so every access is a shared-memory
+// instruction.
+extern __shared__ __align__(16) float smem[];
+
+__device__ __forceinline__ float4 lds4(int off) { return *reinterpret_cast<const float4*>(&smem[off]); }
+
+// The weights of every layer stay in shared memory for the whole step of the CTA, W_l
+// [d_l x d_{l+1}] row-major with its own width as the row stride. A hidden layer's rows
+// (width a multiple of 32) are XOR-swizzled in 16-byte chunks: W[k][c] sits at column
+// c ^ ((k & 7) << 2) of row k, so a row read across consecutive columns (the forward) and
+// a float4 read of consecutive rows at one column chunk (dX) both hit distinct banks, and
+// every 16-byte chunk stays contiguous for cp.async. The output layer (width 9 or 1, odd)
+// is stored as it is: a column read by consecutive rows is conflict-free. The first
+// layer's weights are padded with zero rows to 32 (the input rows are 32 wide, zero past
+// d0). The biases follow, each padded to a multiple of 4.
+__host__ __device__ inline int wrows(int l, int k) { return l == 0 ? 32 : k; }
+__device__ __forceinline__ int swz(int k, int c) { return c ^ ((k & 7) << 2); }
+
+// Register tiles of the row-block products. A warp owns TR rows (r = h + rg i, one row
+// group h per warp, so the row operands are shared-memory broadcasts) and 32 TC columns
+// (c = 32 TC g + lane + 32 j, consecutive lanes on consecutive columns, so the weight
+// reads are conflict-free). Per 4 steps along the reduction a warp reads TR float4 row
+// operands and 4 TC weights for 16 TR TC FMAs: shared-memory wavefronts, one per cycle
+// per SM, bound these steps, and the tile shape is chosen to need the fewest.
+struct Tile {
+  int tr, tc;
+};
+
+// The tile of an [R x N] output (N % 32 == 0) with the fewest wavefronts per step.
+__device__ __forceinline__ Tile pick_tile(int R, int N) {
+  Tile best{0, 0};
+  int cost = 1 << 30;
+  for (int tc = 1; tc <= 2; tc *= 2) {
+    if (N % (32 * tc) != 0) continue;
+    const int cg = N / (32 * tc);
+    if (cg > kW) continue;
+    const int rg = kW / cg;
+    int tr = (R + rg - 1) / rg;
+    tr = tr <= 1 ? 1 : tr <= 2 ? 2 : tr <= 4 ? 4 : tr <= 8 ? 8 : tr <= 16 ? 16 : 32;
+    if (tc == 2 && (tr < 4 || tr > 16)) continue;   // instantiated: (1|2|4|8|16|32, 1), (4|8|16, 2)
+    const int c = (cg * rg) * (tr + 4 * tc);
+    if (c < cost) {
+      cost = c;
+      best = Tile{tr, tc};
+    }
+  }
+  return best;
 }
 
-// out[R x N] = relu(in[R x K] W[K x N] + b) (in: stride ks; out: stride N), N % 32 == 0;
-// also to gout (the activation cache in global memory, stride N) when given. W comes into
-// shared memory (ws, wcap floats) a chunk of whole rows at a time, every thread issuing its
-// share of the 16-byte loads before any is used.
-__device__ void block_forward(const float* in, int ks, int K, const float* W, const float* b, int N, float* out,
-                              float* gout, int R, float* ws, int wcap) {
-  const int cg = N / 4, rg = kT / cg, t = threadIdx.x;
-  const int c = 4 * (t % cg), r0 = t / cg;
-  const bool active = r0 < rg;   // threads past the last full row group (256 % cg != 0) only stage
-  constexpr int kMaxRows = kR / 4;
-  float acc[kMaxRows][4] = {};
-  const int nr = active ? (R - r0 + rg - 1) / rg : 0;   // rows r0, r0 + rg, ... of this thread
-  const int rc = max(4, min(K, wcap / N) & ~3);   // W rows per chunk
-  for (int kc = 0; kc < K; kc += rc) {
-    const int kn = min(rc, K - kc);
-    __syncthreads();   // the previous chunk's readers are done
-    stage16(ws, W + (int64_t)kc * N, kn * N / 4);
-    copies_wait();
-    __syncthreads();
-    for (int k = 0; k < kn; ++k) {
-      const float4 w = *reinterpret_cast<const float4*>(ws + k * N + c);
+// out[R x N] = relu(in[R x K] W[K x N] + b) (in: stride ks, K % 4 == 0; out: stride N,
+// N % 32 == 0), also to gout (the activation cache, stride N) when given.
+template <int TR, int TC>
+__device__ __noinline__ void block_forward_t(int in, int ks, int K, int w, int b, int N, int out, float* gout,
+                                             int R) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cg = N / (32 * TC), rg = kW / cg;
+  if (warp >= cg * rg) return;
+  const int g = warp % cg, h = warp / cg;
+  const int c0 = 32 * TC * g + lane;
+  float acc[TR][TC];
 #pragma unroll
-      for (int j = 0; j < kMaxRows; ++j) {
-        if (j >= nr) break;
-        const float a = in[(r0 + j * rg) * ks + kc + k];
-        acc[j][0] = fmaf(a, w.x, acc[j][0]);
-        acc[j][1] = fmaf(a, w.y, acc[j][1]);
-        acc[j][2] = fmaf(a, w.z, acc[j][2]);
-        acc[j][3] = fmaf(a, w.w, acc[j][3]);
+  for (int i = 0; i < TR; ++i)
+#pragma unroll
+    for (int j = 0; j < TC; ++j) acc[i][j] = 0.f;
+#pragma unroll 2
+  for (int k = 0; k < K; k += 4) {
+    float wv[4][TC];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int j = 0; j < TC; ++j) wv[u][j] = smem[w + (k + u) * N + swz(k + u, c0 + 32 * j)];
+    float4 x[TR];   // rows past R read the block's unused buffer rows; never stored
+#pragma unroll
+    for (int i = 0; i < TR; ++i) x[i] = lds4(in + (h + rg * i) * ks + k);
+#pragma unroll
+    for (int i = 0; i < TR; ++i)
+#pragma unroll
+      for (int j = 0; j < TC; ++j) {
+        float s = acc[i][j];
+        s = fmaf(x[i].x, wv[0][j], s);
+        s = fmaf(x[i].y, wv[1][j], s);
+        s = fmaf(x[i].z, wv[2][j], s);
+        s = fmaf(x[i].w, wv[3][j], s);
+        acc[i][j] = s;
+      }
+  }
+#pragma unroll
+  for (int j = 0; j < TC; ++j) {
+    const int c = c0 + 32 * j;
+    const float bb = smem[b + c];
+#pragma unroll
+    for (int i = 0; i < TR; ++i) {
+      const int r = h + rg * i;
+      if (r < R) {
+        const float y = fmaxf(acc[i][j] + bb, 0.f);
+        smem[out + r * N + c] = y;
+        if (gout) __stcg(gout + (int64_t)r * N + c, y);
       }
     }
   }
-  if (!active) return;
-  const float4 bb = *reinterpret_cast<const float4*>(b + c);
-#pragma unroll
-  for (int j = 0; j < kMaxRows; ++j) {
-    if (j >= nr) break;
-    const int r = r0 + j * rg;
-    float4 y;
-    y.x = fmaxf(acc[j][0] + bb.x, 0.f);
-    y.y = fmaxf(acc[j][1] + bb.y, 0.f);
-    y.z = fmaxf(acc[j][2] + bb.z, 0.f);
-    y.w = fmaxf(acc[j][3] + bb.w, 0.f);
-    *reinterpret_cast<float4*>(out + r * N + c) = y;
-    if (gout) __stcg(reinterpret_cast<float4*>(gout + (int64_t)r * N + c), y);
-  }
 }
 
-// out[R x K] = (dz[R x N] W[K x N]^T) * [act > 0] (dz: stride zs; act, out: stride K),
-// K % 32 == 0 (a hidden width), N any (9 or 1 for the last layer). W comes into shared
-// memory transposed, a chunk of its columns at a time: wt[n][k], row stride K + 4.
-__device__ void block_dx(const float* dz, int zs, int N, const float* W, int K, const float* act, float* out,
-                         int R, float* wt, int wcap) {
-  const int cg = K / 4, rg = kT / cg, t = threadIdx.x;
-  const int c = 4 * (t % cg), r0 = t / cg;
-  const bool active = r0 < rg;
-  constexpr int kMaxRows = kR / 4;
-  float acc[kMaxRows][4] = {};
-  const int nr = active ? (R - r0 + rg - 1) / rg : 0;
-  const int ws = K + 4;
-  const int nc = max(1, min(N, wcap / ws));   // W columns per chunk
-  for (int n0 = 0; n0 < N; n0 += nc) {
-    const int nn = min(nc, N - n0);
-    __syncthreads();
-    // 8 loads in flight per thread, then their transposed stores
-    for (int e0 = t; e0 < K * nn; e0 += 8 * kT) {
-      float v[8];
+// out[R x K] = (dz[R x N] W[K x N]^T) * [act > 0] (dz: stride zs, a multiple of 4; act,
+// out: stride K, K % 32 == 0); the columns of the tile are rows of W.
+template <int TR, int TC>
+__device__ __noinline__ void block_dx_t(int dz, int zs, int N, int w, int K, int act, int out, int R) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int cg = K / (32 * TC), rg = kW / cg;
+  if (warp >= cg * rg) return;
+  const int g = warp % cg, h = warp / cg;
+  const int c0 = 32 * TC * g + lane;
+  float acc[TR][TC];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int e = e0 + u * kT;
-        if (e < K * nn) {
-          const int k = e / nn, n = e - k * nn;
-          v[u] = W[(int64_t)k * N + n0 + n];
+  for (int i = 0; i < TR; ++i)
+#pragma unroll
+    for (int j = 0; j < TC; ++j) acc[i][j] = 0.f;
+  if (N % 32 == 0) {   // swizzled rows: one float4 of each of the TC rows per 4 n
+#pragma unroll 2
+    for (int n = 0; n < N; n += 4) {
+      float4 wv[TC];
+#pragma unroll
+      for (int j = 0; j < TC; ++j) {
+        const int c = c0 + 32 * j;
+        wv[j] = lds4(w + c * N + swz(c, n));
+      }
+      float4 z[TR];   // rows past R read the block's unused buffer rows; never stored
+#pragma unroll
+      for (int i = 0; i < TR; ++i) z[i] = lds4(dz + (h + rg * i) * zs + n);
+#pragma unroll
+      for (int i = 0; i < TR; ++i)
+#pragma unroll
+        for (int j = 0; j < TC; ++j) {
+          float s = acc[i][j];
+          s = fmaf(z[i].x, wv[j].x, s);
+          s = fmaf(z[i].y, wv[j].y, s);
+          s = fmaf(z[i].z, wv[j].z, s);
+          s = fmaf(z[i].w, wv[j].w, s);
+          acc[i][j] = s;
         }
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int e = e0 + u * kT;
-        if (e < K * nn) {
-          const int k = e / nn, n = e - k * nn;
-          wt[n * ws + k] = v[u];
-        }
-      }
     }
-    __syncthreads();
-    for (int n = 0; n < nn; ++n) {
-      const float4 w = *reinterpret_cast<const float4*>(wt + n * ws + c);
+  } else {   // the output layer, stored as it is (odd width)
+    for (int n = 0; n < N; ++n) {
+      float wv[TC];
 #pragma unroll
-      for (int j = 0; j < kMaxRows; ++j) {
-        if (j >= nr) break;
-        const float z = dz[(r0 + j * rg) * zs + n0 + n];
-        acc[j][0] = fmaf(z, w.x, acc[j][0]);
-        acc[j][1] = fmaf(z, w.y, acc[j][1]);
-        acc[j][2] = fmaf(z, w.z, acc[j][2]);
-        acc[j][3] = fmaf(z, w.w, acc[j][3]);
-      }
+      for (int j = 0; j < TC; ++j) wv[j] = smem[w + (c0 + 32 * j) * N + n];
+      float zv[TR];
+#pragma unroll
+      for (int i = 0; i < TR; ++i) zv[i] = smem[dz + (h + rg * i) * zs + n];
+#pragma unroll
+      for (int i = 0; i < TR; ++i)
+#pragma unroll
+        for (int j = 0; j < TC; ++j) acc[i][j] = fmaf(zv[i], wv[j], acc[i][j]);
     }
   }
-  if (!active) return;
 #pragma unroll
-  for (int j = 0; j < kMaxRows; ++j) {
-    if (j >= nr) break;
-    const int r = r0 + j * rg;
-    const float4 m = *reinterpret_cast<const float4*>(act + r * K + c);
-    float4 y;
-    y.x = m.x > 0.f ? acc[j][0] : 0.f;
-    y.y = m.y > 0.f ? acc[j][1] : 0.f;
-    y.z = m.z > 0.f ? acc[j][2] : 0.f;
-    y.w = m.w > 0.f ? acc[j][3] : 0.f;
-    *reinterpret_cast<float4*>(out + r * K + c) = y;
+  for (int j = 0; j < TC; ++j) {
+    const int c = c0 + 32 * j;
+#pragma unroll
+    for (int i = 0; i < TR; ++i) {
+      const int r = h + rg * i;
+      if (r < R) smem[out + r * K + c] = smem[act + r * K + c] > 0.f ? acc[i][j] : 0.f;
+    }
   }
 }
 
-// pw[K x N] (+)= in[R x K]^T dz[R x N] and pb[N] (+)= sum of the rows of dz, over this
-// block's R rows (in: stride ks >= pad4(K), zero past K; dz: stride zs >= pad4(N)).
-__device__ void block_dw(const float* in, int ks, int K, const float* dz, int zs, int N, int R, float* pw,
-                         float* pb, bool first) {
-  const int gk = (K + 3) / 4, gn = (N + 3) / 4;
-  for (int gi = threadIdx.x; gi < gk * gn; gi += kT) {
-    const int k0 = 4 * (gi / gn), n0 = 4 * (gi % gn);
-    float acc[4][4] = {};
+#define SPO_TILE_DISPATCH(FN, ...)                          \
+  do {                                                      \
+    const int key_ = t.tc * 100 + t.tr;                     \
+    switch (key_) {                                         \
+      case 101: FN<1, 1>(__VA_ARGS__); break;               \
+      case 102: FN<2, 1>(__VA_ARGS__); break;               \
+      case 104: FN<4, 1>(__VA_ARGS__); break;               \
+      case 108: FN<8, 1>(__VA_ARGS__); break;               \
+      case 116: FN<16, 1>(__VA_ARGS__); break;              \
+      case 132: FN<32, 1>(__VA_ARGS__); break;              \
+      case 204: FN<4, 2>(__VA_ARGS__); break;               \
+      case 208: FN<8, 2>(__VA_ARGS__); break;               \
+      case 216: FN<16, 2>(__VA_ARGS__); break;              \
+      default: break;                                       \
+    }                                                       \
+  } while (0)
+
+__device__ void block_forward(int in, int ks, int K, int w, int b, int N, int out, float* gout, int R) {
+  const Tile t = pick_tile(R, N);
+  SPO_TILE_DISPATCH(block_forward_t, in, ks, K, w, b, N, out, gout, R);
+}
+
+__device__ void block_dx(int dz, int zs, int N, int w, int K, int act, int out, int R) {
+  const Tile t = pick_tile(R, K);
+  SPO_TILE_DISPATCH(block_dx_t, dz, zs, N, w, K, act, out, R);
+}
+
+// pw[K x N] (+)= in[R x K]^T dz[R x N] and pb[N] (+)= sum of the rows of dz over this
+// block's R rows (in: stride ks, zero past K up to a multiple of 4; dz: stride zs).
+// N % 32 == 0: warp w owns the rows k = 4w + 4 kW i + q (q < 4, i < KI), lane the column
+// lane + 32j; per row of the block, KI broadcast float4 of in and one dz feed 4 KI FMAs,
+// and the partials are stored coalesced.
+template <int KI>
+__device__ __noinline__ void block_dw_t(int in, int ks, int K, int dz, int zs, int N, int R, float* pw, float* pb,
+                                        bool first) {   // pb null: no bias gradient
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int cb = 0; cb < N; cb += 128) {   // 4 columns per lane: c = cb + lane + 32 j
+    const int nj = min(4, (N - cb) >> 5);
+    const int c0 = cb + lane;
+    float acc[KI][4][4];
+#pragma unroll
+    for (int i = 0; i < KI; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][q][j] = 0.f;
+    float db[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
     for (int r = 0; r < R; ++r) {
-      const float4 a = *reinterpret_cast<const float4*>(in + r * ks + k0);
-      const float4 z = *reinterpret_cast<const float4*>(dz + r * zs + n0);
-      const float av[4] = {a.x, a.y, a.z, a.w}, zv[4] = {z.x, z.y, z.z, z.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], zv[j], acc[i][j]);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (k0 + i >= K) break;
+      float z[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (n0 + j >= N) break;
-        float* p = pw + (int64_t)(k0 + i) * N + n0 + j;
-        __stcg(p, first ? acc[i][j] : ldcg(p) + acc[i][j]);
+        z[j] = j < nj ? smem[dz + r * zs + c0 + 32 * j] : 0.f;
+        db[j] += z[j];
+      }
+#pragma unroll
+      for (int i = 0; i < KI; ++i) {
+        const float4 a = lds4(in + r * ks + 4 * warp + 4 * kW * i);
+        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][q][j] = fmaf(av[q], z[j], acc[i][q][j]);
       }
     }
-  }
-  for (int n = threadIdx.x; n < N; n += kT) {
-    float s = 0.f;
-    for (int r = 0; r < R; ++r) s += dz[r * zs + n];
-    __stcg(pb + n, first ? s : ldcg(pb + n) + s);
+    if (first) {   // stores only: no load may sit in front of them
+#pragma unroll
+      for (int i = 0; i < KI; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int k = 4 * warp + 4 * kW * i + q;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (k < K && j < nj) __stcg(pw + (int64_t)k * N + c0 + 32 * j, acc[i][q][j]);
+        }
+      if (warp == 0 && pb)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (j < nj) __stcg(pb + c0 + 32 * j, db[j]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < KI; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int k = 4 * warp + 4 * kW * i + q;
+          float old[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            old[j] = (k < K && j < nj) ? ldcg(pw + (int64_t)k * N + c0 + 32 * j) : 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (k < K && j < nj) __stcg(pw + (int64_t)k * N + c0 + 32 * j, old[j] + acc[i][q][j]);
+        }
+      if (warp == 0 && pb)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (j < nj) __stcg(pb + c0 + 32 * j, ldcg(pb + c0 + 32 * j) + db[j]);
+    }
   }
 }
 
-// Logits / V of rows [0, R) of the block, the row losses and dz (into dz, stride zs); the
-// statistics accumulate in st (lane 0 of each warp).
-__device__ void block_loss(const SmallStepParams& P, const SmallNet& n, const float* act, int64_t row0, int R,
-                           float* dz, int zs, const float* W, float (&st)[kStats]) {
-  const int L = n.L, H = n.dims[L - 1], A = n.dims[L];   // W: the last layer's [H x A] in shared memory
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bool actor = n.mode == 0;
-  const float alpha = (actor && P.z_old) ? softplus_f(*P.log_alpha) : 0.f;
-  const bool valid = lane < A;
-  const float bias = valid ? n.b[L - 1][lane] : 0.f;
-  for (int r = warp; r < R; r += kW) {
-    const int64_t row = row0 + r;
-    float part[kSmallMaxA] = {};
-    for (int h = lane; h < H; h += 32) {
-      const float a = act[r * H + h];
+// The output layer (N <= kSmallMaxA): thread t owns row k = t of dW and all N columns.
+__device__ __noinline__ void block_dw_out(int in, int ks, int K, int dz, int zs, int N, int R, float* pw, float* pb,
+                                          bool first) {
+  for (int k = threadIdx.x; k < K; k += kT) {
+    float acc[kSmallMaxA] = {};
+#pragma unroll 4
+    for (int r = 0; r < R; ++r) {
+      const float a = smem[in + r * ks + k];
+      float z[kSmallMaxA];   // dz rows are zero past N up to their stride (a multiple of 4 >= N)
+#pragma unroll
+      for (int j = 0; j < kSmallMaxA; ++j) z[j] = j < zs ? smem[dz + r * zs + j] : 0.f;
+#pragma unroll
+      for (int j = 0; j < kSmallMaxA; ++j) acc[j] = fmaf(a, z[j], acc[j]);
+    }
+    float* p = pw + (int64_t)k * N;
+    if (first) {
 #pragma unroll
       for (int j = 0; j < kSmallMaxA; ++j)
-        if (j < A) part[j] = fmaf(a, W[h * A + j], part[j]);
+        if (j < N) __stcg(p + j, acc[j]);
+    } else {
+      float old[kSmallMaxA];
+#pragma unroll
+      for (int j = 0; j < kSmallMaxA; ++j) old[j] = j < N ? ldcg(p + j) : 0.f;
+#pragma unroll
+      for (int j = 0; j < kSmallMaxA; ++j)
+        if (j < N) __stcg(p + j, old[j] + acc[j]);
+    }
+  }
+  for (int j = threadIdx.x; j < N; j += kT) {
+    float s = 0.f;
+    for (int r = 0; r < R; ++r) s += smem[dz + r * zs + j];
+    if (first)
+      __stcg(pb + j, s);
+    else
+      __stcg(pb + j, ldcg(pb + j) + s);
+  }
+}
+
+__device__ void block_dw(int in, int ks, int K, int dz, int zs, int N, int R, float* pw, float* pb, bool first) {
+  if (N % 32 != 0) {
+    block_dw_out(in, ks, K, dz, zs, N, R, pw, pb, first);
+    return;
+  }
+  for (int k0 = 0; k0 < K; k0 += 128) {   // 128 rows of dW per pass
+    float* w0 = pw + (int64_t)k0 * N;
+    float* b0 = k0 == 0 ? pb : nullptr;
+    switch (min(128 / (4 * kW), (K - k0 + 4 * kW - 1) / (4 * kW))) {
+      case 1: block_dw_t<1>(in + k0, ks, K - k0, dz, zs, N, R, w0, b0, first); break;
+      case 2: block_dw_t<2>(in + k0, ks, K - k0, dz, zs, N, R, w0, b0, first); break;
+      case 3: block_dw_t<3>(in + k0, ks, K - k0, dz, zs, N, R, w0, b0, first); break;
+      default: block_dw_t<4>(in + k0, ks, K - k0, dz, zs, N, R, w0, b0, first); break;
+    }
+  }
+}
+
+// Logits / V of rows [0, R) of the block (act: [R x H]; W: the output layer [H x A], b its
+// bias), the row losses and dz (stride zs). The per-row inputs come from shared memory (li:
+// mask or cells, q, pi_old logits, 9 each; the critic's target in the first column). Lane
+// 0 of warp w adds the statistics of its rows to stw[w][..].
+__device__ __noinline__ void block_loss(const SmallStepParams& P, bool actor, int H, int A, int act, int li, int R,
+                                        int dz, int zs, int w, int b, float alpha, int stw) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool valid = lane < A;
+  const float bias = valid ? smem[b + lane] : 0.f;
+  float st[kStats] = {};
+  for (int r = warp; r < R; r += kW) {
+    const int in_r = li + r * kLossIn;
+    float part[kSmallMaxA] = {};
+    for (int h = lane; h < H; h += 32) {
+      const float a = smem[act + r * H + h];
+#pragma unroll
+      for (int j = 0; j < kSmallMaxA; ++j)
+        if (j < A) part[j] = fmaf(a, smem[w + h * A + j], part[j]);
     }
     float z = 0.f;
 #pragma unroll
@@ -286,15 +475,15 @@ __device__ void block_loss(const SmallStepParams& P, const SmallNet& n, const fl
     }
     z += bias;
     if (!actor) {
-      const float d = z - P.target[row];   // meaningful in lane 0
-      if (lane < zs) dz[r * zs + lane] = lane == 0 ? d * P.scale : 0.f;
-      if (lane == 0) st[kStatCriticLoss] += 0.5f * d * d * P.scale;
+      const float d = z - smem[in_r];   // meaningful in lane 0
+      if (lane < zs) smem[dz + r * zs + lane] = lane == 0 ? d * P.scale : 0.f;
+      st[kStatCriticLoss] += 0.5f * d * d * P.scale;
       continue;
     }
-    const int64_t o = row * A + lane;
-    const float mk = valid ? (P.mask ? P.mask[o] : (P.cells[row * 9 + lane] == 0.f ? 1.f : 0.f)) : 0.f;
+    const float m_in = valid ? smem[in_r + lane] : 0.f;
+    const float mk = valid ? (P.mask ? m_in : (m_in == 0.f ? 1.f : 0.f)) : 0.f;
     const bool legal = valid && mk != 0.f;
-    const float qv = valid ? P.q[o] : 0.f;
+    const float qv = valid ? smem[in_r + 9 + lane] : 0.f;
     const float zm = legal ? z : kNegInf;
     const float mx = warp_max(zm);
     const float e = valid ? expf(zm - mx) : 0.f;
@@ -303,7 +492,7 @@ __device__ void block_loss(const SmallStepParams& P, const SmallNet& n, const fl
     const float lp = zm - (mx + logf(s));
     float po = 0.f, klo_t = 0.f;
     if (P.z_old) {
-      const float zo = legal ? P.z_old[o] : kNegInf;
+      const float zo = legal ? smem[in_r + 18 + lane] : kNegInf;
       const float mxo = warp_max(zo);
       const float eo = valid ? expf(zo - mxo) : 0.f;
       const float so = warp_sum(eo);
@@ -313,54 +502,115 @@ __device__ void block_loss(const SmallStepParams& P, const SmallNet& n, const fl
     const float ce = warp_sum((valid && qv != 0.f) ? -qv * lp : 0.f);
     const float hq = warp_sum((valid && qv > 0.f) ? -qv * logf(qv) : 0.f);
     const float klo = warp_sum(klo_t);
-    if (lane < zs) dz[r * zs + lane] = legal ? ((pi - qv) + alpha * (pi - po)) * P.scale : 0.f;
-    if (lane == 0) {
-      st[kStatActorLoss] += (ce + alpha * klo) * P.scale;
-      st[kStatCE] += ce * P.scale;
-      st[kStatEntropy] += hq * P.scale;
-      st[kStatKLq] += (ce - hq) * P.scale;
-      st[kStatKLold] += klo * P.scale;
-    }
+    if (lane < zs) smem[dz + r * zs + lane] = legal ? ((pi - qv) + alpha * (pi - po)) * P.scale : 0.f;
+    st[kStatActorLoss] += (ce + alpha * klo) * P.scale;
+    st[kStatCE] += ce * P.scale;
+    st[kStatEntropy] += hq * P.scale;
+    st[kStatKLq] += (ce - hq) * P.scale;
+    st[kStatKLold] += klo * P.scale;
   }
+  if (lane == 0)
+#pragma unroll
+    for (int k = 0; k < kStats; ++k) smem[stw + warp * kStats + k] += st[k];
 }
 
-// Shared memory of one network's row block, in floats: x [kR x 32] | a_0 .. a_{L-2}
-// [kR x d_{l+1}] | dz ping-pong 2 x [kR x dmax] | the last layer's W [H x A] | a weight
-// staging area (the rest, up to kSmallMaxSmem).
-__host__ __device__ inline int small_base_floats(const int* dims, int L) {
-  int f = kR * 32, dmax = (dims[L] + 3) & ~3;
-  for (int l = 1; l < L; ++l) {
-    f += kR * dims[l];
-    dmax = dims[l] > dmax ? dims[l] : dmax;
+// Shared memory of one network's row block, in floats: x [kR x 32] | loss inputs
+// [kR x kLossIn] | per-warp statistics [kW x kStats] | a_0 .. a_{L-2} [kR x d_{l+1}] |
+// dz ping-pong 2 x [kR x dmax] | W_0 .. W_{L-1} [wrows x d_{l+1}] | b_0 .. b_{L-1}
+// [pad4(d_{l+1})]; every region starts on a 16-byte boundary.
+__host__ __device__ inline int small_dmax(const int* dims, int L) {
+  int dmax = (dims[L] + 3) & ~3;
+  for (int l = 1; l < L; ++l) dmax = dims[l] > dmax ? dims[l] : dmax;
+  return dmax;
+}
+__host__ __device__ inline int small_acts_base() { return kR * 32 + kR * kLossIn + kW * kStats; }
+__host__ __device__ inline int small_w_base(const int* dims, int L) {
+  int f = small_acts_base();
+  for (int l = 1; l < L; ++l) f += kR * dims[l];
+  return f + 2 * kR * small_dmax(dims, L);
+}
+__host__ __device__ inline int small_smem_floats(const int* dims, int L) {
+  int f = small_w_base(dims, L);
+  for (int l = 0; l < L; ++l) f += wrows(l, dims[l]) * dims[l + 1] + ((dims[l + 1] + 3) & ~3);
+  return f;
+}
+
+__device__ __forceinline__ void cp4(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cp16(int dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(&smem[dst]))),
+               "l"(src)
+               : "memory");
+}
+
+// Every layer's weights (at wbase, the layout above) and biases (at bbase) into shared
+// memory: asynchronous 16-byte copies, all in flight at once (waited for by the caller);
+// the first layer's padding rows zeroed.
+__device__ void stage_weights(const SmallNet& n, int wbase, int bbase) {
+  int w = wbase, b = bbase;
+  for (int l = 0; l < n.L; ++l) {
+    const int K = n.dims[l], N = n.dims[l + 1];
+    const int n4 = K * N / 4;
+    const float* src = n.W[l];
+    // each CTA starts at its own offset, so that the CTAs do not all ask the same L2
+    // lines at the same time
+    const int rot = (int)(((int64_t)blockIdx.x * 1031) % n4);
+    for (int t = threadIdx.x; t < n4; t += kT) {
+      const int g = t + rot < n4 ? t + rot : t + rot - n4;
+      const int e = 4 * g;
+      if (N % 32 == 0) {
+        const int k = e / N, c = e - k * N;
+        cp16(w + k * N + swz(k, c), src + e);
+      } else {
+        cp16(w + e, src + e);
+      }
+    }
+    for (int e = K * N + threadIdx.x; e < wrows(l, K) * N; e += kT) smem[w + e] = 0.f;
+    const int nb = (N + 3) & ~3;   // the flat parameter buffer pads every tensor to 64 floats
+    for (int g = threadIdx.x; g < nb / 4; g += kT) cp16(b + 4 * g, n.b[l] + 4 * g);
+    w += wrows(l, K) * N;
+    b += nb;
   }
-  return f + 2 * kR * dmax + ((dims[L - 1] * dims[L] + 3) & ~3);
 }
 
 // One network over this CTA's rows [rb, re), 32 rows at a time.
-__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re, float* sm,
-                         float* red) {
+__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re) {
   const int L = n.L, d0 = n.dims[0];
   const int part = blockIdx.x;
-  float* xs = sm;
-  float* acts[kSmallMaxLayers - 1];
-  float* p = xs + kR * 32;
-  int dmax = pad4(n.dims[L]);
-  for (int l = 0; l + 1 < L; ++l) {
-    acts[l] = p;
-    p += kR * n.dims[l + 1];
-    dmax = max(dmax, n.dims[l + 1]);
-  }
-  float* dzb[2] = {p, p + kR * dmax};
-  float* hw = p + 2 * kR * dmax;
-  float* ws = hw + pad4(n.dims[L - 1] * n.dims[L]);
-  const int wcap = (int)(kSmallMaxSmem / sizeof(float)) - small_base_floats(n.dims, L);
-  // the last layer's W: H x A floats, a multiple of 4 (H % 32 == 0), 16-byte aligned
-  stage16(hw, n.W[L - 1], n.dims[L - 1] * n.dims[L] / 4);
-  copies_wait();
-  float st[kStats] = {};
+  const bool actor = n.mode == 0;
+  const int xs = 0, li = kR * 32, stw = li + kR * kLossIn, acts0 = small_acts_base();
+  const int dmax = small_dmax(n.dims, L);
+  int dzb0 = acts0;
+  for (int l = 1; l < L; ++l) dzb0 += kR * n.dims[l];
+  const int wbase = small_w_base(n.dims, L);
+  int bbase = wbase;
+  for (int l = 0; l < L; ++l) bbase += wrows(l, n.dims[l]) * n.dims[l + 1];
+  const float alpha = (actor && P.z_old) ? softplus_f(*P.log_alpha) : 0.f;
+  for (int e = threadIdx.x; e < kW * kStats; e += kT) smem[stw + e] = 0.f;
   bool first = true;
   for (int64_t r0 = rb; r0 < re; r0 += kR, first = false) {
     const int R = (int)min((int64_t)kR, re - r0);
+    // the loss inputs of the block's rows, asynchronously (waited for before the loss)
+    for (int e = threadIdx.x; e < R * kLossIn; e += kT) {
+      const int r = e / kLossIn, f = e - r * kLossIn;
+      const int64_t row = r0 + r;
+      const float* src = nullptr;
+      if (!actor) {
+        if (f == 0) src = P.target + row;
+      } else if (f < 9) {
+        src = P.mask ? P.mask + row * 9 + f : P.cells + row * 9 + f;
+      } else if (f < 18) {
+        src = P.q + row * 9 + (f - 9);
+      } else if (f < 27 && P.z_old) {
+        src = P.z_old + row * 9 + (f - 18);
+      }
+      if (src) cp4(&smem[li + e], src);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     // input rows (zero past d0); board cells expand to the plane-major planes
     {
       float v[kR * 32 / kT];   // this thread's 4 input values, loaded together
@@ -381,40 +631,59 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
           const int plane = f / 9;
           x = (plane == 0 ? x == 0.f : (plane == 1 ? x == 1.f : x == -1.f)) ? 1.f : 0.f;
         }
-        xs[e] = x;
+        smem[xs + e] = x;
       }
     }
+    if (first) stage_weights(n, wbase, bbase);
+    SS_MARK(13);
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    for (int l = 0; l + 1 < L; ++l) {
-      block_forward(l == 0 ? xs : acts[l - 1], l == 0 ? 32 : n.dims[l], n.dims[l], n.W[l], n.b[l], n.dims[l + 1],
-                    acts[l], n.gact[l] ? n.gact[l] + r0 * n.dims[l + 1] : nullptr, R, ws, wcap);
+    SS_MARK(1);
+    {
+      int in = xs, ks = 32, a = acts0, w = wbase, b = bbase;
+      for (int l = 0; l + 1 < L; ++l) {
+        const int K = wrows(l, n.dims[l]), N = n.dims[l + 1];
+        block_forward(in, ks, K, w, b, N, a, n.gact[l] ? n.gact[l] + r0 * N : nullptr, R);
+        __syncthreads();
+        in = a;
+        ks = N;
+        a += kR * N;
+        w += K * N;
+        b += (N + 3) & ~3;
+      }
+      SS_MARK(2);
+      // in: the last hidden activations; w, b: the output layer
+      int zs = (n.dims[L] + 3) & ~3;   // row stride of the gradient in the current dz buffer
+      block_loss(P, actor, n.dims[L - 1], n.dims[L], in, li, R, dzb0, zs, w, b, alpha, stw);
       __syncthreads();
+      SS_MARK(3);
+      int cur = 0;
+      for (int l = L - 1; l >= 0; --l) {
+        const int N = n.dims[l + 1], K = l == 0 ? d0 : n.dims[l];
+        const int dz = dzb0 + cur * kR * dmax, dzn = dzb0 + (cur ^ 1) * kR * dmax;
+        const int act_in = l == 0 ? xs : in;   // the input of layer l
+        block_dw(act_in, l == 0 ? 32 : K, K, dz, zs, N, R, n.pw[l] + (int64_t)part * K * N,
+                 n.pb[l] + (int64_t)part * N, first);
+        if (l == 1) SS_SYNC_MARK(12);
+        if (l >= 1) block_dx(dz, zs, N, w, K, act_in, dzn, R);
+        __syncthreads();
+        zs = K;
+        cur ^= 1;
+        if (l >= 1) {   // step back one layer: its weights, its input activations
+          w -= wrows(l - 1, n.dims[l - 1]) * K;
+          in = l - 1 == 0 ? xs : in - kR * n.dims[l - 1];
+        }
+        SS_MARK(9 + l);
+      }
     }
-    int zs = pad4(n.dims[L]);   // row stride of the gradient in dzb[cur]: its layer's width
-    block_loss(P, n, acts[L - 2], r0, R, dzb[0], zs, hw, st);
-    __syncthreads();
-    int cur = 0;
-    for (int l = L - 1; l >= 0; --l) {
-      const float* in = l == 0 ? xs : acts[l - 1];
-      const int ks = l == 0 ? 32 : n.dims[l];
-      block_dw(in, ks, n.dims[l], dzb[cur], zs, n.dims[l + 1], R, n.pw[l] + (int64_t)part * n.dims[l] * n.dims[l + 1],
-               n.pb[l] + (int64_t)part * n.dims[l + 1], first);
-      if (l >= 1) block_dx(dzb[cur], zs, n.dims[l + 1], n.W[l], n.dims[l], acts[l - 1], dzb[cur ^ 1], R, ws, wcap);
-      __syncthreads();
-      zs = n.dims[l];
-      cur ^= 1;
-    }
+    SS_MARK(4);
   }
   // the statistics of this CTA's rows
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0)
-#pragma unroll
-    for (int k = 0; k < kStats; ++k) red[warp * kStats + k] = st[k];
   __syncthreads();
   if (threadIdx.x < kStats) {
     float v = 0.f;
 #pragma unroll
-    for (int w = 0; w < kW; ++w) v += red[w * kStats + threadIdx.x];
+    for (int w = 0; w < kW; ++w) v += smem[stw + w * kStats + threadIdx.x];
     __stcg(n.pstats + (int64_t)part * kStats + threadIdx.x, v);
   }
   __syncthreads();
@@ -427,44 +696,40 @@ __device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, 
   p = p - lr * (m * bc1) / (sqrtf(v * bc2) + eps);
 }
 
-// sum over k < parts of src[k * stride] with 8 loads in flight: part k goes to partial sum
-// k % 8 and the eight are combined in a fixed order (deterministic).
+// sum over k < parts of src[k * stride] with 16 loads in flight: part k goes to partial
+// sum k % 8 and the eight are combined in a fixed order (deterministic).
 __device__ __forceinline__ float sum_parts(const float* src, int parts, int64_t stride) {
   float a[8] = {};
   int k = 0;
-  for (; k + 8 <= parts; k += 8) {
+  for (; k + 16 <= parts; k += 16) {
+    float v[16];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) a[u] += ldcg(src + (int64_t)(k + u) * stride);
+    for (int u = 0; u < 16; ++u) v[u] = ldcg(src + (int64_t)(k + u) * stride);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) a[u & 7] += v[u];
   }
-  for (int u = 0; k < parts; ++k, ++u) a[u] += ldcg(src + (int64_t)k * stride);
+  for (; k < parts; ++k) a[k & 7] += ldcg(src + (int64_t)k * stride);
   return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
 }
 
-// Reduced value of flat element e (the segment it falls in, its parts in order).
-__device__ __forceinline__ float reduced(const SmallStepParams& P, int64_t e, int& si) {
-  while (si + 1 < P.red.nseg && e >= P.seg_start[si + 1]) ++si;
-  const ReduceSeg& sg = P.red.seg[si];
-  const int64_t i = e - P.seg_start[si];
-  return sum_parts(sg.src + i, sg.parts, sg.part_stride);
-}
-
 __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant__ SmallStepParams P) {
-  extern __shared__ __align__(16) float sm[];
-  __shared__ float red[kW * kStats];
   __shared__ float s_clip[kMaxGroups], s_norm[kMaxGroups];
   __shared__ float s_sq[kW];
   unsigned target = 0;
   bool ok = true;
   const AdamParams& ap = P.adam;
 
+  SS_MARK(0);
   // ---- rows: forward, loss, backward; per-CTA partial sums
   if (blockIdx.x < P.parts) {
     const int64_t rb = (int64_t)blockIdx.x * P.rows_per_cta;
     const int64_t re = min(rb + P.rows_per_cta, P.rows);
     for (int i = 0; i < 2; ++i)
-      if (P.net[i].L) net_rows(P, P.net[i], rb, re, sm, red);
+      if (P.net[i].L) net_rows(P, P.net[i], rb, re);
   }
+  SS_MARK(5);
   ok = grid_barrier(target, P);
+  SS_MARK(6);
 
   // ---- partial sums -> flat gradients (each in CTA order), Adam fused per element
   int t_step = 0;
@@ -483,31 +748,42 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
   if (ok) {
     int si = 0;
     for (int64_t e = (int64_t)blockIdx.x * kT + threadIdx.x; e < P.total_red; e += (int64_t)gridDim.x * kT) {
-      const float g = reduced(P, e, si);
-      const int64_t fe = P.flat_index[si] + (e - P.seg_start[si]);   // element of the flat buffers
-      __stcg(P.red.seg[si].dst + (e - P.seg_start[si]), g);
-      if (!fuse || fe < 0) continue;
+      while (si + 1 < P.red.nseg && e >= P.seg_start[si + 1]) ++si;
+      const int64_t i = e - P.seg_start[si];
+      const int64_t fe = P.flat_index[si] + i;   // element of the flat buffers
       int gi = -1;
+      if (fuse && fe >= 0) {
 #pragma unroll
-      for (int k = 0; k < kMaxGroups; ++k)
-        if (k < ap.ngrp && fe >= ap.grp[k].begin && fe < ap.grp[k].end) gi = k;
+        for (int k = 0; k < kMaxGroups; ++k)
+          if (k < ap.ngrp && fe >= ap.grp[k].begin && fe < ap.grp[k].end) gi = k;
+      }
+      // Adam's operands first: their loads overlap the partial sums'
+      float p = 0.f, m = 0.f, v = 0.f;
+      if (gi >= 0) {
+        p = ldcg(ap.p + fe);
+        m = ldcg(ap.m + fe);
+        v = ldcg(ap.v + fe);
+      }
+      const ReduceSeg& sg = P.red.seg[si];
+      const float g = sum_parts(sg.src + i, sg.parts, sg.part_stride);
+      __stcg(sg.dst + i, g);
       if (gi < 0) continue;
       float gv = g;
       if (fe == ap.alpha_index) {
         // dual gradient: sigmoid(log_alpha) * (eps - mean KL(pi_old || pi)), the KL from the
         // actor's per-CTA statistics in the same order as its own reduced slot
         const float kl = sum_parts(P.net[0].pstats + kStatKLold, P.parts, kStats);
-        gv = (1.f / (1.f + expf(-ldcg(ap.p + fe)))) * (ap.kl_eps - kl);
+        gv = (1.f / (1.f + expf(-p))) * (ap.kl_eps - kl);
         __stcg(ap.g + fe, gv);
         if (ap.report) ap.report[kRepDlogAlpha] = gv;
       }
-      float p = ldcg(ap.p + fe), m = ldcg(ap.m + fe), v = ldcg(ap.v + fe);
       adam_one(p, gv, m, v, ap.grp[gi].lr, ap.b1, ap.b2, ap.eps, bc1, bc2);
       __stcg(ap.p + fe, p);
       __stcg(ap.m + fe, m);
       __stcg(ap.v + fe, v);
     }
   }
+  SS_MARK(7);
   // ---- clipped step: global norms of the reduced gradients, then Adam
   if (ok && P.apply && P.clip) {
     ok = grid_barrier(target, P);
@@ -568,6 +844,7 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
   }
   // ---- exit: the last CTA out resets the barrier words (and advances the step)
   __syncthreads();
+  SS_MARK(8);
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(P.sync + 1, 1u);
@@ -594,16 +871,21 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
 
 }  // namespace
 
+#ifdef SPO_SMALL_TRACE
+extern "C" __attribute__((visibility("default"))) int spo_small_trace_read(unsigned long long* host, int n) {
+  return cudaMemcpyFromSymbol(host, small_trace, sizeof(unsigned long long) * std::min(n, 1024 * kTraceMarks)) ==
+                 cudaSuccess
+             ? 0
+             : -5;
+}
+#endif
+
 size_t small_step_smem(const spo_mlp_desc* nets, int count) {
-  // the base of every network plus room to stage at least 4 rows (forward) and 1 column
-  // (dX, stride <= 260) of its weights; the launch takes all kSmallMaxSmem bytes
   size_t most = 0;
   for (int i = 0; i < count; ++i) {
     const spo_mlp_desc& d = nets[i];
     if (d.num_layers < 2) continue;
-    int wneed = 4 * 256;
-    for (int l = 0; l < d.num_layers; ++l) wneed = std::max(wneed, 4 * d.dims[l + 1]);
-    most = std::max(most, (size_t)(small_base_floats(d.dims, d.num_layers) + wneed) * sizeof(float));
+    most = std::max(most, (size_t)small_smem_floats(d.dims, d.num_layers) * sizeof(float));
   }
   return most;
 }

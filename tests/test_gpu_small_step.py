@@ -43,7 +43,7 @@ WLS = {
     "c0": WORKLOADS["c0"],
     "c1": WORKLOADS["c1"],
     "a1": Workload("a1", actor=NetSpec((27, 64, 9)), batch=300),
-    "ac3": Workload("ac3", actor=NetSpec((27, 96, 160, 256, 9)), critic=NetSpec((27, 96, 160, 256, 1)),
+    "ac3": Workload("ac3", actor=NetSpec((27, 96, 160, 64, 9)), critic=NetSpec((27, 96, 160, 64, 1)),
                     batch=1000),
     "clip": Workload("clip", actor=NetSpec((27, 128, 128, 9)), critic=NetSpec((27, 128, 128, 1)),
                      batch=512, max_grad_norm=0.05),
