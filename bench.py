@@ -69,6 +69,9 @@ def parse():
                          "launch-bound workloads)")
     ap.add_argument("--rows", type=int, default=0,
                     help="override the global batch (profiling of small cases only; not a bench line)")
+    ap.add_argument("--roofline-only", type=int, default=0, metavar="ROWS",
+                    help="launch only the roofline kernel at ROWS rows and print its line (for an ncu "
+                         "capture of a small case; not a bench line)")
     ap.add_argument("--peaks", action="store_true",
                     help="measure the tcgen05 TF32 and FP32-FMA peaks of this GPU (not a bench line) and exit")
     return ap.parse_args()
@@ -216,16 +219,20 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
     bb = torch.zeros(H, device=dev)
     y = torch.empty(rows, H, device=dev)
     if engine == "tensor":
-        # as the learner runs it: the activations plain fp32 (split into TF32 halves in shared
-        # memory by the kernel), W^T as a hi/lo pair, fp32 output with its packed ReLU mask
+        # as the learner runs a hidden layer that feeds another: the activations and W^T as
+        # TF32 hi/lo pairs, the output as a hi/lo pair with its packed ReLU mask
+        xh, xl = torch.empty_like(x), torch.empty_like(x)
+        ffi.call("spo_split_tf32", stream.cuda_stream, xh.data_ptr(), xl.data_ptr(), x.data_ptr(), x.numel(), 0)
         wh, wl = torch.empty_like(w), torch.empty_like(w)
         ffi.call("spo_split_tf32", stream.cuda_stream, wh.data_ptr(), wl.data_ptr(), w.data_ptr(), w.numel(), 0)
+        del x
+        yl = torch.empty_like(y)
         bits = torch.empty(rows, H // 32, dtype=torch.int32, device=dev)
-        d = ffi.TcGemmDesc(kind=ffi.TC_FWD, a_hi=x.data_ptr(), a_lo=None, b_hi=wh.data_ptr(),
+        d = ffi.TcGemmDesc(kind=ffi.TC_FWD, a_hi=xh.data_ptr(), a_lo=xl.data_ptr(), b_hi=wh.data_ptr(),
                            b_lo=wl.data_ptr(), m=rows, n=H, k=H, bias=bb.data_ptr(), c_hi=y.data_ptr(),
-                           c_bits=bits.data_ptr())
+                           c_lo=yl.data_ptr(), c_bits=bits.data_ptr())
         launch = lambda: ffi.call("spo_tc_gemm", stream.cuda_stream, ctypes.byref(d))  # noqa: E731
-        name = "tc_gemm_kernel (tcgen05 3xTF32, fp32 operand split on chip), hidden forward %dx%dx%d" % (rows, H, H)
+        name = "tc_gemm_kernel (tcgen05 3xTF32, hi/lo operands), hidden forward %dx%dx%d" % (rows, H, H)
     else:
         launch = lambda: ffi.call("spo_linear_fwd", stream.cuda_stream, y.data_ptr(), x.data_ptr(),  # noqa: E731
                                   w.data_ptr(), bb.data_ptr(), rows, H, H, 1)
@@ -244,8 +251,9 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
     # the kernel is timed alone (back-to-back launches of it): the burst peak applies
     peak = pk.get("bf16_tflops") or pk.get("bf16_tflops_sustained")
     traffic = TRAFFIC_PER_LAUNCH.get((engine, H), {}).get("bytes") if rows == 1048576 else None
-    # fp32 A read once, C written once, its packed mask, W^T as a hi/lo pair, bias
-    fp32_bytes = 4.0 * (2 * rows * H + 2 * H * H + H) + rows * H / 8
+    # the layer's fp32 essentials: A read once, C written once, its packed mask, W, bias (the
+    # kernel moves A and C as TF32 hi/lo pairs: twice these activation bytes)
+    fp32_bytes = 4.0 * (2 * rows * H + H * H + H) + rows * H / 8
     roof = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak,
             "unit": "TFLOP/s", "frac": achieved / peak,
             "peak_kind": f"{kind} bf16 dense, burst (the kernel is timed alone)",
@@ -280,17 +288,31 @@ TC0_MIN_ROWS = 16384  # the library runs the input layer on tensor cores from th
 SMALL_MAX_ROWS = 8192  # batches up to this many rows run as one launch when the shapes fit
 
 
+SMALL_MAX_SMEM_FLOATS = 220 * 1024 // 4  # the one-launch step's shared memory per CTA
+
+
 def small_step_fits(wl, rows):
-    """Whether the library runs this step as its one-launch small-batch step."""
+    """Whether the library runs this step as its one-launch small-batch step: every
+    network's weights, biases and one 32-row block of activations fit in shared memory
+    (the layout of small_step.cu)."""
     if rows < 1 or rows > SMALL_MAX_ROWS:
         return False
+    pad4 = lambda v: (v + 3) // 4 * 4  # noqa: E731
     for net in (wl.actor, wl.critic):
         if net is None:
             continue
-        d = net.dims
-        if not (2 <= net.num_layers <= 4 and d[0] <= 32 and d[-1] in (1, 9)):
+        d = list(net.dims)
+        L = len(d) - 1
+        if not (2 <= L <= 4 and d[0] <= 32 and d[-1] in (1, 9)):
             return False
         if any(h % 32 or h > 256 for h in d[1:-1]):
+            return False
+        if sum(d[i] * d[i + 1] + d[i + 1] for i in range(L)) > 65536:
+            return False
+        dmax = max([pad4(d[-1])] + d[1:-1])
+        f = 32 * 32 + 32 * 28 + 8 * 8 + 32 * sum(d[1:-1]) + 2 * 32 * dmax
+        f += sum((32 if i == 0 else d[i]) * d[i + 1] + pad4(d[i + 1]) for i in range(L))
+        if f > SMALL_MAX_SMEM_FLOATS:
             return False
     return True
 
@@ -589,6 +611,16 @@ def main():
     args = parse()
     if args.peaks:
         return run_peaks()
+    if args.roofline_only:
+        import torch
+        wl = WORKLOADS[args.workload]
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        stream = torch.cuda.Stream(dev)
+        H = (wl.actor or wl.critic).dims[1]
+        print(json.dumps(roofline_hidden_gemm(args, args.roofline_only, H, dev, stream, engine=args.engine,
+                                              reps=2)))
+        return 0
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

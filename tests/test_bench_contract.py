@@ -62,3 +62,15 @@ def test_reference_arm_other_ranks_print_nothing():
                         "--steps", "1", "--warmup", "0"], capture_output=True, text=True, timeout=300, env=env)
     assert r.returncode == 0, r.stderr
     assert r.stdout.strip() == ""
+
+
+def test_small_step_eligibility_follows_the_shared_memory_layout():
+    from spo_mojo_b200.workloads import NetSpec, Workload
+    assert bench.small_step_fits(WORKLOADS["c0"], 256)
+    assert bench.small_step_fits(WORKLOADS["c1"], 4096)
+    assert not bench.small_step_fits(WORKLOADS["c1"], 8193)
+    assert bench.small_step_fits(Workload("ac3", actor=NetSpec((27, 96, 160, 64, 9)),
+                                          critic=NetSpec((27, 96, 160, 64, 1)), batch=1000), 1000)
+    # 27-256-256-9: 82 k weights do not fit beside the activations of a 32-row block
+    assert not bench.small_step_fits(Workload("w", actor=NetSpec((27, 256, 256, 9)), batch=64), 64)
+    assert not bench.small_step_fits(WORKLOADS["c2"], 4096)
