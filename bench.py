@@ -340,7 +340,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
     from spo_mojo_b200 import ffi
-    from spo_mojo_b200.learner import Comm, HostFeed, Learner
+    from spo_mojo_b200.learner import Comm, HostFeed, Learner, PackedHostBatch
 
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
@@ -357,7 +357,8 @@ def run_ours(args):
     rows = B // world
     params = init_params(wl, seed=0)
     batch_np = make_batch(wl, rows, seed=100 + rank)
-    host = {k: torch.from_numpy(v).pin_memory() for k, v in batch_np.items()}
+    # the host batch: every field a view of one pinned buffer (one upload per step)
+    host = PackedHostBatch.of(batch_np)
     batch = {k: v.to(dev) for k, v in host.items()}
     L = Learner.for_workload(wl, max_rows=rows, device=local, engine=args.engine)
     L.load(actor=params.get("actor"), critic=params.get("critic"), log_alpha=wl.log_alpha)
@@ -468,7 +469,7 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         stats_host = torch.empty(ffi.NUM_STATS, dtype=torch.float32).pin_memory()
-        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        h2d = int(host.flat.numel())  # the packed buffer, field padding included
         d2h = stats_host.numel() * 4
         if world > 1:
             dist.barrier()
@@ -483,8 +484,7 @@ def run_ours(args):
             dbuf = feed.bufs[0]
 
             def e2e_step(i):
-                for k, v in host.items():
-                    dbuf[k].copy_(v, non_blocking=True)
+                feed.copy_into(0, host)
                 step(dbuf)
                 stats_host.copy_(L.stats_tensor(), non_blocking=True)
 

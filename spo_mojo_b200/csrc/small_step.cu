@@ -451,8 +451,8 @@ __device__ void block_dw(int in, int ks, int K, int dz, int zs, int N, int R, fl
 // bias), the row losses and dz (stride zs). The per-row inputs come from shared memory (li:
 // mask or cells, q, pi_old logits, 9 each; the critic's target in the first column). Lane
 // 0 of warp w adds the statistics of its rows to stw[w][..].
-__device__ __noinline__ void block_loss(const SmallStepParams& P, bool actor, int H, int A, int act, int li, int R,
-                                        int dz, int zs, int w, int b, float alpha, int stw) {
+__device__ __noinline__ void block_loss(bool actor, bool has_mask, bool has_old, float scale, int H, int A, int act,
+                                        int li, int R, int dz, int zs, int w, int b, float alpha, int stw) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool valid = lane < A;
   const float bias = valid ? smem[b + lane] : 0.f;
@@ -476,12 +476,12 @@ __device__ __noinline__ void block_loss(const SmallStepParams& P, bool actor, in
     z += bias;
     if (!actor) {
       const float d = z - smem[in_r];   // meaningful in lane 0
-      if (lane < zs) smem[dz + r * zs + lane] = lane == 0 ? d * P.scale : 0.f;
-      st[kStatCriticLoss] += 0.5f * d * d * P.scale;
+      if (lane < zs) smem[dz + r * zs + lane] = lane == 0 ? d * scale : 0.f;
+      st[kStatCriticLoss] += 0.5f * d * d * scale;
       continue;
     }
     const float m_in = valid ? smem[in_r + lane] : 0.f;
-    const float mk = valid ? (P.mask ? m_in : (m_in == 0.f ? 1.f : 0.f)) : 0.f;
+    const float mk = valid ? (has_mask ? m_in : (m_in == 0.f ? 1.f : 0.f)) : 0.f;
     const bool legal = valid && mk != 0.f;
     const float qv = valid ? smem[in_r + 9 + lane] : 0.f;
     const float zm = legal ? z : kNegInf;
@@ -491,7 +491,7 @@ __device__ __noinline__ void block_loss(const SmallStepParams& P, bool actor, in
     const float pi = e * (1.f / s);
     const float lp = zm - (mx + logf(s));
     float po = 0.f, klo_t = 0.f;
-    if (P.z_old) {
+    if (has_old) {
       const float zo = legal ? smem[in_r + 18 + lane] : kNegInf;
       const float mxo = warp_max(zo);
       const float eo = valid ? expf(zo - mxo) : 0.f;
@@ -502,12 +502,12 @@ __device__ __noinline__ void block_loss(const SmallStepParams& P, bool actor, in
     const float ce = warp_sum((valid && qv != 0.f) ? -qv * lp : 0.f);
     const float hq = warp_sum((valid && qv > 0.f) ? -qv * logf(qv) : 0.f);
     const float klo = warp_sum(klo_t);
-    if (lane < zs) smem[dz + r * zs + lane] = legal ? ((pi - qv) + alpha * (pi - po)) * P.scale : 0.f;
-    st[kStatActorLoss] += (ce + alpha * klo) * P.scale;
-    st[kStatCE] += ce * P.scale;
-    st[kStatEntropy] += hq * P.scale;
-    st[kStatKLq] += (ce - hq) * P.scale;
-    st[kStatKLold] += klo * P.scale;
+    if (lane < zs) smem[dz + r * zs + lane] = legal ? ((pi - qv) + alpha * (pi - po)) * scale : 0.f;
+    st[kStatActorLoss] += (ce + alpha * klo) * scale;
+    st[kStatCE] += ce * scale;
+    st[kStatEntropy] += hq * scale;
+    st[kStatKLq] += (ce - hq) * scale;
+    st[kStatKLold] += klo * scale;
   }
   if (lane == 0)
 #pragma unroll
@@ -594,7 +594,9 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
   bool first = true;
   for (int64_t r0 = rb; r0 < re; r0 += kR, first = false) {
     const int R = (int)min((int64_t)kR, re - r0);
-    // the loss inputs of the block's rows, asynchronously (waited for before the loss)
+    // the weights first (the largest copy), then the loss inputs of the block's rows, all
+    // asynchronous; the input rows' loads below overlap them
+    if (first) stage_weights(n, wbase, bbase);
     for (int e = threadIdx.x; e < R * kLossIn; e += kT) {
       const int r = e / kLossIn, f = e - r * kLossIn;
       const int64_t row = r0 + r;
@@ -634,7 +636,6 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
         smem[xs + e] = x;
       }
     }
-    if (first) stage_weights(n, wbase, bbase);
     SS_MARK(13);
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
     __syncthreads();
@@ -654,7 +655,8 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
       SS_MARK(2);
       // in: the last hidden activations; w, b: the output layer
       int zs = (n.dims[L] + 3) & ~3;   // row stride of the gradient in the current dz buffer
-      block_loss(P, actor, n.dims[L - 1], n.dims[L], in, li, R, dzb0, zs, w, b, alpha, stw);
+      block_loss(actor, P.mask != nullptr, P.z_old != nullptr, P.scale, n.dims[L - 1], n.dims[L], in, li, R, dzb0,
+                 zs, w, b, alpha, stw);
       __syncthreads();
       SS_MARK(3);
       int cur = 0;

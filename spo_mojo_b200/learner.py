@@ -235,11 +235,48 @@ class Learner:
                    dual=wl.dual, device=device, **kw)
 
 
+def _packed_layout(like):
+    """Byte offsets of the fields of a batch packed into one buffer (each field on a
+    256-byte boundary) and the total size."""
+    offs, off = {}, 0
+    for k, v in like.items():
+        offs[k] = off
+        off += (v.numel() * v.element_size() + 255) // 256 * 256
+    return offs, max(off, 256)
+
+
+def _packed_views(flat, like, offs):
+    return {k: flat[offs[k]:offs[k] + v.numel() * v.element_size()].view(v.dtype).view(v.shape)
+            for k, v in like.items()}
+
+
+class PackedHostBatch(dict):
+    """A host batch whose fields are views of ONE pinned buffer (`flat`), so that its
+    upload is one host-to-device copy instead of one per field. Fill it like a dict of
+    tensors (`batch[k].copy_(...)`); `HostFeed.upload` recognises it."""
+
+    def __init__(self, like):
+        offs, total = _packed_layout(like)
+        self.flat = torch.empty(total, dtype=torch.uint8).pin_memory()
+        super().__init__(_packed_views(self.flat, like, offs))
+        self.offsets = offs
+
+    @classmethod
+    def of(cls, arrays):
+        """A packed pinned copy of a dict of numpy arrays or tensors."""
+        like = {k: torch.as_tensor(v) for k, v in arrays.items()}
+        b = cls(like)
+        for k, v in like.items():
+            b[k].copy_(v)
+        return b
+
+
 class HostFeed:
     """Feeds host (pinned) batches to the learner through two device buffers: the upload of
     the next step's inputs runs on a copy stream while the current step's kernels run on
     the compute stream (events order each buffer's upload before its step, and the step
-    before the buffer's next upload).
+    before the buffer's next upload). A `PackedHostBatch` with the same fields is uploaded
+    with one copy (the device buffers share its packed layout).
 
         feed = HostFeed(host_batch, device, stream)
         j = feed.upload(host_batch)              # inputs of step 0
@@ -256,19 +293,32 @@ class HostFeed:
         self.device = torch.device(device) if not isinstance(device, torch.device) else device
         self.compute = compute_stream
         self.copy = torch.cuda.Stream(self.device)
-        self.bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=self.device) for k, v in like.items()}
-                     for _ in range(2)]
+        self._offs, total = _packed_layout(like)
+        self.flats = [torch.empty(total, dtype=torch.uint8, device=self.device) for _ in range(2)]
+        self.bufs = [_packed_views(f, like, self._offs) for f in self.flats]
         self.ready = [torch.cuda.Event() for _ in range(2)]
         self.free = [torch.cuda.Event() for _ in range(2)]
         self._next = 0
+
+    def copy_into(self, j, host_batch):
+        """Enqueue the upload of host_batch into buffer j on the current stream; returns
+        the bytes copied."""
+        if isinstance(host_batch, PackedHostBatch) and host_batch.offsets == self._offs \
+                and host_batch.flat.numel() == self.flats[j].numel():
+            self.flats[j].copy_(host_batch.flat, non_blocking=True)
+            return host_batch.flat.numel()
+        n = 0
+        for k, v in host_batch.items():
+            self.bufs[j][k].copy_(v, non_blocking=True)
+            n += v.numel() * v.element_size()
+        return n
 
     def upload(self, host_batch):
         j = self._next
         self._next ^= 1
         self.copy.wait_event(self.free[j])  # a never-recorded event does not block
         with torch.cuda.stream(self.copy):
-            for k, v in host_batch.items():
-                self.bufs[j][k].copy_(v, non_blocking=True)
+            self.copy_into(j, host_batch)
         self.ready[j].record(self.copy)
         return j
 
