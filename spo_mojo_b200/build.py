@@ -6,6 +6,7 @@ spo_mojo_b200/libspo_cuda.so with the CUDA runtime linked statically and NCCL
 
     python -m spo_mojo_b200.build          # incremental
     python -m spo_mojo_b200.build --force  # rebuild everything
+    python -m spo_mojo_b200.build --trace  # libspo_cuda_trace.so: the small step's phase trace
 """
 
 import argparse
@@ -20,6 +21,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libspo_cuda.so")
+# the same library with the one-launch small step's phase marks compiled in
+TRACE_BUILD = os.path.join(HERE, "_build_trace")
+TRACE_LIB = os.path.join(HERE, "libspo_cuda_trace.so")
 ROOT = os.path.dirname(HERE)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -54,7 +58,9 @@ def _deps_newer(obj, src):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force=False, verbose=False):
+def build(force=False, verbose=False, trace=False):
+    BUILD, LIB = (TRACE_BUILD, TRACE_LIB) if trace else (globals()["BUILD"], globals()["LIB"])
+    flags = CFLAGS + (["-DSPO_SMALL_TRACE"] if trace else [])
     os.makedirs(BUILD, exist_ok=True)
     nv = nvcc()
     nccl = nccl_dir()
@@ -68,7 +74,7 @@ def build(force=False, verbose=False):
 
     def compile_one(job):
         src, obj = job
-        cmd = [nv] + ARCH + CFLAGS + inc + ["-c", src, "-o", obj]
+        cmd = [nv] + ARCH + flags + inc + ["-c", src, "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -102,5 +108,6 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--trace", action="store_true")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    print(build(force=a.force, verbose=a.verbose, trace=a.trace))

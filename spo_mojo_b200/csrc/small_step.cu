@@ -243,7 +243,7 @@ __device__ __noinline__ void block_dx_t(int dz, int zs, int N, int w, int K, int
 #pragma unroll
     for (int j = 0; j < TC; ++j) acc[i][j] = 0.f;
   if (N % 32 == 0) {   // swizzled rows: one float4 of each of the TC rows per 4 n
-#pragma unroll 2
+#pragma unroll 1
     for (int n = 0; n < N; n += 4) {
       float4 wv[TC];
 #pragma unroll
@@ -338,7 +338,7 @@ __device__ __noinline__ void block_dw_t(int in, int ks, int K, int dz, int zs, i
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][q][j] = 0.f;
     float db[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
+#pragma unroll 1
     for (int r = 0; r < R; ++r) {
       float z[4];
 #pragma unroll
@@ -397,7 +397,7 @@ __device__ __noinline__ void block_dw_out(int in, int ks, int K, int dz, int zs,
                                           bool first) {
   for (int k = threadIdx.x; k < K; k += kT) {
     float acc[kSmallMaxA] = {};
-#pragma unroll 4
+#pragma unroll 1
     for (int r = 0; r < R; ++r) {
       const float a = smem[in + r * ks + k];
       float z[kSmallMaxA];   // dz rows are zero past N up to their stride (a multiple of 4 >= N)
@@ -698,19 +698,19 @@ __device__ __forceinline__ void adam_one(float& p, float g, float& m, float& v, 
   p = p - lr * (m * bc1) / (sqrtf(v * bc2) + eps);
 }
 
-// sum over k < parts of src[k * stride] with 16 loads in flight: part k goes to partial
-// sum k % 8 and the eight are combined in a fixed order (deterministic).
+// sum over k < parts of src[k * stride], 32 loads in flight per round (the last round
+// predicated): part k goes to partial sum k % 8 and the eight are combined in a fixed order
+// (deterministic).
 __device__ __forceinline__ float sum_parts(const float* src, int parts, int64_t stride) {
+  constexpr int kU = 32;
   float a[8] = {};
-  int k = 0;
-  for (; k + 16 <= parts; k += 16) {
-    float v[16];
+  for (int k = 0; k < parts; k += kU) {
+    float v[kU];
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = ldcg(src + (int64_t)(k + u) * stride);
+    for (int u = 0; u < kU; ++u) v[u] = k + u < parts ? ldcg(src + (int64_t)(k + u) * stride) : 0.f;
 #pragma unroll
-    for (int u = 0; u < 16; ++u) a[u & 7] += v[u];
+    for (int u = 0; u < kU; ++u) a[u & 7] += v[u];
   }
-  for (; k < parts; ++k) a[k & 7] += ldcg(src + (int64_t)k * stride);
   return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
 }
 
