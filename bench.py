@@ -277,9 +277,13 @@ def roofline_hidden_gemm(args, rows, H, dev, stream, engine="tensor", reps=20):
 
 # DRAM bytes (read + write) of one launch of the roofline kernel at 1,048,576 rows, from an
 # ncu capture of the same kernel at 262,144 rows scaled by the 4x rows (the kernel streams
-# its activations once, so traffic grows with the rows). Filled in from the capture of the
-# current kernel (profiles/); absent until then.
-TRAFFIC_PER_LAUNCH = {}
+# its activations once, so traffic grows with the rows): dram__bytes_read.sum 1,076,124,672
+# + dram__bytes_write.sum 1,043,872,000 (profiles/roofline_tc_gemm_fwd_c3.md).
+TRAFFIC_PER_LAUNCH = {
+    ("tensor", 512): {"bytes": 4 * (1076124672 + 1043872000),
+                      "source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this kernel at 262,144 rows "
+                                "(bench.py --roofline-only 262144), x4 rows"},
+}
 
 
 TC0_MIN_ROWS = 16384  # the library runs the input layer on tensor cores from this many rows
