@@ -42,6 +42,7 @@ constexpr int kW = kT / 32;  // warps per CTA
 constexpr int kR = 32;       // rows held in shared memory at a time
 constexpr int kLossIn = 28;  // per-row loss inputs in shared memory: mask | q | pi_old logits (9 each)
 constexpr int kErrGridWait = 16;
+constexpr int kErrWeightCopy = 17;
 
 // SPO_SMALL_TRACE builds record %globaltimer at the phase boundaries of every CTA (thread
 // 0) into small_trace[CTA][mark], read back with spo_small_trace_read; other builds
@@ -133,16 +134,16 @@ extern __shared__ __align__(16) float smem[];
 __device__ __forceinline__ float4 lds4(int off) { return *reinterpret_cast<const float4*>(&smem[off]); }
 
 // The weights of every layer stay in shared memory for the whole step of the CTA, W_l
-// [d_l x d_{l+1}] row-major with its own width as the row stride. A hidden layer's rows
-// (width a multiple of 32) are XOR-swizzled in 16-byte chunks: W[k][c] sits at column
-// c ^ ((k & 7) << 2) of row k, so a row read across consecutive columns (the forward) and
-// a float4 read of consecutive rows at one column chunk (dX) both hit distinct banks, and
-// every 16-byte chunk stays contiguous for cp.async. The output layer (width 9 or 1, odd)
-// is stored as it is: a column read by consecutive rows is conflict-free. The first
-// layer's weights are padded with zero rows to 32 (the input rows are 32 wide, zero past
-// d0). The biases follow, each padded to a multiple of 4.
+// [d_l x d_{l+1}] row-major. A hidden layer's rows (width N a multiple of 32) are padded
+// by 16 bytes (row stride N + 4): a row read across consecutive columns (the forward) is
+// contiguous, and a float4 read of consecutive rows at one column (dX) steps 16 bytes
+// across the banks every row, so both are conflict-free, and every row is one contiguous
+// bulk copy. The output layer (width 9 or 1, odd) is stored as it is (one bulk copy): a
+// column read by consecutive rows is conflict-free. The first layer's weights are padded
+// with zero rows to 32 (the input rows are 32 wide, zero past d0). The biases follow,
+// each padded to a multiple of 4.
 __host__ __device__ inline int wrows(int l, int k) { return l == 0 ? 32 : k; }
-__device__ __forceinline__ int swz(int k, int c) { return c ^ ((k & 7) << 2); }
+__host__ __device__ inline int wst(int n) { return n % 32 == 0 ? n + 4 : n; }
 
 // Register tiles of the row-block products. A warp owns TR rows (r = h + rg i, one row
 // group h per warp, so the row operands are shared-memory broadcasts) and 32 TC columns
@@ -196,7 +197,7 @@ __device__ __noinline__ void block_forward_t(int in, int ks, int K, int w, int b
 #pragma unroll
     for (int u = 0; u < 4; ++u)
 #pragma unroll
-      for (int j = 0; j < TC; ++j) wv[u][j] = smem[w + (k + u) * N + swz(k + u, c0 + 32 * j)];
+      for (int j = 0; j < TC; ++j) wv[u][j] = smem[w + (k + u) * (N + 4) + c0 + 32 * j];
     float4 x[TR];   // rows past R read the block's unused buffer rows; never stored
 #pragma unroll
     for (int i = 0; i < TR; ++i) x[i] = lds4(in + (h + rg * i) * ks + k);
@@ -242,14 +243,14 @@ __device__ __noinline__ void block_dx_t(int dz, int zs, int N, int w, int K, int
   for (int i = 0; i < TR; ++i)
 #pragma unroll
     for (int j = 0; j < TC; ++j) acc[i][j] = 0.f;
-  if (N % 32 == 0) {   // swizzled rows: one float4 of each of the TC rows per 4 n
+  if (N % 32 == 0) {   // padded rows: one float4 of each of the TC rows per 4 n
 #pragma unroll 1
     for (int n = 0; n < N; n += 4) {
       float4 wv[TC];
 #pragma unroll
       for (int j = 0; j < TC; ++j) {
         const int c = c0 + 32 * j;
-        wv[j] = lds4(w + c * N + swz(c, n));
+        wv[j] = lds4(w + c * (N + 4) + n);
       }
       float4 z[TR];   // rows past R read the block's unused buffer rows; never stored
 #pragma unroll
@@ -516,7 +517,7 @@ __device__ __noinline__ void block_loss(bool actor, bool has_mask, bool has_old,
 
 // Shared memory of one network's row block, in floats: x [kR x 32] | loss inputs
 // [kR x kLossIn] | per-warp statistics [kW x kStats] | a_0 .. a_{L-2} [kR x d_{l+1}] |
-// dz ping-pong 2 x [kR x dmax] | W_0 .. W_{L-1} [wrows x d_{l+1}] | b_0 .. b_{L-1}
+// dz ping-pong 2 x [kR x dmax] | W_0 .. W_{L-1} [wrows x wst(d_{l+1})] | b_0 .. b_{L-1}
 // [pad4(d_{l+1})]; every region starts on a 16-byte boundary.
 __host__ __device__ inline int small_dmax(const int* dims, int L) {
   int dmax = (dims[L] + 3) & ~3;
@@ -531,7 +532,7 @@ __host__ __device__ inline int small_w_base(const int* dims, int L) {
 }
 __host__ __device__ inline int small_smem_floats(const int* dims, int L) {
   int f = small_w_base(dims, L);
-  for (int l = 0; l < L; ++l) f += wrows(l, dims[l]) * dims[l + 1] + ((dims[l + 1] + 3) & ~3);
+  for (int l = 0; l < L; ++l) f += wrows(l, dims[l]) * wst(dims[l + 1]) + ((dims[l + 1] + 3) & ~3);
   return f;
 }
 
@@ -541,44 +542,82 @@ __device__ __forceinline__ void cp4(float* dst, const float* src) {
                : "memory");
 }
 
-__device__ __forceinline__ void cp16(int dst, const float* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(&smem[dst]))),
-               "l"(src)
+__device__ __forceinline__ uint32_t smem_u32(int off) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(&smem[off]));
+}
+
+// One bulk copy (the copy engine, completion counted in bytes on the mbarrier bar).
+__device__ __forceinline__ void bulk_copy(int dst, const float* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
 
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bytes of every layer's weights and biases as staged (the bulk copies' total).
+__device__ uint32_t staged_bytes(const SmallNet& n) {
+  uint32_t bytes = 0;
+  for (int l = 0; l < n.L; ++l) bytes += 4u * (n.dims[l] * n.dims[l + 1] + ((n.dims[l + 1] + 3) & ~3));
+  return bytes;
+}
+
+// Bounded wait for the weight copies (parity phase of bar). On expiry: the step's abort
+// word and the error word are set, and a second bounded wait lets the copies in flight
+// land before the CTA goes on (its results are then discarded by the abort).
+__device__ bool wait_staged(uint32_t bar, uint32_t parity, const SmallStepParams& P) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = now_ns();
+  while (!mbar_try(bar, parity)) {
+    if (now_ns() - t0 > P.wait_ns) {
+      atomicExch(P.sync + 2, 1u);
+      if (P.err) atomicCAS(P.err, 0, kErrWeightCopy);
+      const uint64_t t1 = now_ns();
+      while (!mbar_try(bar, parity) && now_ns() - t1 < P.wait_ns) {
+      }
+      return false;
+    }
+  }
+  return true;
+}
+
 // Every layer's weights (at wbase, the layout above) and biases (at bbase) into shared
-// memory: asynchronous 16-byte copies, all in flight at once (waited for by the caller);
-// the first layer's padding rows zeroed.
-__device__ void stage_weights(const SmallNet& n, int wbase, int bbase) {
+// memory by bulk copies: one per hidden-layer row, one for the output layer, one per bias
+// (the flat parameter buffer pads every tensor to 64 floats, so a bias padded to 4 is
+// still inside it); the first layer's padding rows zeroed. Thread 0 has armed bar with
+// the total bytes; the caller waits on it.
+__device__ void stage_weights(const SmallNet& n, int wbase, int bbase, uint32_t bar) {
   int w = wbase, b = bbase;
   for (int l = 0; l < n.L; ++l) {
     const int K = n.dims[l], N = n.dims[l + 1];
-    const int n4 = K * N / 4;
     const float* src = n.W[l];
-    // each CTA starts at its own offset, so that the CTAs do not all ask the same L2
-    // lines at the same time
-    const int rot = (int)(((int64_t)blockIdx.x * 1031) % n4);
-    for (int t = threadIdx.x; t < n4; t += kT) {
-      const int g = t + rot < n4 ? t + rot : t + rot - n4;
-      const int e = 4 * g;
-      if (N % 32 == 0) {
-        const int k = e / N, c = e - k * N;
-        cp16(w + k * N + swz(k, c), src + e);
-      } else {
-        cp16(w + e, src + e);
-      }
+    if (N % 32 == 0) {
+      for (int r = threadIdx.x; r < K; r += kT) bulk_copy(w + r * (N + 4), src + (int64_t)r * N, 4u * N, bar);
+    } else if (threadIdx.x == kT - 1) {
+      bulk_copy(w, src, 4u * K * N, bar);
     }
-    for (int e = K * N + threadIdx.x; e < wrows(l, K) * N; e += kT) smem[w + e] = 0.f;
-    const int nb = (N + 3) & ~3;   // the flat parameter buffer pads every tensor to 64 floats
-    for (int g = threadIdx.x; g < nb / 4; g += kT) cp16(b + 4 * g, n.b[l] + 4 * g);
-    w += wrows(l, K) * N;
-    b += nb;
+    for (int e = K * wst(N) + threadIdx.x; e < wrows(l, K) * wst(N); e += kT) smem[w + e] = 0.f;
+    if (threadIdx.x == kT - 2 - l) bulk_copy(b, n.b[l], 4u * ((N + 3) & ~3), bar);
+    w += wrows(l, K) * wst(N);
+    b += (N + 3) & ~3;
   }
 }
 
 // One network over this CTA's rows [rb, re), 32 rows at a time.
-__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re) {
+// bar: the CTA's mbarrier of the weight copies, phase its next parity.
+__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re, uint32_t bar,
+                         uint32_t& phase) {
   const int L = n.L, d0 = n.dims[0];
   const int part = blockIdx.x;
   const bool actor = n.mode == 0;
@@ -588,7 +627,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
   for (int l = 1; l < L; ++l) dzb0 += kR * n.dims[l];
   const int wbase = small_w_base(n.dims, L);
   int bbase = wbase;
-  for (int l = 0; l < L; ++l) bbase += wrows(l, n.dims[l]) * n.dims[l + 1];
+  for (int l = 0; l < L; ++l) bbase += wrows(l, n.dims[l]) * wst(n.dims[l + 1]);
   const float alpha = (actor && P.z_old) ? softplus_f(*P.log_alpha) : 0.f;
   for (int e = threadIdx.x; e < kW * kStats; e += kT) smem[stw + e] = 0.f;
   bool first = true;
@@ -596,7 +635,15 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
     const int R = (int)min((int64_t)kR, re - r0);
     // the weights first (the largest copy), then the loss inputs of the block's rows, all
     // asynchronous; the input rows' loads below overlap them
-    if (first) stage_weights(n, wbase, bbase);
+    if (first) {
+      if (threadIdx.x == 0) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(staged_bytes(n))
+                     : "memory");
+      }
+      __syncthreads();   // armed before any copy can complete; earlier reads of this memory done
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      stage_weights(n, wbase, bbase, bar);
+    }
     for (int e = threadIdx.x; e < R * kLossIn; e += kT) {
       const int r = e / kLossIn, f = e - r * kLossIn;
       const int64_t row = r0 + r;
@@ -638,6 +685,10 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
     }
     SS_MARK(13);
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    if (first) {
+      wait_staged(bar, phase, P);   // on expiry the step is aborted (the results are not used)
+      phase ^= 1u;
+    }
     __syncthreads();
     SS_MARK(1);
     {
@@ -649,7 +700,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
         in = a;
         ks = N;
         a += kR * N;
-        w += K * N;
+        w += K * wst(N);
         b += (N + 3) & ~3;
       }
       SS_MARK(2);
@@ -672,7 +723,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
         zs = K;
         cur ^= 1;
         if (l >= 1) {   // step back one layer: its weights, its input activations
-          w -= wrows(l - 1, n.dims[l - 1]) * K;
+          w -= wrows(l - 1, n.dims[l - 1]) * wst(K);
           in = l - 1 == 0 ? xs : in - kR * n.dims[l - 1];
         }
         SS_MARK(9 + l);
@@ -724,10 +775,18 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
   SS_MARK(0);
   // ---- rows: forward, loss, backward; per-CTA partial sums
   if (blockIdx.x < P.parts) {
+    __shared__ __align__(8) unsigned long long s_wbar;   // completion of the weight copies
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&s_wbar));
+    if (threadIdx.x == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    uint32_t phase = 0;
     const int64_t rb = (int64_t)blockIdx.x * P.rows_per_cta;
     const int64_t re = min(rb + P.rows_per_cta, P.rows);
     for (int i = 0; i < 2; ++i)
-      if (P.net[i].L) net_rows(P, P.net[i], rb, re);
+      if (P.net[i].L) net_rows(P, P.net[i], rb, re, bar, phase);
   }
   SS_MARK(5);
   ok = grid_barrier(target, P);
