@@ -155,6 +155,15 @@ struct Tile {
   int tr, tc;
 };
 
+// Row groups of a tile with cg column groups: the warps left per column group, rounded
+// down to a power of two, so that a tile's rows h + rg i (i < TR, TR a power of two that
+// covers R <= 32 rows) never pass the block's 32-row buffers.
+__host__ __device__ inline int row_groups(int cg) {
+  int rg = 1;
+  while (2 * rg * cg <= kW) rg *= 2;
+  return rg;
+}
+
 // The tile of an [R x N] output (N % 32 == 0) with the fewest wavefronts per step.
 __device__ __forceinline__ Tile pick_tile(int R, int N) {
   Tile best{0, 0};
@@ -163,7 +172,7 @@ __device__ __forceinline__ Tile pick_tile(int R, int N) {
     if (N % (32 * tc) != 0) continue;
     const int cg = N / (32 * tc);
     if (cg > kW) continue;
-    const int rg = kW / cg;
+    const int rg = row_groups(cg);
     int tr = (R + rg - 1) / rg;
     tr = tr <= 1 ? 1 : tr <= 2 ? 2 : tr <= 4 ? 4 : tr <= 8 ? 8 : tr <= 16 ? 16 : 32;
     if (tc == 2 && (tr < 4 || tr > 16)) continue;   // instantiated: (1|2|4|8|16|32, 1), (4|8|16, 2)
@@ -182,7 +191,7 @@ template <int TR, int TC>
 __device__ __noinline__ void block_forward_t(int in, int ks, int K, int w, int b, int N, int out, float* gout,
                                              int R) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int cg = N / (32 * TC), rg = kW / cg;
+  const int cg = N / (32 * TC), rg = row_groups(cg);
   if (warp >= cg * rg) return;
   const int g = warp % cg, h = warp / cg;
   const int c0 = 32 * TC * g + lane;
@@ -234,7 +243,7 @@ __device__ __noinline__ void block_forward_t(int in, int ks, int K, int w, int b
 template <int TR, int TC>
 __device__ __noinline__ void block_dx_t(int dz, int zs, int N, int w, int K, int act, int out, int R) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int cg = K / (32 * TC), rg = kW / cg;
+  const int cg = K / (32 * TC), rg = row_groups(cg);
   if (warp >= cg * rg) return;
   const int g = warp % cg, h = warp / cg;
   const int c0 = 32 * TC * g + lane;
