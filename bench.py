@@ -160,35 +160,68 @@ def run_reference(args):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
+    """nvidia-smi sampling every 50 ms on a reader thread, each line time-stamped on
+    arrival. start() waits (bounded) for the first line, so a short job is still covered;
+    mark() and stop() bracket the timed region, whose samples are the ones reported (all
+    samples since start() when the region was shorter than the interval)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 50
 
     def __init__(self, gpu_indices):
         self.gpus = ",".join(str(g) for g in gpu_indices)
         self.proc = None
+        self.lines = []
+        self.t_mark = None
+        self._reader = None
 
-    def start(self):
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.perf_counter(), line))
+
+    def start(self, wait_s=5.0):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpus, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.INTERVAL_MS)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+            return
+        self._reader = threading.Thread(target=self._read, daemon=True)
+        self._reader.start()
+        t_end = time.perf_counter() + wait_s
+        while not self.lines and time.perf_counter() < t_end and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def mark(self):
+        """The start of the timed region."""
+        self.t_mark = time.perf_counter()
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t_stop = time.perf_counter()
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-            out = ""
+        if self._reader is not None:
+            self._reader.join(timeout=5)
+        lines = list(self.lines)
+        window = "timed region"
+        if self.t_mark is not None:
+            inside = [(t, ln) for t, ln in lines if self.t_mark <= t <= t_stop + self.INTERVAL_MS / 1e3]
+            if inside:
+                lines = inside
+            else:
+                window = "warm-up and timed region (the timed region was shorter than the interval)"
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.splitlines():
+        for _, line in lines:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -201,7 +234,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "window": window}
 
 
 # ---------------------------------------------------------------- GPU arm
@@ -448,6 +481,8 @@ def run_ours(args):
         evs[-1][1].synchronize()
         return sum(a.elapsed_time(b) for a, b in evs) / args.steps
 
+    if clocks is not None:
+        clocks.mark()
     if flush:
         ms = flushed_ms(lambda i: step(batch))
     else:

@@ -429,6 +429,15 @@ SPO_API int spo_learner_status(spo_learner_t learner, int32_t* device_error);
  * No reference counterpart (the reference's update() is ~35 launches,
  * demos/train_spo.mojo:417-554). */
 SPO_API int spo_learner_set_small_rows(spo_learner_t learner, int64_t max_rows);
+/* No reference counterpart: a test of the one-launch step's failure path. Runs the
+ * one-launch step of spo_learner_step on batch (which must take it: 1 <= rows <= the
+ * small-rows limit) with the first CTA's arrival at the first grid-wide barrier withheld
+ * and every barrier wait limited to wait_us microseconds (1 .. 2,000,000; the step itself
+ * waits up to 2 s). The other CTAs' waits run out: the step is aborted (no gradient is
+ * written, no parameter, moment or step counter changes), the learner's error word gets a
+ * nonzero code (spo_learner_status) and the barrier words are reset for the next step. */
+SPO_API int spo_learner_step_withheld(spo_learner_t learner, spo_stream_t stream, const spo_batch* batch,
+                                      const spo_train_state* state, int64_t wait_us);
 /* backward (grad_scale = 1 / rows) + apply. */
 SPO_API int spo_learner_step(spo_learner_t learner, spo_stream_t stream, const spo_batch* batch,
                      const spo_train_state* state);

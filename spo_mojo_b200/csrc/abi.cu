@@ -812,8 +812,10 @@ int learner_apply(spo_learner* Lr, cudaStream_t s, const spo_train_state* st) {
 
 // The whole step of a small batch in one launch (small_step.cu); with apply, the clip and
 // Adam too.
+// wait_ns: the limit of every barrier wait; withhold: 1 + the CTA whose first barrier
+// arrival is withheld (a test of the bounded waits), 0 in every other launch.
 int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale, const spo_train_state* st,
-               bool apply) {
+               bool apply, uint64_t wait_ns = 2000000000ull, uint32_t withhold = 0) {
   SmallStepParams p{};
   const spo_learner_layout& lay = Lr->layout;
   const int G = Lr->sm_grid;
@@ -877,7 +879,8 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
   p.sumsq = Lr->sm_sumsq;
   p.sync = Lr->sm_sync;
   p.err = Lr->err;
-  p.wait_ns = 2000000000ull;
+  p.wait_ns = wait_ns;
+  p.withhold = withhold;
   Lr->last_small = true;
   return small_step_launch(p, G, kSmallMaxSmem, s);
 }
@@ -1435,6 +1438,19 @@ int spo_learner_set_small_rows(spo_learner_t learner, int64_t max_rows) {
                 "the one-launch step needs 2-4 layers, input <= 32, hidden widths multiples of 32 up to 256");
   learner->small_rows = std::min<int64_t>(max_rows, learner->desc.max_rows);
   return kOk;
+}
+
+int spo_learner_step_withheld(spo_learner_t learner, spo_stream_t stream, const spo_batch* batch,
+                              const spo_train_state* state, int64_t wait_us) {
+  SPO_CHECK_ARG(learner && batch && state && state->params && state->grads, kErrArg, "null argument");
+  SPO_CHECK_ARG(wait_us >= 1 && wait_us <= 2000000, kErrArg, "wait_us must be in [1, 2000000]");
+  SPO_CHECK_ARG(learner->err != nullptr, kErrArg, "learner has no error word");
+  SPO_CHECK_ARG(batch->rows >= 1 && batch->rows <= learner->small_rows, kErrUnsupported,
+                "spo_learner_step_withheld: the batch does not take the one-launch step");
+  SPO_CHECK_ARG(aligned16(state->params) && aligned16(state->grads), kErrAlign,
+                "params and grads must be 16-byte aligned");
+  const float scale = 1.0f / (float)batch->rows;
+  return small_step(learner, S(stream), batch, scale, state, true, (uint64_t)wait_us * 1000u, 1u);
 }
 
 int spo_learner_forward(spo_learner_t learner, spo_stream_t stream, int32_t which,

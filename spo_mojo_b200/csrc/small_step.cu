@@ -93,14 +93,15 @@ __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ float softplus_f(float x) { return log1pf(expf(-fabsf(x))) + fmaxf(x, 0.f); }
 
 // Grid-wide barrier: every CTA arrives, then waits (bounded) until all have. false when
-// the step was aborted.
-__device__ bool grid_barrier(unsigned& target, const SmallStepParams& P) {
+// the step was aborted. withhold: this CTA does not arrive (a test of the bounded wait: the
+// others' waits then run out).
+__device__ bool grid_barrier(unsigned& target, const SmallStepParams& P, bool withhold = false) {
   __shared__ int s_ok;
   __syncthreads();
   target += gridDim.x;
   if (threadIdx.x == 0) {
     __threadfence();
-    atomicAdd(P.sync + 0, 1u);
+    if (!withhold) atomicAdd(P.sync + 0, 1u);
     int ok = 1;
     const uint64_t t0 = now_ns();
     while (ld_acquire(P.sync + 0) < target) {
@@ -798,7 +799,7 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
       if (P.net[i].L) net_rows(P, P.net[i], rb, re, bar, phase);
   }
   SS_MARK(5);
-  ok = grid_barrier(target, P);
+  ok = grid_barrier(target, P, P.withhold == blockIdx.x + 1u);
   SS_MARK(6);
 
   // ---- partial sums -> flat gradients (each in CTA order), Adam fused per element

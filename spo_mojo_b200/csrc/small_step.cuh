@@ -51,6 +51,8 @@ struct SmallStepParams {
   unsigned* sync;                      // [0] barrier arrivals, [1] exits, [2] abort; zero between launches
   int* err;                            // learner error word
   uint64_t wait_ns;                    // limit of every barrier wait
+  uint32_t withhold;                   // a test of the bounded waits: 1 + the CTA whose first
+                                       // barrier arrival is withheld (0: none)
 };
 
 // Dynamic shared memory of the nets' row blocks (the largest of the given networks).

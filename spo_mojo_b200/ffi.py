@@ -155,6 +155,7 @@ SIGNATURES = {
     "spo_learner_apply": (INT, [P, P, ctypes.POINTER(TrainState)]),
     "spo_learner_step": (INT, [P, P, ctypes.POINTER(Batch), ctypes.POINTER(TrainState)]),
     "spo_learner_set_small_rows": (INT, [P, I64]),
+    "spo_learner_step_withheld": (INT, [P, P, ctypes.POINTER(Batch), ctypes.POINTER(TrainState), I64]),
     "spo_learner_status": (INT, [P, ctypes.POINTER(I32)]),
     "spo_learner_cache": (INT, [P, I32, I32, ctypes.POINTER(P), ctypes.POINTER(P)]),
     "spo_learner_forward": (INT, [P, P, I32, P, P, P, I64, P, P]),

@@ -153,3 +153,40 @@ def test_small_rows_are_refused_for_wide_networks():
     with pytest.raises(ffi.SpoError, match="one-launch step"):
         L.set_small_rows(64)
     L.set_small_rows(0)
+
+
+def test_bounded_barrier_wait_runs_out_and_the_next_step_is_exact():
+    """The one-launch step's bounded grid-barrier waits, made to run out without a fault:
+    the first CTA withholds its arrival at the first barrier and every wait is limited to
+    2 ms (spo_learner_step_withheld). The launch must end by itself with a nonzero code in
+    the learner's error word and change no parameter, moment or step counter; the next
+    normal step must then match a fresh learner's step exactly (barrier words reset)."""
+    import ctypes
+    import time
+    from spo_mojo_b200 import ffi
+    wl = WLS["c0"]
+    rows = 256
+    batch = dev(make_batch(wl, rows, seed=5))
+    L, _ = learner(wl, rows, True)
+    assert L.device_status() == 0
+    p0, m0, v0 = L.params.clone(), L.adam_m.clone(), L.adam_v.clone()
+    b = L._batch(batch)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ffi.call("spo_learner_step_withheld", L._h, None, ctypes.byref(b), ctypes.byref(L._state), 2000)
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 10.0
+    assert L.device_status() == 16          # a grid-barrier wait ran out
+    assert torch.equal(L.params, p0) and torch.equal(L.adam_m, m0) and torch.equal(L.adam_v, v0)
+    assert L.report_dict()["step"] == 0 and int(L.step_counter.item()) == 0
+    with pytest.raises(ffi.SpoError, match="one-launch step"):
+        big = dev(make_batch(wl, rows, seed=5))
+        L.set_small_rows(128)
+        ffi.call("spo_learner_step_withheld", L._h, None, ctypes.byref(L._batch(big)), ctypes.byref(L._state), 2000)
+    L.set_small_rows(rows)
+    L.step(batch)
+    R, _ = learner(wl, rows, True)
+    R.step(batch)
+    torch.cuda.synchronize()
+    assert L.device_status() == 0
+    assert torch.equal(L.params, R.params) and torch.equal(L.grads, R.grads)
