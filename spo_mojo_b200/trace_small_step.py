@@ -50,9 +50,15 @@ def main():
         p = init_params(wl, seed=0)
         L.load(actor=p.get("actor"), critic=p.get("critic"), log_alpha=wl.log_alpha)
         b = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in make_batch(wl, rows, seed=1).items()}
-        for _ in range(args.steps):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(args.steps):
+            if i == args.steps // 2:
+                s0.record()
             L.step(b)
+        s1.record()
         torch.cuda.synchronize()
+        # back-to-back steps (no L2 flush between them), CUDA events: kernel + launch gaps
+        back_to_back_us = s0.elapsed_time(s1) * 1e3 / (args.steps - args.steps // 2)
         buf = (ctypes.c_ulonglong * (1024 * MARKS))()
         if read(buf, 1024 * MARKS) != 0:
             raise RuntimeError("spo_small_trace_read failed")
@@ -63,7 +69,8 @@ def main():
         rel[a == 0] = np.nan
         clk, ns = a[:, 15] - a[:, 14], a[:, 8] - a[:, 0]
         out = {"workload": name, "rows": rows, "steps": args.steps,
-               "sm_mhz": float(np.median(clk[ns > 0] * 1000.0 / ns[ns > 0]))}
+               "sm_mhz": float(np.median(clk[ns > 0] * 1000.0 / ns[ns > 0])),
+               "back_to_back_us_per_step": round(back_to_back_us, 2)}
         for m in range(14):
             col = rel[:, m]
             if np.any(~np.isnan(col)):
