@@ -124,6 +124,61 @@ class Learner:
         self.adam_v.zero_()
         self.step_counter.zero_()
 
+    # ------------------------------------------------------------ checkpoint
+    CHECKPOINT_FILES = ("params.bin", "adam_m.bin", "adam_v.bin")
+
+    def _checkpoint_meta(self):
+        d = self.desc
+        return {"format": "spo-learner-checkpoint/1", "actor_dims": self.actor_dims,
+                "critic_dims": self.critic_dims, "total": int(self.layout.total),
+                "lr_actor": d.lr_actor, "lr_critic": d.lr_critic, "beta1": d.beta1, "beta2": d.beta2,
+                "adam_eps": d.adam_eps, "max_grad_norm": d.max_grad_norm, "kl_eps": d.kl_eps,
+                "use_kl": int(d.use_kl), "dual": int(d.dual)}
+
+    def save_checkpoint(self, path):
+        """Write the learner's state into directory `path`: the flat parameter buffer and
+        both Adam moments as raw little-endian float32 (`params.bin`, `adam_m.bin`,
+        `adam_v.bin`; the layout of spo_learner_layout_of, the raw-f32 convention of the
+        reference's golden tensors, tests/golden_io.mojo) and `checkpoint.json` (the
+        networks, hyperparameters and Adam's step). Waits for the learner's device."""
+        import json
+        import os
+        os.makedirs(path, exist_ok=True)
+        torch.cuda.synchronize(self.device)
+        for name, buf in zip(self.CHECKPOINT_FILES, (self.params, self.adam_m, self.adam_v)):
+            buf.detach().cpu().numpy().astype("<f4").tofile(os.path.join(path, name))
+        meta = self._checkpoint_meta()
+        meta["step"] = int(self.step_counter.item())
+        with open(os.path.join(path, "checkpoint.json"), "w") as f:
+            json.dump(meta, f, indent=1)
+
+    def load_checkpoint(self, path):
+        """Restore a state written by save_checkpoint into this learner, which must have the
+        same networks and hyperparameters (ValueError otherwise); the next step continues
+        Adam where the saved one stopped."""
+        import json
+        import os
+        import numpy as np
+        with open(os.path.join(path, "checkpoint.json")) as f:
+            meta = json.load(f)
+        mine = self._checkpoint_meta()
+        for k, v in mine.items():
+            saved = meta.get(k)
+            if isinstance(v, tuple):
+                saved = tuple(saved) if saved is not None else None
+            same = saved == v if not isinstance(v, float) else (
+                saved is not None and (saved == v or math.isclose(saved, v, rel_tol=1e-6)))
+            if not same:
+                raise ValueError(f"checkpoint {path}: {k} is {saved!r}, this learner has {v!r}")
+        total = int(self.layout.total)
+        for name, buf in zip(self.CHECKPOINT_FILES, (self.params, self.adam_m, self.adam_v)):
+            raw = np.fromfile(os.path.join(path, name), dtype="<f4")
+            if raw.size != total:
+                raise ValueError(f"checkpoint {path}: {name} holds {raw.size} floats, expected {total}")
+            buf.copy_(torch.from_numpy(raw))
+        self.step_counter.fill_(int(meta["step"]))
+        torch.cuda.synchronize(self.device)
+
     @property
     def log_alpha(self):
         return self.params[self.layout.alpha_index]
