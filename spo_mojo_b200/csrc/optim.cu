@@ -39,19 +39,23 @@ __global__ void __launch_bounds__(kThreads) reduce_kernel(const ReduceParams P) 
     if (s >= P.nseg) break;  // block-uniform
     const ReduceSeg sg = P.seg[s];
     const int64_t i = (gch - base) * kRedCols + c;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    // this group's parts k = g, g + G, g + 2G, ... (G = kRedGroups), eight loads in flight:
+    // the j-th of a round goes to accumulator j, the eight combine in a fixed tree
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (i < sg.count) {
       const float* src = sg.src + i;
-      int k = g;
-      for (; k + 3 * kRedGroups < sg.parts; k += 4 * kRedGroups) {
-        a0 += __ldg(src + (int64_t)k * sg.part_stride);
-        a1 += __ldg(src + (int64_t)(k + kRedGroups) * sg.part_stride);
-        a2 += __ldg(src + (int64_t)(k + 2 * kRedGroups) * sg.part_stride);
-        a3 += __ldg(src + (int64_t)(k + 3 * kRedGroups) * sg.part_stride);
+      for (int k = g; k < sg.parts; k += 8 * kRedGroups) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int kk = k + j * kRedGroups;
+          v[j] = kk < sg.parts ? __ldg(src + (int64_t)kk * sg.part_stride) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] += v[j];
       }
-      for (; k < sg.parts; k += kRedGroups) a0 += __ldg(src + (int64_t)k * sg.part_stride);
     }
-    gsum[g][c] = (a0 + a1) + (a2 + a3);
+    gsum[g][c] = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
     __syncthreads();
     if (g == 0 && i < sg.count) {
       float v = gsum[0][c];
@@ -272,7 +276,20 @@ int reduce_launch(const ReduceParams& p, cudaStream_t s) {
   int64_t total = 0;  // chunks over all segments
   for (int i = 0; i < p.nseg; ++i) total += red_chunks(p.seg[i]);
   if (p.nseg == 0) return kOk;
-  const int grid = (int)std::min<int64_t>(total, 4LL * sm_count());
+  // every block resident at once (the occupancy of this kernel, asked once per device)
+  static int per_sm[64] = {};
+  int dev = 0;
+  SPO_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && per_sm[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_kernel, kThreads, 0) != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = 4;
+    }
+    per_sm[dev] = n;
+  }
+  const int64_t resident = (int64_t)(dev >= 0 && dev < 64 ? per_sm[dev] : 4) * sm_count();
+  const int grid = (int)std::min<int64_t>(total, resident);
   SPO_CUDA_TRY(launch_pdl(reduce_kernel, dim3(std::max(grid, 1)), dim3(kThreads), 0, s, 0u, p));
   return kOk;
 }
