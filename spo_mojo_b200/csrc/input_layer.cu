@@ -17,7 +17,9 @@
 // Weight gradient: dW[k x n] = x^T dY summed over rows, dY [rows x n].
 // CTA = 256 threads over one chunk of rows and 512 columns: thread t owns the 4 columns
 // 4 (t % 128) .. +3 of its column block and one half of the k features (t / 128: 16
-// feature slots, or 14 when k <= 28), so its accumulators are [half of k] x 4. Rows are walked in blocks of kRows: the block's x rows
+// feature slots, or 14 when k <= 28), so its accumulators are [half of k] x 4. With fewer
+// columns (n / 4 dividing 128) the spare threads take interleaved rows of the same
+// columns and hand their sums over at the end. Rows are walked in blocks of kRows: the block's x rows
 // are staged in shared memory (zero-padded to 32 features) and read as broadcasts, the dY
 // float4 of each row is loaded straight from global memory, 8 rows in flight per thread.
 // Each CTA writes its partial [k x n] tile to part[chunk]; a deterministic reduction adds
@@ -107,7 +109,12 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
   pdl_trigger();
   const int tid = threadIdx.x;
   const int half = tid / 128;
-  const int64_t col = (int64_t)blockIdx.y * kCols + 4 * (tid % 128);
+  // Fewer than 512 columns: the 128 threads of a half split into RS row subgroups of n/4
+  // column threads each (subgroup s takes rows s, s + RS, ... of every block); their sums
+  // are added in subgroup order at the end.
+  const int rs = (n < kCols && 128 % (n / 4) == 0) ? (int)(128 / (n / 4)) : 1;
+  const int per = 128 / rs, ct = (tid % 128) % per, rsub = (tid % 128) / per;
+  const int64_t col = (int64_t)blockIdx.y * kCols + 4 * ct;
   const bool col_ok = col < n;
   const int64_t r_begin = (int64_t)blockIdx.x * chunk;
   const int64_t r_end = min(rows, r_begin + chunk);
@@ -138,17 +145,18 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
     }
     float (*xs)[kMaxK] = xs2[blk & 1];
     if (col_ok) {
-      for (int r0 = 0; r0 < nr; r0 += kUnroll) {
+      for (int r0 = rsub; r0 < nr; r0 += kUnroll * rs) {
         float4 g[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u)
-          g[u] = r0 + u < nr ? __ldg(reinterpret_cast<const float4*>(dy + (rb + r0 + u) * n + col))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+          g[u] = r0 + u * rs < nr ? __ldg(reinterpret_cast<const float4*>(dy + (rb + r0 + u * rs) * n + col))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
+          const int xr_row = min(r0 + u * rs, kRows - 1);   // past nr: dY is zero there
           const float gv[4] = {g[u].x, g[u].y, g[u].z, g[u].w};
           if constexpr (KH == 16) {
-            const float4* xr = reinterpret_cast<const float4*>(&xs[r0 + u][i0]);
+            const float4* xr = reinterpret_cast<const float4*>(&xs[xr_row][i0]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const float2 gg = make_float2(gv[q], gv[q]);
@@ -160,7 +168,7 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
               }
             }
           } else {
-            const float2* xr = reinterpret_cast<const float2*>(&xs[r0 + u][i0]);
+            const float2* xr = reinterpret_cast<const float2*>(&xs[xr_row][i0]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const float2 gg = make_float2(gv[q], gv[q]);
@@ -174,6 +182,31 @@ dw_skinny_kernel(const float* __restrict__ x, const float* __restrict__ cells, c
     __syncthreads();  // buffer blk & 1 is consumed before block blk + 2 is copied into it
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (rs > 1) {
+    // row subgroups 1 .. rs-1 hand their sums to subgroup 0 through shared memory (the
+    // staging buffers are free now), one subgroup and one column of the 4 at a time
+    float* buf = &xs2[0][0][0];   // [2 halves][per][KH]
+    for (int s = 1; s < rs; ++s) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __syncthreads();
+        if (rsub == s)
+#pragma unroll
+          for (int i = 0; i < KH / 2; ++i) {
+            buf[(half * per + ct) * KH + 2 * i] = acc[q][i].x;
+            buf[(half * per + ct) * KH + 2 * i + 1] = acc[q][i].y;
+          }
+        __syncthreads();
+        if (rsub == 0)
+#pragma unroll
+          for (int i = 0; i < KH / 2; ++i) {
+            acc[q][i].x += buf[(half * per + ct) * KH + 2 * i];
+            acc[q][i].y += buf[(half * per + ct) * KH + 2 * i + 1];
+          }
+      }
+    }
+    if (rsub != 0) return;
+  }
   if (!col_ok) return;
   float* out = part + (int64_t)blockIdx.x * k * n;
 #pragma unroll
