@@ -576,11 +576,9 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bytes of every layer's weights and biases as staged (the bulk copies' total).
-__device__ uint32_t staged_bytes(const SmallNet& n) {
-  uint32_t bytes = 0;
-  for (int l = 0; l < n.L; ++l) bytes += 4u * (n.dims[l] * n.dims[l + 1] + ((n.dims[l + 1] + 3) & ~3));
-  return bytes;
+// Bytes of layer l's weights and bias as staged (its bulk copies' total).
+__device__ __forceinline__ uint32_t staged_bytes(const SmallNet& n, int l) {
+  return 4u * (n.dims[l] * n.dims[l + 1] + ((n.dims[l + 1] + 3) & ~3));
 }
 
 // Bounded wait for the weight copies (parity phase of bar). On expiry: the step's abort
@@ -605,13 +603,15 @@ __device__ bool wait_staged(uint32_t bar, uint32_t parity, const SmallStepParams
 // Every layer's weights (at wbase, the layout above) and biases (at bbase) into shared
 // memory by bulk copies: one per hidden-layer row, one for the output layer, one per bias
 // (the flat parameter buffer pads every tensor to 64 floats, so a bias padded to 4 is
-// still inside it); the first layer's padding rows zeroed. Thread 0 has armed bar with
-// the total bytes; the caller waits on it.
-__device__ void stage_weights(const SmallNet& n, int wbase, int bbase, uint32_t bar) {
+// still inside it); the first layer's padding rows zeroed. Layer l's copies complete on
+// the mbarrier bar0 + 8 l, which thread 0 has armed with that layer's bytes: the forward
+// of a layer waits for its own weights only.
+__device__ void stage_weights(const SmallNet& n, int wbase, int bbase, uint32_t bar0) {
   int w = wbase, b = bbase;
   for (int l = 0; l < n.L; ++l) {
     const int K = n.dims[l], N = n.dims[l + 1];
     const float* src = n.W[l];
+    const uint32_t bar = bar0 + 8u * l;
     if (N % 32 == 0) {
       for (int r = threadIdx.x; r < K; r += kT) bulk_copy(w + r * (N + 4), src + (int64_t)r * N, 4u * N, bar);
     } else if (threadIdx.x == kT - 1) {
@@ -625,8 +625,9 @@ __device__ void stage_weights(const SmallNet& n, int wbase, int bbase, uint32_t 
 }
 
 // One network over this CTA's rows [rb, re), 32 rows at a time.
-// bar: the CTA's mbarrier of the weight copies, phase its next parity.
-__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re, uint32_t bar,
+// bar0: the CTA's mbarriers of the weight copies (one per layer, 8 bytes apart), phase
+// their next parity.
+__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re, uint32_t bar0,
                          uint32_t& phase) {
   const int L = n.L, d0 = n.dims[0];
   const int part = blockIdx.x;
@@ -646,13 +647,14 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
     // the weights first (the largest copy), then the loss inputs of the block's rows, all
     // asynchronous; the input rows' loads below overlap them
     if (first) {
-      if (threadIdx.x == 0) {
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(staged_bytes(n))
-                     : "memory");
-      }
+      if (threadIdx.x == 0)
+        for (int l = 0; l < L; ++l)
+          asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar0 + 8u * l),
+                       "r"(staged_bytes(n, l))
+                       : "memory");
       __syncthreads();   // armed before any copy can complete; earlier reads of this memory done
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      stage_weights(n, wbase, bbase, bar);
+      stage_weights(n, wbase, bbase, bar0);
     }
     for (int e = threadIdx.x; e < R * kLossIn; e += kT) {
       const int r = e / kLossIn, f = e - r * kLossIn;
@@ -695,16 +697,15 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
     }
     SS_MARK(13);
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-    if (first) {
-      wait_staged(bar, phase, P);   // on expiry the step is aborted (the results are not used)
-      phase ^= 1u;
-    }
     __syncthreads();
     SS_MARK(1);
     {
       int in = xs, ks = 32, a = acts0, w = wbase, b = bbase;
       for (int l = 0; l + 1 < L; ++l) {
         const int K = wrows(l, n.dims[l]), N = n.dims[l + 1];
+        // the first block waits for each layer's weights just before using them (on
+        // expiry the step is aborted and its results are not used)
+        if (first) wait_staged(bar0 + 8u * l, phase, P);
         block_forward(in, ks, K, w, b, N, a, n.gact[l] ? n.gact[l] + r0 * N : nullptr, R);
         __syncthreads();
         in = a;
@@ -715,6 +716,10 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
       }
       SS_MARK(2);
       // in: the last hidden activations; w, b: the output layer
+      if (first) {
+        wait_staged(bar0 + 8u * (L - 1), phase, P);
+        phase ^= 1u;   // every layer's barrier has completed this phase
+      }
       int zs = (n.dims[L] + 3) & ~3;   // row stride of the gradient in the current dz buffer
       block_loss(actor, P.mask != nullptr, P.z_old != nullptr, P.scale, n.dims[L - 1], n.dims[L], in, li, R, dzb0,
                  zs, w, b, alpha, stw);
@@ -785,10 +790,21 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
   SS_MARK(0);
   // ---- rows: forward, loss, backward; per-CTA partial sums
   if (blockIdx.x < P.parts) {
-    __shared__ __align__(8) unsigned long long s_wbar;   // completion of the weight copies
-    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&s_wbar));
+    __shared__ __align__(8) unsigned long long s_wbar[kSmallMaxLayers];   // each layer's weight copies
+    // Both networks' descriptors (dims, tensor addresses: read throughout the rows phase)
+    // copied from the launch parameters into shared memory, one word per thread at once,
+    // instead of a chain of dependent parameter reads.
+    __shared__ __align__(8) SmallNet s_net[2];
+    static_assert(sizeof(SmallNet) % 4 == 0, "SmallNet is copied as 4-byte words");
+    {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(&P.net[0]);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(&s_net[0]);
+      for (int e = threadIdx.x; e < (int)(2 * sizeof(SmallNet) / 4); e += kT) dst[e] = src[e];
+    }
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&s_wbar[0]));
     if (threadIdx.x == 0) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+      for (int l = 0; l < kSmallMaxLayers; ++l)
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar + 8u * l) : "memory");
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -796,7 +812,7 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
     const int64_t rb = (int64_t)blockIdx.x * P.rows_per_cta;
     const int64_t re = min(rb + P.rows_per_cta, P.rows);
     for (int i = 0; i < 2; ++i)
-      if (P.net[i].L) net_rows(P, P.net[i], rb, re, bar, phase);
+      if (s_net[i].L) net_rows(P, s_net[i], rb, re, bar, phase);
   }
   SS_MARK(5);
   ok = grid_barrier(target, P, P.withhold == blockIdx.x + 1u);

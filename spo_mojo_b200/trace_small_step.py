@@ -9,10 +9,11 @@ in microseconds from the earliest CTA's start, and the SM clock over the kernel.
 
     python -m spo_mojo_b200.trace_small_step c0 c1 [--steps 300]
 
-Marks: 0 start, 13 weight copies issued, 1 weights and first input rows in shared
-memory, 2 forward done, 3 loss done, 9 + l layer l's backward done, 12 layer 1's dW done
-(a barrier is added there in the trace build), 4 last row block done, 5 rows phase done,
-6 after the grid barrier, 7 reduction and Adam done, 8 exit.
+Marks: 0 start, 13 weight copies issued and the first block's input rows loaded, 1 the
+block's loss inputs in shared memory, 2 forward done (each layer waits for its own
+weights first), 3 loss done, 9 + l layer l's backward done, 12 layer 1's dW done (a
+barrier is added there in the trace build), 4 last row block done, 5 rows phase done, 6
+after the grid barrier, 7 reduction and Adam done, 8 exit.
 """
 
 import argparse
