@@ -281,52 +281,55 @@ head_kernel(const HeadParams p) {
             zp2[1][2 * c + 1] = __ffma2_rn(aa1, wb, zp2[1][2 * c + 1]);
           }
         }
+        // transpose-reduce each row: lane L ends with the sum of its row's zp[L & 15] over
+        // its half of the warp
+        float zr[2];
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
-          if (k == 1 && !two) break;
-          const int rr = k ? r2 : r;
-          const int64_t row = r0 + rr;
-          const float2* zk = zp2[k];
-      float zp[16];
+          float zp[16];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) {
-        zp[2 * a] = zk[a].x;
-        zp[2 * a + 1] = zk[a].y;
-      }
-      // transpose-reduce: lane L ends with the sum of zp[L & 15] over the warp
+          for (int a = 0; a < 8; ++a) {
+            zp[2 * a] = zp2[k][a].x;
+            zp[2 * a + 1] = zp2[k][a].y;
+          }
 #pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) {
-        const bool upper = (lane & o) != 0;
+          for (int o = 8; o >= 1; o >>= 1) {
+            const bool upper = (lane & o) != 0;
 #pragma unroll
-        for (int i = 0; i < o; ++i) {
-          const float send = upper ? zp[i] : zp[i + o];
-          const float keep = upper ? zp[i + o] : zp[i];
-          zp[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            for (int i = 0; i < o; ++i) {
+              const float send = upper ? zp[i] : zp[i + o];
+              const float keep = upper ? zp[i + o] : zp[i];
+              zp[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+          }
+          zr[k] = zp[0];
         }
-      }
-      const float zv = zp[0] + __shfl_xor_sync(0xffffffffu, zp[0], 16) + lbias;
+        // one exchange completes both rows: lanes 0-15 hold row r, lanes 16-31 row r2, so
+        // the masked softmax, the loss terms and dz below run once for the two rows
+        const bool up = lane >= 16;
+        const float zv = (up ? zr[1] : zr[0]) + __shfl_xor_sync(0xffffffffu, up ? zr[0] : zr[1], 16) + lbias;
+        const int rr = up ? r2 : r;
+        const bool rvalid = !up || two;     // no second row in the last pass of an odd count
+        const bool lv = lvalid && rvalid;
+        const int64_t row = r0 + rr;
 
       float dz = 0.f;
       if (p.mode == kHeadCritic) {
-        if (lvalid) {
-          const float d = zv - rq[rr * A + la];
-          dz = d * p.scale;
-          const float l2 = half_sum(0.5f * d * d * p.scale);
-          if (lane == 0) st[kStatCriticLoss] += l2;
-          if (p.out_logits && lane < A) p.out_logits[row * A + la] = zv;
-        } else {
-          half_sum(0.f);
-        }
+        const float d = lv ? zv - rq[rr * A + la] : 0.f;
+        dz = d * p.scale;
+        const float l2 = half_sum(0.5f * d * d * p.scale);
+        if (la == 0 && rvalid) st[kStatCriticLoss] += l2;
+        if (p.out_logits && lv) p.out_logits[row * A + la] = zv;
       } else {
         float mk = 1.f, qv = 0.f;
-        if (lvalid) {
+        if (lv) {
           const float m = rm[rr * A + la];
           mk = p.mask ? m : (from_cells ? (m == 0.f ? 1.f : 0.f) : 1.f);
           qv = rq[rr * A + la];
         }
-        const float zm = (!lvalid || mk == 0.f) ? kNegInf : zv;
+        const float zm = (!lv || mk == 0.f) ? kNegInf : zv;
         const float mx = half_max(zm);
-        const float e = lvalid ? expf(zm - mx) : 0.f;
+        const float e = lv ? expf(zm - mx) : 0.f;
         const float s = half_sum(e);
         const float inv_s = 1.f / s;
         const float lse = mx + logf(s);
@@ -334,37 +337,35 @@ head_kernel(const HeadParams p) {
         const float lp = zm - lse;
         float po = 0.f, klo_t = 0.f;
         if (p.z_old != nullptr) {
-          const float zo = (!lvalid || mk == 0.f) ? kNegInf : rz[rr * A + la];
+          const float zo = (!lv || mk == 0.f) ? kNegInf : rz[rr * A + la];
           const float mxo = half_max(zo);
-          const float eo = lvalid ? expf(zo - mxo) : 0.f;
+          const float eo = lv ? expf(zo - mxo) : 0.f;
           const float so = half_sum(eo);
           const float inv_so = 1.f / so, lseo = mxo + logf(so);
           po = eo * inv_so;
-          if (lvalid && po > 0.f) klo_t = po * ((zo - lseo) - lp);
+          if (lv && po > 0.f) klo_t = po * ((zo - lseo) - lp);
         }
-        const float ce = half_sum((lvalid && qv != 0.f) ? -qv * lp : 0.f);
-        const float hq = half_sum((lvalid && qv > 0.f) ? -qv * logf(qv) : 0.f);
+        const float ce = half_sum((lv && qv != 0.f) ? -qv * lp : 0.f);
+        const float hq = half_sum((lv && qv > 0.f) ? -qv * logf(qv) : 0.f);
         const float klo = half_sum(klo_t);
-        dz = (!lvalid || mk == 0.f) ? 0.f : ((pi - qv) + alpha * (pi - po)) * p.scale;
-        if (lane == 0) {
+        dz = (!lv || mk == 0.f) ? 0.f : ((pi - qv) + alpha * (pi - po)) * p.scale;
+        if (la == 0 && rvalid) {
           st[kStatActorLoss] += (ce + alpha * klo) * p.scale;
           st[kStatCE] += ce * p.scale;
           st[kStatEntropy] += hq * p.scale;
           st[kStatKLq] += (ce - hq) * p.scale;
           st[kStatKLold] += klo * p.scale;
         }
-        if (lane < A) {
+        if (lv) {
           if (p.out_logits) p.out_logits[row * A + la] = zm;
           if (p.out_pi) p.out_pi[row * A + la] = pi;
         }
       }
-      if (lane < A) {
+      if (lv) {
         if (p.dz_out) p.dz_out[row * A + la] = dz;
         dbl += dz;
       }
-      if (lane < AP) dzs[rr * AP + lane] = dz;  // dz is 0 on the padding lanes
-
-        }
+      if (la < AP && rvalid) dzs[rr * AP + la] = dz;  // dz is 0 on the padding lanes
       }
     }
     __syncthreads();
@@ -486,6 +487,10 @@ head_kernel(const HeadParams p) {
   }
   __syncthreads();
   constexpr int RW = AP + kStats;
+  // lanes 16-31 hold the sums of the second row of each pair (zero where unused)
+  dbl += __shfl_xor_sync(0xffffffffu, dbl, 16);
+#pragma unroll
+  for (int s = 0; s < kStats; ++s) st[s] += __shfl_xor_sync(0xffffffffu, st[s], 16);
   if (lane < A) red[warp * RW + lane] = dbl;
   if (lane == 0)
 #pragma unroll
