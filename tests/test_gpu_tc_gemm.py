@@ -75,7 +75,8 @@ def test_split_keeps_nan_and_infinities(keep_positive):
     assert h[11] == 1.0 and lo.cpu().numpy()[11] == 0
 
 
-@pytest.mark.parametrize("M,K,N", [(128, 128, 128), (1000, 256, 256), (4096, 512, 512), (300, 1024, 1024)])
+@pytest.mark.parametrize("M,K,N", [(128, 128, 128), (1000, 256, 256), (4096, 512, 512), (300, 1024, 1024),
+                                   (4099, 32, 512), (1000, 32, 1024), (77, 32, 256)])
 def test_forward_bias_relu(M, K, N):
     f = ffi()
     g = torch.Generator(device="cuda").manual_seed(M + K + N)
@@ -130,7 +131,8 @@ def pack_mask(m):
     return np.packbits(np.asarray(m, bool), axis=1, bitorder="little").view(np.uint32)
 
 
-@pytest.mark.parametrize("M,K,N", [(1000, 256, 256), (4096, 512, 512), (300, 1024, 1024)])
+@pytest.mark.parametrize("M,K,N", [(1000, 256, 256), (4096, 512, 512), (300, 1024, 1024), (4099, 32, 512),
+                                   (1000, 32, 1024)])
 def test_forward_writes_packed_relu_mask(M, K, N):
     f = ffi()
     g = torch.Generator(device="cuda").manual_seed(7 * M + K)
