@@ -417,15 +417,19 @@ SPO_API int spo_learner_apply(spo_learner_t learner, spo_stream_t stream, const 
 SPO_API int spo_learner_cache(spo_learner_t learner, int32_t which, int32_t layer,
                               const float** hi, const float** lo);
 /* Reads (synchronously) and clears the learner's device error word: 0 when every
- * bounded wait of its tensor-core kernels completed since the last call. */
+ * bounded wait of its kernels completed since the last call (tensor-core GEMM waits 1-6,
+ * a grid-barrier wait of the one-launch step 16, its weight copies 17; a step whose wait
+ * ran out applied no update). */
 SPO_API int spo_learner_status(spo_learner_t learner, int32_t* device_error);
 /* Batches of at most max_rows rows run the whole step (or the backward of
  * spo_learner_backward) as ONE cooperative launch whose phases are separated by grid-wide
  * barriers, instead of ~10 dependent launches; 0 turns that off. The default is
- * min(8192, desc.max_rows) when every network has 2-4 layers, an input at most 32 wide and
- * hidden widths that are multiples of 32 up to 256 (else 0, and nonzero values are
- * refused). Results agree with the multi-launch path within the fp32 tolerances; the
- * reduction order of the partial sums differs, so the two are not bit-identical.
+ * min(8192, desc.max_rows) when every network has 2-4 layers, an input at most 32 wide,
+ * hidden widths that are multiples of 32 up to 256, at most 65,536 parameters, and its
+ * weights, biases and a 32-row block of activations fit in 220 KB of shared memory (else
+ * 0, and nonzero values are refused). Results agree with the multi-launch path within the
+ * fp32 tolerances; the reduction order of the partial sums differs, so the two are not
+ * bit-identical.
  * No reference counterpart (the reference's update() is ~35 launches,
  * demos/train_spo.mojo:417-554). */
 SPO_API int spo_learner_set_small_rows(spo_learner_t learner, int64_t max_rows);
