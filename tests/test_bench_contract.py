@@ -74,3 +74,37 @@ def test_small_step_eligibility_follows_the_shared_memory_layout():
     # 27-256-256-9: 82 k weights do not fit beside the activations of a 32-row block
     assert not bench.small_step_fits(Workload("w", actor=NetSpec((27, 256, 256, 9)), batch=64), 64)
     assert not bench.small_step_fits(WORKLOADS["c2"], 4096)
+
+
+def test_clock_sampler_reports_the_timed_region():
+    """The sampler's parsing and window: samples taken during the timed region are the ones
+    reported (with any active throttle reason); when the region was shorter than the
+    sampling interval, the samples since start() stand in, and the window says so."""
+    import time
+
+    class FakeProc:
+        def terminate(self):
+            pass
+
+        def wait(self, timeout=None):
+            return 0
+
+        def kill(self):
+            pass
+
+    idle = "0, 1965, 1965, 500, 0x0, Not Active, Not Active, Not Active, Not Active\n"
+    capped = "0, 1700, 1965, 990, 0x4, Not Active, Not Active, Not Active, Active\n"
+    c = bench.ClockSampler([0])
+    c.proc = FakeProc()
+    now = time.perf_counter()
+    c.lines = [(now - 1.0, idle), (now + 0.01, capped)]
+    c.t_mark = now
+    clk = c.stop()
+    assert clk["sm_mhz"] == 1700.0 and clk["sm_max_mhz"] == 1965.0 and clk["reasons"] == ["sw_power_cap"]
+    assert clk["samples"] == 1 and clk["window"] == "timed region"
+    c = bench.ClockSampler([0])
+    c.proc = FakeProc()
+    c.lines = [(now - 1.0, idle)]
+    c.t_mark = time.perf_counter()
+    clk = c.stop()
+    assert clk["sm_mhz"] == 1965.0 and clk["samples"] == 1 and clk["window"].startswith("warm-up")
