@@ -348,8 +348,8 @@ def small_step_fits(wl, rows):
             return False
         dmax = max([pad4(d[-1])] + d[1:-1])
         f = 32 * 32 + 32 * 28 + 8 * 8 + 32 * sum(d[1:-1]) + 2 * 32 * dmax
-        wst = lambda n: n + 4 if n % 32 == 0 else n  # noqa: E731  (hidden rows padded by 16 B)
-        f += sum((32 if i == 0 else d[i]) * wst(d[i + 1]) + pad4(d[i + 1]) for i in range(L))
+        f += 255  # to the 1024-byte boundary of the weight slabs
+        f += sum((32 if i == 0 else d[i]) * d[i + 1] + pad4(d[i + 1]) for i in range(L))
         if f > SMALL_MAX_SMEM_FLOATS:
             return False
     return True

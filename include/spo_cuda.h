@@ -429,7 +429,9 @@ SPO_API int spo_learner_status(spo_learner_t learner, int32_t* device_error);
  * weights, biases and a 32-row block of activations fit in 220 KB of shared memory (else
  * 0, and nonzero values are refused). Results agree with the multi-launch path within the
  * fp32 tolerances; the reduction order of the partial sums differs, so the two are not
- * bit-identical.
+ * bit-identical. The first such step on a parameter buffer copies the tensor maps of its
+ * weights into the workspace (stream-ordered); under stream capture that step is refused
+ * (SPO_ERR_UNSUPPORTED): run one step on the buffer before capturing.
  * No reference counterpart (the reference's update() is ~35 launches,
  * demos/train_spo.mojo:417-554). */
 SPO_API int spo_learner_set_small_rows(spo_learner_t learner, int64_t max_rows);

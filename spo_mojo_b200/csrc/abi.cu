@@ -269,6 +269,9 @@ struct NetPlan {
   float* sm_pw[SPO_MAX_LAYERS] = {};   // [grid][d_l x d_{l+1}]
   float* sm_pb[SPO_MAX_LAYERS] = {};   // [grid][d_{l+1}]
   float* sm_pstats = nullptr;          // [grid][kStats]
+  // the tensor maps of the hidden layers' W (encoded for the parameter buffer at sm_wmap_of)
+  CUtensorMap sm_wmap[kSmallMaxLayers - 1] = {};
+  const float* sm_wmap_of = nullptr;
 };
 
 }  // namespace spo
@@ -285,6 +288,7 @@ struct spo_learner {
   int64_t small_rows = 0;
   int sm_grid = 0;
   float* sm_sumsq = nullptr;            // [kMaxGroups][sm_grid]
+  CUtensorMap* sm_wmap = nullptr;       // [2][kSmallMaxLayers - 1]: the networks' weight maps
   unsigned* sm_sync = nullptr;          // barrier words, zero between launches
   bool last_small = false;              // the last forward ran in the small step
 };
@@ -487,6 +491,7 @@ int build_plan(const spo_learner_desc* desc, spo_learner* L, void* ws, size_t* b
       n.sm_pstats = c.take<float>((size_t)G * kStats);
     }
     L->sm_sumsq = c.take<float>((size_t)kMaxGroups * G);
+    L->sm_wmap = c.take<CUtensorMap>(2 * (kSmallMaxLayers - 1));
   }
   *bytes = c.off + 256;
   return kOk;
@@ -828,8 +833,9 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
   p.parts = (int)ceil_div(b->rows, p.rows_per_cta);
   const float* stats_src[2] = {nullptr, nullptr};
   int stats_parts[2] = {0, 0};
+  bool upload = false;   // a network's weight maps were encoded anew
   for (int i = 0; i < 2; ++i) {
-    const NetPlan& n = Lr->net[i];
+    NetPlan& n = Lr->net[i];
     SmallNet& sn = p.net[i];
     if (!n.present) continue;
     const spo_mlp_desc& d = n.d;
@@ -849,12 +855,42 @@ int small_step(spo_learner* Lr, cudaStream_t s, const spo_batch* b, float scale,
     }
     sn.pstats = n.sm_pstats;
     for (int l = 0; l + 1 < d.num_layers; ++l) sn.gact[l] = n.acts[l];   // the activation cache
+    if (n.sm_wmap_of != prm) {   // a new parameter buffer: encode its hidden layers' maps
+      for (int l = 0; l + 1 < d.num_layers; ++l) {
+        int rc = small_weight_map(&n.sm_wmap[l], prm + n.w_off[l], l, d.dims[l], d.dims[l + 1]);
+        if (rc) {
+          n.sm_wmap_of = nullptr;
+          return rc;
+        }
+      }
+      n.sm_wmap_of = prm;
+      upload = true;
+    }
     add_gap_segs(p.red, d, n.w_off, n.b_off, n.size, grads);
     stats_src[i] = n.sm_pstats;
     stats_parts[i] = p.parts;
   }
   add_stats_segs(p.red, Lr, st->grads, stats_src, stats_parts);
   SPO_CHECK_ARG(p.red.nseg <= kMaxSegs, kErrUnsupported, "too many reduction segments");
+  if (upload) {   // the maps into device memory, ahead of the launch on the same stream
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cs);
+    if (cs != cudaStreamCaptureStatusNone) {
+      for (int i = 0; i < 2; ++i) Lr->net[i].sm_wmap_of = nullptr;
+      return set_error(kErrUnsupported, "small step: the first step on a parameter buffer must run outside "
+                                        "stream capture (it uploads the weights' tensor maps)");
+    }
+    CUtensorMap maps[2][kSmallMaxLayers - 1] = {};
+    for (int i = 0; i < 2; ++i)
+      for (int l = 0; Lr->net[i].present && l + 1 < Lr->net[i].d.num_layers; ++l) maps[i][l] = Lr->net[i].sm_wmap[l];
+    // pageable source: staged before the call returns, so the local array may go
+    cudaError_t ce = cudaMemcpyAsync(Lr->sm_wmap, maps, sizeof(maps), cudaMemcpyHostToDevice, s);
+    if (ce != cudaSuccess) {
+      for (int i = 0; i < 2; ++i) Lr->net[i].sm_wmap_of = nullptr;
+      return set_error(kErrCuda, std::string("small step: tensor maps: ") + cudaGetErrorString(ce));
+    }
+  }
+  p.wmap = Lr->sm_wmap;
   int64_t e = 0;
   for (int k = 0; k < p.red.nseg; ++k) {
     p.seg_start[k] = e;

@@ -32,6 +32,7 @@
 #include "spo_common.cuh"
 #include "kernels.cuh"
 #include "small_step.cuh"
+#include "tc_gemm.cuh"
 
 namespace spo {
 
@@ -134,17 +135,21 @@ extern __shared__ __align__(16) float smem[];
 
 __device__ __forceinline__ float4 lds4(int off) { return *reinterpret_cast<const float4*>(&smem[off]); }
 
-// The weights of every layer stay in shared memory for the whole step of the CTA, W_l
-// [d_l x d_{l+1}] row-major. A hidden layer's rows (width N a multiple of 32) are padded
-// by 16 bytes (row stride N + 4): a row read across consecutive columns (the forward) is
-// contiguous, and a float4 read of consecutive rows at one column (dX) steps 16 bytes
-// across the banks every row, so both are conflict-free, and every row is one contiguous
-// bulk copy. The output layer (width 9 or 1, odd) is stored as it is (one bulk copy): a
-// column read by consecutive rows is conflict-free. The first layer's weights are padded
-// with zero rows to 32 (the input rows are 32 wide, zero past d0). The biases follow,
-// each padded to a multiple of 4.
+// The weights of every layer stay in shared memory for the whole step of the CTA. A hidden
+// layer's W_l [K x N] (N a multiple of 32) is held as N / 32 slabs of 32 columns, each
+// [K x 32] with rows of 128 bytes, 128-byte swizzled: the 16-byte chunk q of row k sits at
+// chunk q ^ (k & 7), so column n of row k is word (n & 31) ^ ((k & 7) << 2) of the row
+// (w_at). A row read across 32 consecutive columns (the forward) then touches every bank
+// once, and so does a float4 read of 8 consecutive rows at one column (dX). Each slab is
+// one 2-D tensor copy (the copy engine applies the swizzle), with the first layer's rows
+// past d0 zero-filled up to 32 (the input rows are 32 wide, zero past d0); the slabs start
+// on 1024-byte boundaries, the period of the swizzle. The output layer (width 9 or 1) is
+// stored as it is (one bulk copy): a column read by consecutive rows is conflict-free. The
+// biases follow, each padded to a multiple of 4.
 __host__ __device__ inline int wrows(int l, int k) { return l == 0 ? 32 : k; }
-__host__ __device__ inline int wst(int n) { return n % 32 == 0 ? n + 4 : n; }
+
+// Float offset of W[k][n] within a hidden layer's slabs (K rows each).
+__device__ __forceinline__ int w_at(int K, int k, int n) { return (n >> 5) * K * 32 + k * 32 + ((n & 31) ^ ((k & 7) << 2)); }
 
 // Register tiles of the row-block products. A warp owns TR rows (r = h + rg i, one row
 // group h per warp, so the row operands are shared-memory broadcasts) and 32 TC columns
@@ -196,6 +201,7 @@ __device__ __noinline__ void block_forward_t(int in, int ks, int K, int w, int b
   if (warp >= cg * rg) return;
   const int g = warp % cg, h = warp / cg;
   const int c0 = 32 * TC * g + lane;
+  const int ws = w + TC * g * K * 32;   // the warp's first slab: columns 32 TC g ..
   float acc[TR][TC];
 #pragma unroll
   for (int i = 0; i < TR; ++i)
@@ -203,11 +209,13 @@ __device__ __noinline__ void block_forward_t(int in, int ks, int K, int w, int b
     for (int j = 0; j < TC; ++j) acc[i][j] = 0.f;
 #pragma unroll 2
   for (int k = 0; k < K; k += 4) {
+    // row k + u (k % 4 == 0): column lane at word lane ^ ((k & 4) << 2) ^ (u << 2) (w_at)
+    const int wk = ws + k * 32, lx = lane ^ ((k & 4) << 2);
     float wv[4][TC];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
 #pragma unroll
-      for (int j = 0; j < TC; ++j) wv[u][j] = smem[w + (k + u) * (N + 4) + c0 + 32 * j];
+      for (int j = 0; j < TC; ++j) wv[u][j] = smem[wk + u * 32 + j * K * 32 + (lx ^ (u << 2))];
     float4 x[TR];   // rows past R read the block's unused buffer rows; never stored
 #pragma unroll
     for (int i = 0; i < TR; ++i) x[i] = lds4(in + (h + rg * i) * ks + k);
@@ -253,15 +261,14 @@ __device__ __noinline__ void block_dx_t(int dz, int zs, int N, int w, int K, int
   for (int i = 0; i < TR; ++i)
 #pragma unroll
     for (int j = 0; j < TC; ++j) acc[i][j] = 0.f;
-  if (N % 32 == 0) {   // padded rows: one float4 of each of the TC rows per 4 n
+  if (N % 32 == 0) {   // swizzled slabs: one float4 of each of the TC rows per 4 n
+    const int wc = w + c0 * 32, cx = (lane & 7) << 2;   // row c = c0 + 32 j: c & 7 == lane & 7
 #pragma unroll 1
     for (int n = 0; n < N; n += 4) {
+      const int off = wc + (n >> 5) * K * 32 + ((n & 31) ^ cx);   // w + w_at(K, c0, n); row c0 + 32 j: + 1024 j
       float4 wv[TC];
 #pragma unroll
-      for (int j = 0; j < TC; ++j) {
-        const int c = c0 + 32 * j;
-        wv[j] = lds4(w + c * (N + 4) + n);
-      }
+      for (int j = 0; j < TC; ++j) wv[j] = lds4(off + 32 * 32 * j);
       float4 z[TR];   // rows past R read the block's unused buffer rows; never stored
 #pragma unroll
       for (int i = 0; i < TR; ++i) z[i] = lds4(dz + (h + rg * i) * zs + n);
@@ -329,6 +336,31 @@ __device__ void block_dx(int dz, int zs, int N, int w, int K, int act, int out, 
   SPO_TILE_DISPATCH(block_dx_t, dz, zs, N, w, K, act, out, R);
 }
 
+// One row of a dW tile: its dz values (4 columns of the lane) and the KI float4 of its
+// input that the warp's dW rows take.
+template <int KI>
+__device__ __forceinline__ void dw_load(int in, int dz, int c0, int nj, int warp, float (&z)[4], float4 (&a)[KI]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) z[j] = j < nj ? smem[dz + c0 + 32 * j] : 0.f;
+#pragma unroll
+  for (int i = 0; i < KI; ++i) a[i] = lds4(in + 4 * warp + 4 * kW * i);
+}
+
+template <int KI>
+__device__ __forceinline__ void dw_row(float (&acc)[KI][4][4], float (&db)[4], const float (&z)[4],
+                                       const float4 (&a)[KI]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) db[j] += z[j];
+#pragma unroll
+  for (int i = 0; i < KI; ++i) {
+    const float av[4] = {a[i].x, a[i].y, a[i].z, a[i].w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][q][j] = fmaf(av[q], z[j], acc[i][q][j]);
+  }
+}
+
 // pw[K x N] (+)= in[R x K]^T dz[R x N] and pb[N] (+)= sum of the rows of dz over this
 // block's R rows (in: stride ks, zero past K up to a multiple of 4; dz: stride zs).
 // N % 32 == 0: warp w owns the rows k = 4w + 4 kW i + q (q < 4, i < KI), lane the column
@@ -349,23 +381,17 @@ __device__ __noinline__ void block_dw_t(int in, int ks, int K, int dz, int zs, i
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][q][j] = 0.f;
     float db[4] = {0.f, 0.f, 0.f, 0.f};
+    // two register sets of row operands: row r + 1's load under row r's FMAs
+    float z0[4], z1[4];
+    float4 a0[KI], a1[KI];
+    dw_load<KI>(in, dz, c0, nj, warp, z0, a0);
 #pragma unroll 1
-    for (int r = 0; r < R; ++r) {
-      float z[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        z[j] = j < nj ? smem[dz + r * zs + c0 + 32 * j] : 0.f;
-        db[j] += z[j];
-      }
-#pragma unroll
-      for (int i = 0; i < KI; ++i) {
-        const float4 a = lds4(in + r * ks + 4 * warp + 4 * kW * i);
-        const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][q][j] = fmaf(av[q], z[j], acc[i][q][j]);
-      }
+    for (int r = 0; r < R; r += 2) {
+      dw_load<KI>(in + min(r + 1, R - 1) * ks, dz + min(r + 1, R - 1) * zs, c0, nj, warp, z1, a1);
+      dw_row<KI>(acc, db, z0, a0);
+      if (r + 1 >= R) break;
+      dw_load<KI>(in + min(r + 2, R - 1) * ks, dz + min(r + 2, R - 1) * zs, c0, nj, warp, z0, a0);
+      dw_row<KI>(acc, db, z1, a1);
     }
     if (first) {   // stores only: no load may sit in front of them
 #pragma unroll
@@ -403,47 +429,58 @@ __device__ __noinline__ void block_dw_t(int in, int ks, int K, int dz, int zs, i
   }
 }
 
-// The output layer (N <= kSmallMaxA): thread t owns row k = t of dW and all N columns.
-__device__ __noinline__ void block_dw_out(int in, int ks, int K, int dz, int zs, int N, int R, float* pw, float* pb,
-                                          bool first) {
+// The output layer (N <= NA <= kSmallMaxA): thread t owns row k = t of dW and all N
+// columns; thread 0 also sums the rows of dz for the bias.
+template <int NA>
+__device__ __noinline__ void block_dw_out_t(int in, int ks, int K, int dz, int zs, int N, int R, float* pw,
+                                            float* pb, bool first) {
   for (int k = threadIdx.x; k < K; k += kT) {
-    float acc[kSmallMaxA] = {};
-#pragma unroll 1
+    float acc[NA] = {}, db[NA] = {};
+#pragma unroll 4
     for (int r = 0; r < R; ++r) {
       const float a = smem[in + r * ks + k];
-      float z[kSmallMaxA];   // dz rows are zero past N up to their stride (a multiple of 4 >= N)
+      float z[NA];   // dz rows are zero past N up to their stride (a multiple of 4 >= N)
 #pragma unroll
-      for (int j = 0; j < kSmallMaxA; ++j) z[j] = j < zs ? smem[dz + r * zs + j] : 0.f;
+      for (int j = 0; j < NA; ++j) z[j] = j < zs ? smem[dz + r * zs + j] : 0.f;
 #pragma unroll
-      for (int j = 0; j < kSmallMaxA; ++j) acc[j] = fmaf(a, z[j], acc[j]);
+      for (int j = 0; j < NA; ++j) {
+        acc[j] = fmaf(a, z[j], acc[j]);
+        db[j] += z[j];
+      }
     }
     float* p = pw + (int64_t)k * N;
     if (first) {
 #pragma unroll
-      for (int j = 0; j < kSmallMaxA; ++j)
+      for (int j = 0; j < NA; ++j)
         if (j < N) __stcg(p + j, acc[j]);
+      if (k == 0)
+#pragma unroll
+        for (int j = 0; j < NA; ++j)
+          if (j < N) __stcg(pb + j, db[j]);
     } else {
-      float old[kSmallMaxA];
+      float old[NA], oldb[NA];
 #pragma unroll
-      for (int j = 0; j < kSmallMaxA; ++j) old[j] = j < N ? ldcg(p + j) : 0.f;
+      for (int j = 0; j < NA; ++j) {
+        old[j] = j < N ? ldcg(p + j) : 0.f;
+        oldb[j] = (k == 0 && j < N) ? ldcg(pb + j) : 0.f;
+      }
 #pragma unroll
-      for (int j = 0; j < kSmallMaxA; ++j)
+      for (int j = 0; j < NA; ++j)
         if (j < N) __stcg(p + j, old[j] + acc[j]);
+      if (k == 0)
+#pragma unroll
+        for (int j = 0; j < NA; ++j)
+          if (j < N) __stcg(pb + j, oldb[j] + db[j]);
     }
-  }
-  for (int j = threadIdx.x; j < N; j += kT) {
-    float s = 0.f;
-    for (int r = 0; r < R; ++r) s += smem[dz + r * zs + j];
-    if (first)
-      __stcg(pb + j, s);
-    else
-      __stcg(pb + j, ldcg(pb + j) + s);
   }
 }
 
 __device__ void block_dw(int in, int ks, int K, int dz, int zs, int N, int R, float* pw, float* pb, bool first) {
   if (N % 32 != 0) {
-    block_dw_out(in, ks, K, dz, zs, N, R, pw, pb, first);
+    if (N == 1)
+      block_dw_out_t<1>(in, ks, K, dz, zs, N, R, pw, pb, first);
+    else
+      block_dw_out_t<kSmallMaxA>(in, ks, K, dz, zs, N, R, pw, pb, first);
     return;
   }
   for (int k0 = 0; k0 < K; k0 += 128) {   // 128 rows of dW per pass
@@ -527,22 +564,25 @@ __device__ __noinline__ void block_loss(bool actor, bool has_mask, bool has_old,
 
 // Shared memory of one network's row block, in floats: x [kR x 32] | loss inputs
 // [kR x kLossIn] | per-warp statistics [kW x kStats] | a_0 .. a_{L-2} [kR x d_{l+1}] |
-// dz ping-pong 2 x [kR x dmax] | W_0 .. W_{L-1} [wrows x wst(d_{l+1})] | b_0 .. b_{L-1}
-// [pad4(d_{l+1})]; every region starts on a 16-byte boundary.
+// dz ping-pong 2 x [kR x dmax] | up to 255 floats to the next 1024-byte boundary | W_0 ..
+// W_{L-1} [wrows x d_{l+1}] | b_0 .. b_{L-1} [pad4(d_{l+1})]; every region starts on a
+// 16-byte boundary, every hidden layer's W on a 1024-byte one (their sizes are multiples
+// of 4096 bytes).
 __host__ __device__ inline int small_dmax(const int* dims, int L) {
   int dmax = (dims[L] + 3) & ~3;
   for (int l = 1; l < L; ++l) dmax = dims[l] > dmax ? dims[l] : dmax;
   return dmax;
 }
 __host__ __device__ inline int small_acts_base() { return kR * 32 + kR * kLossIn + kW * kStats; }
+// the end of the dz buffers (W_0 starts at the next 1024-byte boundary after it)
 __host__ __device__ inline int small_w_base(const int* dims, int L) {
   int f = small_acts_base();
   for (int l = 1; l < L; ++l) f += kR * dims[l];
   return f + 2 * kR * small_dmax(dims, L);
 }
 __host__ __device__ inline int small_smem_floats(const int* dims, int L) {
-  int f = small_w_base(dims, L);
-  for (int l = 0; l < L; ++l) f += wrows(l, dims[l]) * wst(dims[l + 1]) + ((dims[l + 1] + 3) & ~3);
+  int f = small_w_base(dims, L) + 255;
+  for (int l = 0; l < L; ++l) f += wrows(l, dims[l]) * dims[l + 1] + ((dims[l + 1] + 3) & ~3);
   return f;
 }
 
@@ -576,9 +616,23 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bytes of layer l's weights and bias as staged (its bulk copies' total).
+// Bytes of layer l's weights and bias as staged (its copies' total; a hidden layer's slabs
+// count their zero-filled rows).
 __device__ __forceinline__ uint32_t staged_bytes(const SmallNet& n, int l) {
-  return 4u * (n.dims[l] * n.dims[l + 1] + ((n.dims[l + 1] + 3) & ~3));
+  return 4u * (wrows(l, n.dims[l]) * n.dims[l + 1] + ((n.dims[l + 1] + 3) & ~3));
+}
+
+// The first float offset at or after f whose shared-memory address is 1024-byte aligned.
+__device__ __forceinline__ int align_1k(int f) { return f + (int)(((1024u - (smem_u32(f) & 1023u)) & 1023u) >> 2); }
+
+// One 2-D tensor copy: the box at columns x.., rows y.. of the tensor map's array into
+// shared memory at dst (completion counted in bytes on the mbarrier bar).
+__device__ __forceinline__ void tensor_copy(int dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
 }
 
 // Bounded wait for the weight copies (parity phase of bar). On expiry: the step's abort
@@ -601,34 +655,34 @@ __device__ bool wait_staged(uint32_t bar, uint32_t parity, const SmallStepParams
 }
 
 // Every layer's weights (at wbase, the layout above) and biases (at bbase) into shared
-// memory by bulk copies: one per hidden-layer row, one for the output layer, one per bias
-// (the flat parameter buffer pads every tensor to 64 floats, so a bias padded to 4 is
-// still inside it); the first layer's padding rows zeroed. Layer l's copies complete on
-// the mbarrier bar0 + 8 l, which thread 0 has armed with that layer's bytes: the forward
-// of a layer waits for its own weights only.
-__device__ void stage_weights(const SmallNet& n, int wbase, int bbase, uint32_t bar0) {
+// memory: a hidden layer's slabs by one tensor copy each (map wmap[l]: the layer's W with
+// a box of 32 columns x wrows rows, 128-byte swizzle, zero fill past d_l), the output
+// layer by one bulk copy, each bias by one bulk copy (the flat parameter buffer pads every
+// tensor to 64 floats, so a bias padded to 4 is still inside it). Layer l's copies complete
+// on the mbarrier bar0 + 8 l, which thread 0 has armed with that layer's bytes: the
+// forward of a layer waits for its own weights only. Warp l issues layer l's slab copies.
+__device__ void stage_weights(const SmallNet& n, const CUtensorMap* wmap, int wbase, int bbase, uint32_t bar0) {
   int w = wbase, b = bbase;
   for (int l = 0; l < n.L; ++l) {
-    const int K = n.dims[l], N = n.dims[l + 1];
-    const float* src = n.W[l];
+    const int K = wrows(l, n.dims[l]), N = n.dims[l + 1];
     const uint32_t bar = bar0 + 8u * l;
     if (N % 32 == 0) {
-      for (int r = threadIdx.x; r < K; r += kT) bulk_copy(w + r * (N + 4), src + (int64_t)r * N, 4u * N, bar);
+      const int t = threadIdx.x - 32 * l;
+      if (t >= 0 && t < N / 32) tensor_copy(w + t * K * 32, wmap + l, 32 * t, 0, bar);
     } else if (threadIdx.x == kT - 1) {
-      bulk_copy(w, src, 4u * K * N, bar);
+      bulk_copy(w, n.W[l], 4u * K * N, bar);
     }
-    for (int e = K * wst(N) + threadIdx.x; e < wrows(l, K) * wst(N); e += kT) smem[w + e] = 0.f;
     if (threadIdx.x == kT - 2 - l) bulk_copy(b, n.b[l], 4u * ((N + 3) & ~3), bar);
-    w += wrows(l, K) * wst(N);
+    w += K * N;
     b += (N + 3) & ~3;
   }
 }
 
 // One network over this CTA's rows [rb, re), 32 rows at a time.
-// bar0: the CTA's mbarriers of the weight copies (one per layer, 8 bytes apart), phase
-// their next parity.
-__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb, int64_t re, uint32_t bar0,
-                         uint32_t& phase) {
+// wmap: the tensor maps of its hidden layers' W; bar0: the CTA's mbarriers of the weight
+// copies (one per layer, 8 bytes apart), phase their next parity.
+__device__ void net_rows(const SmallStepParams& P, const SmallNet& n, const CUtensorMap* wmap, int64_t rb,
+                         int64_t re, uint32_t bar0, uint32_t& phase) {
   const int L = n.L, d0 = n.dims[0];
   const int part = blockIdx.x;
   const bool actor = n.mode == 0;
@@ -636,10 +690,14 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
   const int dmax = small_dmax(n.dims, L);
   int dzb0 = acts0;
   for (int l = 1; l < L; ++l) dzb0 += kR * n.dims[l];
-  const int wbase = small_w_base(n.dims, L);
+  const int wbase = align_1k(small_w_base(n.dims, L));
   int bbase = wbase;
-  for (int l = 0; l < L; ++l) bbase += wrows(l, n.dims[l]) * wst(n.dims[l + 1]);
-  const float alpha = (actor && P.z_old) ? softplus_f(*P.log_alpha) : 0.f;
+  for (int l = 0; l < L; ++l) bbase += wrows(l, n.dims[l]) * n.dims[l + 1];
+  // log_alpha's load is issued here, its softplus taken at the first loss: the load's
+  // latency stays off the path to the weight copies
+  const bool has_kl = actor && P.z_old;
+  const float log_alpha = has_kl ? *P.log_alpha : 0.f;
+  float alpha = 0.f;
   for (int e = threadIdx.x; e < kW * kStats; e += kT) smem[stw + e] = 0.f;
   bool first = true;
   for (int64_t r0 = rb; r0 < re; r0 += kR, first = false) {
@@ -654,7 +712,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
                        : "memory");
       __syncthreads();   // armed before any copy can complete; earlier reads of this memory done
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      stage_weights(n, wbase, bbase, bar0);
+      stage_weights(n, wmap, wbase, bbase, bar0);
     }
     for (int e = threadIdx.x; e < R * kLossIn; e += kT) {
       const int r = e / kLossIn, f = e - r * kLossIn;
@@ -711,7 +769,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
         in = a;
         ks = N;
         a += kR * N;
-        w += K * wst(N);
+        w += K * N;
         b += (N + 3) & ~3;
       }
       SS_MARK(2);
@@ -721,6 +779,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
         phase ^= 1u;   // every layer's barrier has completed this phase
       }
       int zs = (n.dims[L] + 3) & ~3;   // row stride of the gradient in the current dz buffer
+      if (first && has_kl) alpha = softplus_f(log_alpha);
       block_loss(actor, P.mask != nullptr, P.z_old != nullptr, P.scale, n.dims[L - 1], n.dims[L], in, li, R, dzb0,
                  zs, w, b, alpha, stw);
       __syncthreads();
@@ -738,7 +797,7 @@ __device__ void net_rows(const SmallStepParams& P, const SmallNet& n, int64_t rb
         zs = K;
         cur ^= 1;
         if (l >= 1) {   // step back one layer: its weights, its input activations
-          w -= wrows(l - 1, n.dims[l - 1]) * wst(K);
+          w -= wrows(l - 1, n.dims[l - 1]) * K;
           in = l - 1 == 0 ? xs : in - kR * n.dims[l - 1];
         }
         SS_MARK(9 + l);
@@ -790,6 +849,12 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
   SS_MARK(0);
   // ---- rows: forward, loss, backward; per-CTA partial sums
   if (blockIdx.x < P.parts) {
+    {   // the weight slabs' tensor maps into the copy engine's cache, ahead of the copies
+      const int i = threadIdx.x / (kSmallMaxLayers - 1), l = threadIdx.x % (kSmallMaxLayers - 1);
+      if (i < 2 && l + 1 < P.net[i].L)
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(P.wmap + i * (kSmallMaxLayers - 1) + l))
+                     : "memory");
+    }
     __shared__ __align__(8) unsigned long long s_wbar[kSmallMaxLayers];   // each layer's weight copies
     // Both networks' descriptors (dims, tensor addresses: read throughout the rows phase)
     // copied from the launch parameters into shared memory, one word per thread at once,
@@ -812,7 +877,7 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
     const int64_t rb = (int64_t)blockIdx.x * P.rows_per_cta;
     const int64_t re = min(rb + P.rows_per_cta, P.rows);
     for (int i = 0; i < 2; ++i)
-      if (s_net[i].L) net_rows(P, s_net[i], rb, re, bar, phase);
+      if (s_net[i].L) net_rows(P, s_net[i], P.wmap + i * (kSmallMaxLayers - 1), rb, re, bar, phase);
   }
   SS_MARK(5);
   ok = grid_barrier(target, P, P.withhold == blockIdx.x + 1u);
@@ -966,6 +1031,10 @@ extern "C" __attribute__((visibility("default"))) int spo_small_trace_read(unsig
              : -5;
 }
 #endif
+
+int small_weight_map(CUtensorMap* m, const float* W, int l, int rows, int cols) {
+  return make_map(m, W, (uint64_t)cols, (uint64_t)rows, 32u, (uint32_t)wrows(l, rows), CU_TENSOR_MAP_SWIZZLE_128B);
+}
 
 size_t small_step_smem(const spo_mlp_desc* nets, int count) {
   size_t most = 0;

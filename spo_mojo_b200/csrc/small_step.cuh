@@ -1,6 +1,8 @@
 // The one-launch learner step for small batches (small_step.cu): parameters and limits.
 #pragma once
 
+#include <cuda.h>
+
 #include "spo_cuda.h"
 #include "kernels.cuh"
 
@@ -28,6 +30,11 @@ struct SmallNet {
 
 struct SmallStepParams {
   SmallNet net[2];                     // actor, critic
+  // [2][kSmallMaxLayers - 1] in device memory: per network, its hidden layers' W_l
+  // [d_l x d_{l+1}] as boxes of 32 columns x wrows rows (32 for the first layer, d_l after
+  // it), 128-byte swizzle, zero fill past d_l (kept out of the launch parameters, whose
+  // size every launch pays for)
+  const CUtensorMap* wmap;
   const float* obs;                    // [rows x d0], or null: cells
   const float* cells;                  // [rows x 9] board cells
   const float* mask;                   // actor [rows x 9] (null: the empty cells)
@@ -59,5 +66,7 @@ struct SmallStepParams {
 size_t small_step_smem(const spo_mlp_desc* nets, int count);
 int small_step_grid();                 // CTAs of a launch (all co-resident), 0 if unavailable
 int small_step_launch(const SmallStepParams& p, int grid, size_t smem, cudaStream_t s);
+// The tensor map of hidden layer l's W (rows d_l, columns d_{l+1}) for the small step.
+int small_weight_map(CUtensorMap* m, const float* W, int l, int rows, int cols);
 
 }  // namespace spo

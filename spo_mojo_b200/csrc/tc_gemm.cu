@@ -1086,38 +1086,6 @@ __global__ void split_weights_kernel(const float* __restrict__ w, int64_t K, int
 }
 
 // ---------------------------------------------------------------- host side
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// 2-D fp32 map of a row-major [outer x inner] array, 128-byte swizzle (16-byte or
-// 32-byte atoms), zero fill out of bounds.
-int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
-             uint32_t box_outer, CUtensorMapSwizzle swz) {
-  auto fn = encode_fn();
-  if (!fn) return set_error(kErrCuda, "cuTensorMapEncodeTiled unavailable");
-  if (!aligned16(ptr) || (inner * 4) % 16 != 0)
-    return set_error(kErrAlign, "tensor map: base and row pitch must be 16-byte aligned");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 4};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
-                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_error(kErrCuda, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
-  return kOk;
-}
-
 // CTA pairs (cta_group::2) for the dW products, unless built with SPO_TC_PAIR=0. Measured
 // at 1048576 x 512 x 512 on B200: dW 2.89 ms paired vs 3.26 ms single; the forward and dX
 // products run 5-10% slower paired (the pair advances at the pace of its slower CTA and
@@ -1270,6 +1238,38 @@ int64_t units_of(const TcGemmArgs& a, int* splits) {
 }
 
 }  // namespace
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D fp32 map of a row-major [outer x inner] array, 128-byte swizzle (16-byte or
+// 32-byte atoms), zero fill out of bounds.
+int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
+             uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(kErrCuda, "cuTensorMapEncodeTiled unavailable");
+  if (!aligned16(ptr) || (inner * 4) % 16 != 0)
+    return set_error(kErrAlign, "tensor map: base and row pitch must be 16-byte aligned");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
+                  es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(kErrCuda, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return kOk;
+}
 
 bool tc_gemm_supported(int kind, int64_t M, int64_t N, int64_t K) {
   if (M < 1 || N < 1 || K < 1 || N % 128 != 0) return false;

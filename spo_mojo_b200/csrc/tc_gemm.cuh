@@ -13,6 +13,8 @@
 // to bound the error of the tensor memory accumulation.
 #pragma once
 
+#include <cuda.h>
+
 #include "spo_common.cuh"
 
 namespace spo {
@@ -58,6 +60,9 @@ int tc_gemm_splits(const TcGemmArgs& a);   // TC_DW partial count
 int64_t tc_gemm_tiles(int kind, int64_t M, int64_t N);  // output tiles (units per split)
 int tc_gemm_slots(int kind, int64_t N);     // units that run at once (SMs or CTA pairs)
 bool tc_gemm_supported(int kind, int64_t M, int64_t N, int64_t K);
+// 2-D fp32 tensor map of a row-major [outer x inner] array (host; error code, kOk).
+int make_map(CUtensorMap* m, const float* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
+             uint32_t box_outer, CUtensorMapSwizzle swz);
 int tc_gemm_launch(const TcGemmArgs& a, cudaStream_t s);
 
 // hi/lo split of n floats (elementwise); keep_positive: a positive x never gets hi == 0
