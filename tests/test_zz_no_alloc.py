@@ -82,3 +82,18 @@ def test_noalloc_refuses_shapes_beyond_its_scratch(k, n):
     with pytest.raises(f.SpoError) as e:
         f.call("spo_linear_bwd_noalloc", None, 1, 1, None, 1, 1, 1, None, 16, k, n)
     assert e.value.code == -4 and "static scratch" in str(e.value)
+
+
+@pytest.mark.parametrize("case,m,k,n", [(0, 3, 4, 8), (1, 20, 18, 64), (2, 64, 64, 64), (3, 1, 1, 1)])
+def test_noalloc_matches_the_reference_goldens(case, m, k, n):
+    # the reference's linear backward goldens (tests/test_linear_backward.mojo:287-292),
+    # at that test's tolerance, on two calls in a row through the shared static scratch
+    from golden_io import read_f32
+    x, w, dy = (torch.from_numpy(np.ascontiguousarray(read_f32(f"linbwd{case}_{s}"), dtype=np.float32))
+                .cuda() for s in ("x", "w", "dy"))
+    for call in range(2):
+        dw, db, dx = _run("spo_linear_bwd_noalloc", x, w, dy, None, m, k, n)
+        for name, got, tol in (("dw", dw, _tol(m)), ("db", db, _tol(m)), ("dx", dx, _tol(n))):
+            want = read_f32(f"linbwd{case}_{name}").reshape(-1)
+            err = float(np.max(np.abs(got.cpu().numpy().reshape(-1) - want)))
+            assert err <= tol, f"call {call}: {name} off by {err}"
