@@ -22,10 +22,11 @@
 //   reduce    partials -> flat gradients, gaps zeroed, loss statistics, then Adam
 //             (networks/optim.mojo:75-187) with the dual gradient of log_alpha
 //
-// Every grid barrier wait is bounded (wait_ns); on expiry the CTA raises a shared abort
-// word, records a code in the learner's error word and goes to the exit; the others see
-// the abort word in their own waits. The last CTA to leave resets the barrier words for
-// the next launch and, after a complete Adam phase, advances the step counter.
+// Every grid barrier wait is bounded (wait_ns); on expiry the CTA raises the abort bit of
+// the arrival word, records a code in the learner's error word and goes to the exit; the
+// others see the bit in the same word their waits poll. The last CTA to leave resets the
+// barrier words for the next launch and, after a complete Adam phase, advances the step
+// counter.
 #include <algorithm>
 #include <cmath>
 
@@ -86,6 +87,22 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   return v;
 }
 
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Bit of the arrival word (sync[0]) that aborts the step. Arrivals count up to 3 * grid
+// per launch, far below it. Set before the raising CTA's own arrival (same word, same
+// thread order), so every CTA that sees a full count of arrivals also sees the bit.
+constexpr unsigned kAbortBit = 1u << 30;
+
+__device__ __forceinline__ void raise_abort(const SmallStepParams& P, int code) {
+  atomicOr(P.sync + 0, kAbortBit);
+  if (P.err) atomicCAS(P.err, 0, code);
+}
+
 // Data that other CTAs write during the launch (partials, gradients, parameters in the
 // Adam phase) is read through L2 (.cg): never a stale L1 line. Weights are read before any
 // write to them in the launch, through L1.
@@ -101,24 +118,23 @@ __device__ bool grid_barrier(unsigned& target, const SmallStepParams& P, bool wi
   __syncthreads();
   target += gridDim.x;
   if (threadIdx.x == 0) {
-    __threadfence();
-    if (!withhold) atomicAdd(P.sync + 0, 1u);
-    int ok = 1;
-    const uint64_t t0 = now_ns();
-    while (ld_acquire(P.sync + 0) < target) {
-      if (ld_acquire(P.sync + 2) != 0u) {
-        ok = 0;
-        break;
-      }
-      if (now_ns() - t0 > P.wait_ns) {
-        atomicExch(P.sync + 2, 1u);
-        if (P.err) atomicCAS(P.err, 0, kErrGridWait);
-        ok = 0;
-        break;
+    // acq_rel arrival: the CTA's writes before the barrier (ordered before this thread by
+    // the bar.sync above) are released to every CTA that acquires the count, and the
+    // returned count acquires the others'; abort and completion are read from one word
+    unsigned v = withhold ? ld_acquire(P.sync + 0) : atom_add_acq_rel(P.sync + 0, 1u) + 1u;
+    if (!(v & kAbortBit) && v < target) {
+      const uint64_t t0 = now_ns();
+      for (;;) {
+        v = ld_acquire(P.sync + 0);
+        if ((v & kAbortBit) || v >= target) break;
+        if (now_ns() - t0 > P.wait_ns) {
+          raise_abort(P, kErrGridWait);
+          v |= kAbortBit;
+          break;
+        }
       }
     }
-    __threadfence();
-    s_ok = ok;
+    s_ok = !(v & kAbortBit);
   }
   __syncthreads();
   return s_ok != 0;
@@ -643,8 +659,7 @@ __device__ bool wait_staged(uint32_t bar, uint32_t parity, const SmallStepParams
   const uint64_t t0 = now_ns();
   while (!mbar_try(bar, parity)) {
     if (now_ns() - t0 > P.wait_ns) {
-      atomicExch(P.sync + 2, 1u);
-      if (P.err) atomicCAS(P.err, 0, kErrWeightCopy);
+      raise_abort(P, kErrWeightCopy);
       const uint64_t t1 = now_ns();
       while (!mbar_try(bar, parity) && now_ns() - t1 < P.wait_ns) {
       }
@@ -994,15 +1009,17 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
       }
     }
   }
-  // ---- exit: the last CTA out resets the barrier words (and advances the step)
+  // ---- exit: the last CTA out resets the barrier words (and advances the step). Nothing
+  // after the reset needs a fence: the launch ends there, and its end makes every write
+  // visible to the next kernel in the stream.
   __syncthreads();
   SS_MARK(8);
   if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(P.sync + 1, 1u);
+    // acq_rel: this CTA is done with the barrier words before the last one resets them
+    const unsigned prev = atom_add_acq_rel(P.sync + 1, 1u);
     if (prev == gridDim.x - 1) {
-      const bool done = ld_acquire(P.sync + 2) == 0u;
-      if (done && P.apply) {
+      const unsigned arrivals = atomicExch(P.sync + 0, 0u);   // reset, reading the abort bit
+      if (!(arrivals & kAbortBit) && P.apply) {
         *ap.step = t_step;
         if (ap.report) {
           for (int k = 0; k < kMaxGroups; ++k) {
@@ -1012,11 +1029,7 @@ __global__ void __launch_bounds__(kT, 1) small_step_kernel(const __grid_constant
           ap.report[kRepStep] = (float)t_step;
         }
       }
-      P.sync[0] = 0u;
-      P.sync[2] = 0u;
-      __threadfence();
       P.sync[1] = 0u;
-      __threadfence();
     }
   }
 }

@@ -55,7 +55,7 @@ struct SmallStepParams {
   AdamParams adam;
   int64_t total;                       // length of the flat buffers
   float* sumsq;                        // [kMaxGroups][grid]
-  unsigned* sync;                      // [0] barrier arrivals, [1] exits, [2] abort; zero between launches
+  unsigned* sync;                      // [0] barrier arrivals (bit 30: abort), [1] exits; zero between launches
   int* err;                            // learner error word
   uint64_t wait_ns;                    // limit of every barrier wait
   uint32_t withhold;                   // a test of the bounded waits: 1 + the CTA whose first
