@@ -483,6 +483,7 @@ def run_ours(args):
 
     if clocks is not None:
         clocks.mark()
+    launch_floor_us = None
     if flush:
         ms = flushed_ms(lambda i: step(batch))
     else:
@@ -495,6 +496,17 @@ def run_ours(args):
         t1.synchronize()
         ms = t0.elapsed_time(t1) / args.steps
     clk = clocks.stop() if clocks is not None else None
+    if flush:
+        # the same timing applied to a graph of one one-element fill: what the launch, the
+        # event records and the flush's aftermath cost a step that does no work
+        tiny = torch.zeros(1, device=dev)
+        torch.cuda.synchronize(dev)
+        g_tiny = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_tiny, stream=stream):
+            tiny.fill_(1.0)
+        torch.cuda.synchronize(dev)
+        launch_floor_us = 1e3 * flushed_ms(lambda i: g_tiny.replay())
+        del g_tiny
     ms_max, ms_ranks = ms, [ms]
     if world > 1:
         tm = torch.tensor([ms], device=dev)
@@ -605,6 +617,7 @@ def run_ours(args):
                               % (in_bytes / 1e6, act_bytes / 1e9))},
             "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
             "ms_per_rank": ms_ranks,
+            "launch_floor_us": launch_floor_us,
             "allreduce_ms": allreduce_ms,
             "allreduce_bytes": int(L.grads.numel() * 4) if world > 1 else 0,
             # the whole step's arithmetic (forward, dW, dX: 2 flop per multiply-add, fp32
