@@ -515,63 +515,85 @@ __device__ void block_dw(int in, int ks, int K, int dz, int zs, int N, int R, fl
 // bias), the row losses and dz (stride zs). The per-row inputs come from shared memory (li:
 // mask or cells, q, pi_old logits, 9 each; the critic's target in the first column). Lane
 // 0 of warp w adds the statistics of its rows to stw[w][..].
+// Butterfly sums (max) of N values at once: the same xor order per value as warp_sum
+// (warp_max), the N exchanges of a level issued together instead of N dependent chains.
+template <int N>
+__device__ __forceinline__ void warp_sum_n(float (&v)[N]) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+}
+template <int N>
+__device__ __forceinline__ void warp_max_n(float (&v)[N]) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = fmaxf(v[j], __shfl_xor_sync(0xffffffffu, v[j], o));
+}
+
 __device__ __noinline__ void block_loss(bool actor, bool has_mask, bool has_old, float scale, int H, int A, int act,
                                         int li, int R, int dz, int zs, int w, int b, float alpha, int stw) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool valid = lane < A;
   const float bias = valid ? smem[b + lane] : 0.f;
   float st[kStats] = {};
-  for (int r = warp; r < R; r += kW) {
-    const int in_r = li + r * kLossIn;
-    float part[kSmallMaxA] = {};
-    for (int h = lane; h < H; h += 32) {
-      const float a = smem[act + r * H + h];
-#pragma unroll
-      for (int j = 0; j < kSmallMaxA; ++j)
-        if (j < A) part[j] = fmaf(a, smem[w + h * A + j], part[j]);
-    }
-    float z = 0.f;
-#pragma unroll
-    for (int j = 0; j < kSmallMaxA; ++j) {
-      if (j >= A) break;
-      const float s = warp_sum(part[j]);
-      if (lane == j) z = s;
-    }
-    z += bias;
-    if (!actor) {
-      const float d = z - smem[in_r];   // meaningful in lane 0
+  if (!actor) {
+    for (int r = warp; r < R; r += kW) {   // value head (A == 1): one row per warp at a time
+      float p0 = 0.f;
+      for (int h = lane; h < H; h += 32) p0 = fmaf(smem[act + r * H + h], smem[w + h], p0);
+      const float v = warp_sum(p0);   // every lane takes part in the exchange
+      const float z = (lane == 0 ? v : 0.f) + bias;
+      const float d = z - smem[li + r * kLossIn];   // meaningful in lane 0
       if (lane < zs) smem[dz + r * zs + lane] = lane == 0 ? d * scale : 0.f;
       st[kStatCriticLoss] += 0.5f * d * d * scale;
-      continue;
     }
-    const float m_in = valid ? smem[in_r + lane] : 0.f;
-    const float mk = valid ? (has_mask ? m_in : (m_in == 0.f ? 1.f : 0.f)) : 0.f;
-    const bool legal = valid && mk != 0.f;
-    const float qv = valid ? smem[in_r + 9 + lane] : 0.f;
-    const float zm = legal ? z : kNegInf;
-    const float mx = warp_max(zm);
-    const float e = valid ? expf(zm - mx) : 0.f;
-    const float s = warp_sum(e);
-    const float pi = e * (1.f / s);
-    const float lp = zm - (mx + logf(s));
-    float po = 0.f, klo_t = 0.f;
-    if (has_old) {
-      const float zo = legal ? smem[in_r + 18 + lane] : kNegInf;
-      const float mxo = warp_max(zo);
-      const float eo = valid ? expf(zo - mxo) : 0.f;
-      const float so = warp_sum(eo);
-      po = eo * (1.f / so);
-      if (valid && po > 0.f) klo_t = po * ((zo - (mxo + logf(so))) - lp);
+  } else {
+    for (int r = warp; r < R; r += kW) {
+      const int in_r = li + r * kLossIn;
+      float part[kSmallMaxA] = {};
+      for (int h = lane; h < H; h += 32) {
+        const float a = smem[act + r * H + h];
+#pragma unroll
+        for (int j = 0; j < kSmallMaxA; ++j)
+          if (j < A) part[j] = fmaf(a, smem[w + h * A + j], part[j]);
+      }
+      warp_sum_n(part);   // outputs j >= A stay 0
+      float z = 0.f;
+#pragma unroll
+      for (int j = 0; j < kSmallMaxA; ++j)
+        if (lane == j && j < A) z = part[j];
+      z += bias;
+      const float m_in = valid ? smem[in_r + lane] : 0.f;
+      const float mk = valid ? (has_mask ? m_in : (m_in == 0.f ? 1.f : 0.f)) : 0.f;
+      const bool legal = valid && mk != 0.f;
+      const float qv = valid ? smem[in_r + 9 + lane] : 0.f;
+      // the softmax of z and, with pi_old, of its logits: their reductions side by side
+      float mxs[2] = {legal ? z : kNegInf, (has_old && legal) ? smem[in_r + 18 + lane] : kNegInf};
+      const float zm = mxs[0], zo = mxs[1];
+      warp_max_n(mxs);
+      const float mx = mxs[0], mxo = mxs[1];
+      float ss[2] = {valid ? expf(zm - mx) : 0.f, (has_old && valid) ? expf(zo - mxo) : 0.f};
+      const float e = ss[0], eo = ss[1];
+      warp_sum_n(ss);
+      const float s = ss[0], so = ss[1];
+      const float pi = e * (1.f / s);
+      const float lp = zm - (mx + logf(s));
+      float po = 0.f, klo_t = 0.f;
+      if (has_old) {
+        po = eo * (1.f / so);
+        if (valid && po > 0.f) klo_t = po * ((zo - (mxo + logf(so))) - lp);
+      }
+      float sums[3] = {(valid && qv != 0.f) ? -qv * lp : 0.f, (valid && qv > 0.f) ? -qv * logf(qv) : 0.f, klo_t};
+      warp_sum_n(sums);
+      const float ce = sums[0], hq = sums[1], klo = sums[2];
+      if (lane < zs) smem[dz + r * zs + lane] = legal ? ((pi - qv) + alpha * (pi - po)) * scale : 0.f;
+      st[kStatActorLoss] += (ce + alpha * klo) * scale;
+      st[kStatCE] += ce * scale;
+      st[kStatEntropy] += hq * scale;
+      st[kStatKLq] += (ce - hq) * scale;
+      st[kStatKLold] += klo * scale;
     }
-    const float ce = warp_sum((valid && qv != 0.f) ? -qv * lp : 0.f);
-    const float hq = warp_sum((valid && qv > 0.f) ? -qv * logf(qv) : 0.f);
-    const float klo = warp_sum(klo_t);
-    if (lane < zs) smem[dz + r * zs + lane] = legal ? ((pi - qv) + alpha * (pi - po)) * scale : 0.f;
-    st[kStatActorLoss] += (ce + alpha * klo) * scale;
-    st[kStatCE] += ce * scale;
-    st[kStatEntropy] += hq * scale;
-    st[kStatKLq] += (ce - hq) * scale;
-    st[kStatKLold] += klo * scale;
   }
   if (lane == 0)
 #pragma unroll
