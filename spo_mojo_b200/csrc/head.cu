@@ -83,6 +83,21 @@ __device__ __forceinline__ float half_sum(float v) {
   for (int o = 8; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// The same for N values at once: the N exchanges of a level issued together.
+template <int N>
+__device__ __forceinline__ void half_max_n(float (&v)[N]) {
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = fmaxf(v[j], __shfl_xor_sync(0xffffffffu, v[j], o));
+}
+template <int N>
+__device__ __forceinline__ void half_sum_n(float (&v)[N]) {
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+}
 
 template <int A, int NJ>
 __global__ void __launch_bounds__(kHeadThreads, 2)
@@ -327,27 +342,31 @@ head_kernel(const HeadParams p) {
           mk = p.mask ? m : (from_cells ? (m == 0.f ? 1.f : 0.f) : 1.f);
           qv = rq[rr * A + la];
         }
-        const float zm = (!lv || mk == 0.f) ? kNegInf : zv;
-        const float mx = half_max(zm);
-        const float e = lv ? expf(zm - mx) : 0.f;
-        const float s = half_sum(e);
+        // the softmax of z and, with pi_old, of its logits: their half-warp reductions side
+        // by side (each value in the same xor order as alone)
+        const bool has_old = p.z_old != nullptr;
+        float mxs[2] = {(!lv || mk == 0.f) ? kNegInf : zv,
+                        (!has_old || !lv || mk == 0.f) ? kNegInf : rz[rr * A + la]};
+        const float zm = mxs[0], zo = mxs[1];
+        half_max_n(mxs);
+        const float mx = mxs[0], mxo = mxs[1];
+        float ss[2] = {lv ? expf(zm - mx) : 0.f, (has_old && lv) ? expf(zo - mxo) : 0.f};
+        const float e = ss[0], eo = ss[1];
+        half_sum_n(ss);
+        const float s = ss[0], so = ss[1];
         const float inv_s = 1.f / s;
         const float lse = mx + logf(s);
         const float pi = e * inv_s;
         const float lp = zm - lse;
         float po = 0.f, klo_t = 0.f;
-        if (p.z_old != nullptr) {
-          const float zo = (!lv || mk == 0.f) ? kNegInf : rz[rr * A + la];
-          const float mxo = half_max(zo);
-          const float eo = lv ? expf(zo - mxo) : 0.f;
-          const float so = half_sum(eo);
+        if (has_old) {
           const float inv_so = 1.f / so, lseo = mxo + logf(so);
           po = eo * inv_so;
           if (lv && po > 0.f) klo_t = po * ((zo - lseo) - lp);
         }
-        const float ce = half_sum((lv && qv != 0.f) ? -qv * lp : 0.f);
-        const float hq = half_sum((lv && qv > 0.f) ? -qv * logf(qv) : 0.f);
-        const float klo = half_sum(klo_t);
+        float sums[3] = {(lv && qv != 0.f) ? -qv * lp : 0.f, (lv && qv > 0.f) ? -qv * logf(qv) : 0.f, klo_t};
+        half_sum_n(sums);
+        const float ce = sums[0], hq = sums[1], klo = sums[2];
         dz = (!lv || mk == 0.f) ? 0.f : ((pi - qv) + alpha * (pi - po)) * p.scale;
         if (la == 0 && rvalid) {
           st[kStatActorLoss] += (ce + alpha * klo) * p.scale;
