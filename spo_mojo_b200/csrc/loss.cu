@@ -32,6 +32,23 @@ constexpr int kWarps = kThreads / 32;
 
 __device__ __forceinline__ float softplus_f(float x) { return log1pf(expf(-fabsf(x))) + fmaxf(x, 0.f); }
 
+// Butterfly sums (max) of N values at once: the same xor order per value as warp_sum
+// (warp_max), the N exchanges of a level issued together instead of N dependent chains.
+template <int N>
+__device__ __forceinline__ void warp_sum_n(float (&v)[N]) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+}
+template <int N>
+__device__ __forceinline__ void warp_max_n(float (&v)[N]) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < N; ++j) v[j] = fmaxf(v[j], __shfl_xor_sync(0xffffffffu, v[j], o));
+}
+
 struct LossParams {
   const float* z;        // actor: logits [rows x A]; critic: V [rows]
   const float* mask;     // actor: [rows x A] or null (all legal)
@@ -59,24 +76,27 @@ __global__ void __launch_bounds__(kThreads) actor_loss_rows_kernel(const LossPar
     const float mk = valid ? (p.mask ? __ldg(p.mask + o) : 1.f) : 0.f;
     const bool legal = valid && mk != 0.f;
     const float qv = valid ? __ldg(p.q + o) : 0.f;
-    const float zm = legal ? __ldg(p.z + o) : kNegInf;
-    const float mx = warp_max(zm);
-    const float e = valid ? expf(zm - mx) : 0.f;
-    const float s = warp_sum(e);
+    // the softmax of z and, with pi_old, of its logits: their reductions side by side
+    // (each value in the same xor order as alone)
+    const bool has_old = p.z_old != nullptr;
+    float mxs[2] = {legal ? __ldg(p.z + o) : kNegInf, (has_old && legal) ? __ldg(p.z_old + o) : kNegInf};
+    const float zm = mxs[0], zo = mxs[1];
+    warp_max_n(mxs);
+    const float mx = mxs[0], mxo = mxs[1];
+    float ss[2] = {valid ? expf(zm - mx) : 0.f, (has_old && valid) ? expf(zo - mxo) : 0.f};
+    const float e = ss[0], eo = ss[1];
+    warp_sum_n(ss);
+    const float s = ss[0], so = ss[1];
     const float pi = e * (1.f / s);
     const float lp = zm - (mx + logf(s));
     float po = 0.f, klo_t = 0.f;
-    if (p.z_old != nullptr) {
-      const float zo = legal ? __ldg(p.z_old + o) : kNegInf;
-      const float mxo = warp_max(zo);
-      const float eo = valid ? expf(zo - mxo) : 0.f;
-      const float so = warp_sum(eo);
+    if (has_old) {
       po = eo * (1.f / so);
       if (valid && po > 0.f) klo_t = po * ((zo - (mxo + logf(so))) - lp);
     }
-    const float ce = warp_sum((valid && qv != 0.f) ? -qv * lp : 0.f);
-    const float hq = warp_sum((valid && qv > 0.f) ? -qv * logf(qv) : 0.f);
-    const float klo = warp_sum(klo_t);
+    float sums[3] = {(valid && qv != 0.f) ? -qv * lp : 0.f, (valid && qv > 0.f) ? -qv * logf(qv) : 0.f, klo_t};
+    warp_sum_n(sums);
+    const float ce = sums[0], hq = sums[1], klo = sums[2];
     if (valid) p.dz[o] = legal ? ((pi - qv) + alpha * (pi - po)) * p.scale : 0.f;
     st[kStatActorLoss] += (ce + alpha * klo) * p.scale;
     st[kStatCE] += ce * p.scale;
