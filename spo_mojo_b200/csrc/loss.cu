@@ -116,6 +116,82 @@ __global__ void __launch_bounds__(kThreads) actor_loss_rows_kernel(const LossPar
   }
 }
 
+// The same loss with one row per thread, for a fixed action count NA: a row's logits,
+// mask, targets and pi_old logits come from consecutive words (a warp reads 32 adjacent
+// rows, whose lines the later words of each row then hit in L1), and the row's maxima and
+// sums are taken serially in action order, with no exchange between lanes. Per element
+// the same expressions as the kernel above; the statistics are reduced over the warp and
+// then the CTA's warps in order.
+template <int NA>
+__global__ void __launch_bounds__(kThreads) actor_loss_row_per_thread_kernel(const LossParams p) {
+  __shared__ float red[kWarps][kStats];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool has_old = p.z_old != nullptr;
+  const float alpha = has_old ? softplus_f(__ldg(p.log_alpha)) : 0.f;
+  float st[kStats] = {};
+  for (int64_t r = (int64_t)blockIdx.x * kThreads + threadIdx.x; r < p.rows; r += (int64_t)gridDim.x * kThreads) {
+    const int64_t o = r * NA;
+    float zm[NA], zo[NA], qv[NA];
+    bool legal[NA];
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      const float mk = p.mask ? __ldg(p.mask + o + a) : 1.f;
+      legal[a] = mk != 0.f;
+      qv[a] = __ldg(p.q + o + a);
+      zm[a] = legal[a] ? __ldg(p.z + o + a) : kNegInf;
+      zo[a] = (has_old && legal[a]) ? __ldg(p.z_old + o + a) : kNegInf;
+    }
+    float mx = zm[0], mxo = zo[0];
+#pragma unroll
+    for (int a = 1; a < NA; ++a) {
+      mx = fmaxf(mx, zm[a]);
+      mxo = fmaxf(mxo, zo[a]);
+    }
+    float e[NA], eo[NA], s = 0.f, so = 0.f;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      e[a] = expf(zm[a] - mx);
+      s += e[a];
+      eo[a] = has_old ? expf(zo[a] - mxo) : 0.f;
+      so += eo[a];
+    }
+    const float inv_s = 1.f / s, lse = mx + logf(s);
+    const float inv_so = has_old ? 1.f / so : 0.f, lseo = has_old ? mxo + logf(so) : 0.f;
+    float ce = 0.f, hq = 0.f, klo = 0.f;
+#pragma unroll
+    for (int a = 0; a < NA; ++a) {
+      const float pi = e[a] * inv_s;
+      const float lp = zm[a] - lse;
+      float po = 0.f;
+      if (has_old) {
+        po = eo[a] * inv_so;
+        if (po > 0.f) klo += po * ((zo[a] - lseo) - lp);
+      }
+      if (qv[a] != 0.f) ce += -qv[a] * lp;
+      if (qv[a] > 0.f) hq += -qv[a] * logf(qv[a]);
+      p.dz[o + a] = legal[a] ? ((pi - qv[a]) + alpha * (pi - po)) * p.scale : 0.f;
+    }
+    st[kStatActorLoss] += (ce + alpha * klo) * p.scale;
+    st[kStatCE] += ce * p.scale;
+    st[kStatEntropy] += hq * p.scale;
+    st[kStatKLq] += (ce - hq) * p.scale;
+    st[kStatKLold] += klo * p.scale;
+  }
+  warp_sum_n(st);
+  if (lane == 0)
+#pragma unroll
+    for (int k = 0; k < kStats; ++k) red[warp][k] = st[k];
+  __syncthreads();
+  if (threadIdx.x < kStats) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += red[w][threadIdx.x];
+    p.part[(int64_t)blockIdx.x * kStats + threadIdx.x] = v;
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) value_loss_rows_kernel(const LossParams p) {
   __shared__ float red[kWarps];
   pdl_wait();
@@ -181,8 +257,15 @@ int actor_loss_launch(const float* z, const float* mask, const float* q, const f
   p.scale = scale;
   p.dz = dz;
   p.part = part;
-  const int grid = rows > 0 ? loss_grid(rows, kWarps) : 0;
-  if (grid > 0) SPO_CUDA_TRY(launch_pdl(actor_loss_rows_kernel, dim3(grid), dim3(kThreads), 0, s, 0u, p));
+  // nine actions (the board's cells): one row per thread; other widths: one row per warp
+  const bool per_thread = A == 9;
+  const int grid = rows > 0 ? loss_grid(rows, per_thread ? kThreads : kWarps) : 0;
+  if (grid > 0) {
+    if (per_thread)
+      SPO_CUDA_TRY(launch_pdl(actor_loss_row_per_thread_kernel<9>, dim3(grid), dim3(kThreads), 0, s, 0u, p));
+    else
+      SPO_CUDA_TRY(launch_pdl(actor_loss_rows_kernel, dim3(grid), dim3(kThreads), 0, s, 0u, p));
+  }
   SPO_CUDA_TRY(launch_pdl(loss_finish_kernel, dim3(1), dim3(32), 0, s, 0u, (const float*)part, grid,
                           (int)kStatActorLoss, (int)kStatKLold + 1, stats, log_alpha, eps_kl, dlog_alpha));
   return kOk;
