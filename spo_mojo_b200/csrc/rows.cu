@@ -1,7 +1,7 @@
 // Row-wise and elementwise kernels behind the reference-shaped entry points
 // (the pieces the fused head combines; exposed so a caller can run the reference's
-// step-by-step composition). One warp per row for the softmax family, one thread
-// per row or element for the rest.
+// step-by-step composition). The softmax family: one thread per row up to 16 columns,
+// one warp per row beyond; one thread per row or element for the rest.
 //
 //   mask_logits_kernel        networks/actor.mojo:50-71
 //   softmax_rows / log_softmax_rows / logsumexp_rows   ops/softmax.mojo:29-135
@@ -54,6 +54,38 @@ __global__ void softmax_rows_kernel(float* out, const float* in, int64_t rows, i
       for (int c = lane; c < cols; c += 32) out[r * cols + c] = a[c] - lse;
     } else {
       for (int c = lane; c < cols; c += 32) out[r * cols + c] = expf(a[c] - mx) / s;
+    }
+  }
+}
+
+// The same for rows of at most kThreadCols columns (the 9 actions): one row per thread,
+// its maximum and sum taken serially in column order with no exchange between lanes.
+constexpr int kThreadCols = 16;
+__global__ void softmax_rows_thread_kernel(float* out, const float* in, int64_t rows, int cols, int mode) {
+  GRID_STRIDE(r, rows) {
+    const float* a = in + r * cols;
+    float v[kThreadCols];
+    float mx = kNegInf;
+#pragma unroll
+    for (int c = 0; c < kThreadCols; ++c) {
+      v[c] = c < cols ? a[c] : kNegInf;
+      mx = fmaxf(mx, v[c]);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < kThreadCols; ++c)
+      if (c < cols) s += expf(v[c] - mx);
+    if (mode == 2) {
+      out[r] = mx + logf(s);
+    } else if (mode == 1) {
+      const float lse = mx + logf(s);
+#pragma unroll
+      for (int c = 0; c < kThreadCols; ++c)
+        if (c < cols) out[r * cols + c] = v[c] - lse;
+    } else {
+#pragma unroll
+      for (int c = 0; c < kThreadCols; ++c)
+        if (c < cols) out[r * cols + c] = expf(v[c] - mx) / s;
     }
   }
 }
@@ -166,6 +198,11 @@ int mask_logits_launch(float* logits, const float* mask, int64_t n, cudaStream_t
 int softmax_rows_launch(float* out, const float* in, int64_t rows, int cols, int mode,
                         cudaStream_t s) {
   if (rows <= 0) return kOk;
+  if (cols <= kThreadCols) {
+    softmax_rows_thread_kernel<<<blocks(rows), kThreads, 0, s>>>(out, in, rows, cols, mode);
+    SPO_LAUNCH_CHECK();
+    return kOk;
+  }
   const int64_t warps_per_block = kThreads / 32;
   const int grid = (int)std::min<int64_t>(ceil_div(rows, warps_per_block), 16LL * sm_count());
   softmax_rows_kernel<<<grid, kThreads, 0, s>>>(out, in, rows, cols, mode);
