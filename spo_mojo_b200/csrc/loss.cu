@@ -4,8 +4,8 @@
 // own forward (the reference's actor_backward and critic_backward start from logits / V,
 // networks/actor_loss.mojo:194-214, networks/mlp.mojo:212-233).
 //
-// Actor: one warp per row, lane a holds action a (A <= 32). Per row, in the order of the
-// fused head's loss phase:
+// Actor: nine actions, one row per thread; other widths, one warp per row with lane a
+// holding action a (A <= 32). Per row, in the order of the fused head's loss phase:
 //   z_m = z, or -FLT_MAX where mask == 0            mask_logits_kernel, networks/actor.mojo:50-71
 //   log pi = z_m - logsumexp(z_m), pi = softmax(z_m)  ops/softmax.mojo:58-135
 //   ce  = -sum_{q != 0} q log pi                      networks/actor_loss.mojo:40-65
